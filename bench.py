@@ -1,0 +1,436 @@
+"""Deep f32 MLP inference throughput on 1..8 B200 (samples/s).
+
+Workload (the headline configuration): a global batch of 65536 rows x 4096
+f32 features, 8 x [Linear(4096, 4096) + GELU], then Linear(4096, 1000) and a
+row softmax.  Weights are Kaiming-normal (std sqrt(2/4096)), biases zero, the
+input N(0, 1), all seeded synthetic data.  Each layer is the reference's op
+sequence MATMUL -> ADD(bias) -> GELU (magnetron/magnetron_cpu.c:2151, :1616,
+:942-1000), built as a deferred graph of magnetron tensors and executed by
+this backend as one CUDA graph; the softmax is the backend's row-softmax
+extension.  The batch is sharded by rows over one process per GPU; logits are
+collected with an NCCL all-gather.
+
+One step = one forward over the whole batch.  `value` is whole-job samples/s
+with inputs resident in HBM; `e2e` adds, every step, the host->device copy of
+each rank's input shard from pinned host memory (through the storage callback
+cpy_host_device) and the device->host read of the gathered softmax output on
+rank 0.  The activations (1 GiB per layer at one GPU) exceed the 126 MB L2, so
+no flush is needed between steps.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "magnetron-pre-oss-release-old_b200")
+sys.path.insert(0, PKG)
+
+GLOBAL_BATCH = 65536
+D_IN, D_HID, N_HID, D_OUT = 4096, 4096, 8, 1000
+METRIC = "MLP fwd samples/s"
+FLOP_PER_SAMPLE = 2 * (N_HID * D_IN * D_HID + D_HID * D_OUT)
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p, "measured"
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+        self.t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------- CPU baselines
+def _ref_mlp_rows(rows: int, seed: int, use_ref: bool):
+    """Forward of `rows` samples through the reference library (or the oracle
+    port when the reference library is absent); returns seconds."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    from oracle import Oracle, RefLib, REF_SO, pad6
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((rows, D_IN), dtype=np.float32)
+    ws = [(rng.standard_normal((D_IN, D_HID), dtype=np.float32) * np.float32((2.0 / D_IN) ** 0.5))
+          for _ in range(N_HID)]
+    wo = rng.standard_normal((D_HID, D_OUT), dtype=np.float32) * np.float32((2.0 / D_HID) ** 0.5)
+    if use_ref and os.path.exists(REF_SO):
+        R = RefLib()
+        tx = R.tensor_nd((rows, D_IN))
+        R.write(tx, x)
+        tws = []
+        for w in ws:
+            t = R.tensor_nd((D_IN, D_HID))
+            R.write(t, w)
+            tws.append(t)
+        to = R.tensor_nd((D_HID, D_OUT))
+        R.write(to, wo)
+        tb = R.tensor_nd((rows, D_HID))
+        tbo = R.tensor_nd((rows, D_OUT))
+        t0 = time.perf_counter()
+        h = tx
+        for t in tws:
+            m = R.op("MATMUL", h, t)
+            a = R.op("ADD", m, tb)
+            g = R.op("GELU", a)
+            if h is not tx:
+                R.free(h)
+            R.free(m, a)
+            h = g
+        z = R.op("MATMUL", h, to)
+        z2 = R.op("ADD", z, tbo)
+        logits = R.read(z2).reshape(rows, D_OUT)
+        o = Oracle()
+        o.softmax_rows(logits, rows, D_OUT)
+        dt = time.perf_counter() - t0
+        R.close()
+        return dt, "reference"
+    o = Oracle()
+    t0 = time.perf_counter()
+    h = x.reshape(-1)
+    for w in ws:
+        h = o.matmul(h, w, rows, D_IN, D_HID)
+        h = o.unary("GELU", h, pad6((rows, D_HID)))
+    z = o.matmul(h, wo, rows, D_HID, D_OUT)
+    o.softmax_rows(z, rows, D_OUT)
+    return time.perf_counter() - t0, "port"
+
+
+def _ref_worker(args):
+    rows, seed = args
+    return _ref_mlp_rows(rows, seed, True)
+
+
+def cpu_baseline():
+    rows = 256
+    dt, kind = _ref_mlp_rows(rows, 1234, True)
+    return {"value": rows / dt, "unit": "samples/s", "cores": 1, "kind": kind,
+            "sample": f"{rows} rows of the same MLP forward (8x4096^2 + 4096x1000 matmuls, GELU, softmax), "
+                      f"single thread as the reference CPU backend runs ({dt:.1f} s)"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import multiprocessing as mp
+    ncpu = os.cpu_count() or 1
+    try:
+        avail = int(open("/proc/meminfo").read().split("MemAvailable:")[1].split()[0]) * 1024
+    except Exception:
+        avail = 16 << 30
+    procs = max(1, min(ncpu, int(avail // (2 << 30))))
+    rows_per = 16
+    ctx = mp.get_context("spawn")
+    times = []
+    kind = "reference"
+    with ctx.Pool(procs) as pool:
+        for step in range(args.warmup + args.steps):
+            t0 = time.perf_counter()
+            res = pool.map(_ref_worker, [(rows_per, 77 + i) for i in range(procs)])
+            dt = time.perf_counter() - t0
+            kind = res[0][1]
+            if step >= args.warmup:
+                times.append(dt)
+    per_step = statistics.median(times)
+    value = procs * rows_per / per_step
+    cfg = bench_config(args.gpus)
+    line = {"metric": METRIC, "value": value, "unit": "samples/s", "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": cfg,
+            "cpu_baseline": {"value": value, "unit": "samples/s", "cores": procs, "kind": kind,
+                             "sample": f"{procs} processes x {rows_per} rows of the MLP forward per step "
+                                       "(the reference CPU backend is single-threaded; rows are split across processes)"},
+            "e2e": {"value": value, "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def bench_config(n):
+    return {"workload": "deep f32 MLP inference: batch 65536 x 4096, 8 x (Linear 4096x4096 + GELU), "
+                        "Linear 4096x1000 + row softmax", "global_batch": GLOBAL_BATCH, "d_in": D_IN,
+            "hidden_layers": N_HID, "d_out": D_OUT, "parallelism": f"dp{n} (rows sharded, logits all-gathered)",
+            "l2_flush": "not needed: every activation (>= 128 MiB per rank at 8 GPUs) exceeds the 126 MB L2"}
+
+
+# ----------------------------------------------------------------- ours
+class _CudaArray:
+    def __init__(self, ptr, n, stream):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (ptr, False), "version": 3,
+                                         "stream": None}
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    import mag_b200 as MB
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    os.environ["MAG_CUDA_DEVICE"] = str(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    rows = GLOBAL_BATCH // world
+    dev = MB.Device()
+    stream = torch.cuda.ExternalStream(dev.stream, device=torch.device("cuda", local))
+
+    # ---- model: magnetron tensors, deferred graph (MATMUL -> ADD -> GELU per layer)
+    g = torch.Generator().manual_seed(1234)
+    std = (2.0 / D_IN) ** 0.5
+    X = dev.tensor((rows, D_IN))
+    Ws, Bs = [], []
+    for _ in range(N_HID):
+        W = dev.tensor((D_IN, D_HID))
+        W.write((torch.randn(D_IN * D_HID, generator=g) * std).numpy())
+        Ws.append(W)
+        Bs.append(dev.tensor((rows, D_HID)))  # zero bias, full shape: the core tiles y by modulo (F5)
+    Wo = dev.tensor((D_HID, D_OUT))
+    Wo.write((torch.randn(D_HID * D_OUT, generator=g) * std).numpy())
+    Bo = dev.tensor((rows, D_OUT))
+    dev.eager = False
+    h = X
+    for W, B in zip(Ws, Bs):
+        h = dev.op("MATMUL", h, W)
+        h = dev.op("ADD", h, B)
+        h = dev.op("GELU", h, inplace=True)
+    z = dev.op("MATMUL", h, Wo)
+    z = dev.op("ADD", z, Bo)
+    dev.eager = True
+    P = dev.tensor((rows * D_OUT,))
+    gathered = torch.empty(world * rows * D_OUT, dtype=torch.float32, device=f"cuda:{local}") if world > 1 else None
+
+    # ---- inputs in pinned host memory
+    xh = torch.randn(rows * D_IN, generator=torch.Generator().manual_seed(99 + rank)).pin_memory()
+    out_h = torch.empty(world * rows * D_OUT, dtype=torch.float32).pin_memory()
+    X.write(xh.numpy())
+    dev.sync()
+
+    def step():
+        dev.graph_exec(z)
+        MB.check(dev.L.mag_cuda_softmax_rows_f32(dev.p, P.data_ptr, z.data_ptr, rows, D_OUT), "softmax")
+        if world > 1:
+            with torch.cuda.stream(stream):
+                src = torch.as_tensor(_CudaArray(P.data_ptr, rows * D_OUT, dev.stream), device=f"cuda:{local}")
+                dist.all_gather_into_tensor(gathered, src)
+
+    def e2e_step():
+        X.write(xh.numpy())  # pinned -> straight DMA
+        step()
+        if rank == 0:
+            with torch.cuda.stream(stream):
+                if world > 1:
+                    out_h.copy_(gathered, non_blocking=True)
+                else:
+                    out_h.copy_(torch.as_tensor(_CudaArray(P.data_ptr, rows * D_OUT, dev.stream),
+                                                device=f"cuda:{local}"), non_blocking=True)
+            stream.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+        dev.sync()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    launches0 = dev.launches()
+    dev.profile_start()  # graph captured on the first step carries per-op event nodes
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    dev.profile_collect()
+    dev.profile_start()  # reset the per-op totals; timing below only
+    clocks = ClockSampler(local)
+    clocks.start()
+    barrier()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    launches_before = dev.launches()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+        dev.profile_collect()  # reads this replay's op events (syncs the device stream)
+    ev1.record(stream)
+    barrier()
+    launches_timed = dev.launches() - launches_before
+    ms = ev0.elapsed_time(ev1)
+    ms = max_over_ranks(ms)
+    n_mm, us_mm = dev.profile_stats("MATMUL")
+
+    # ---- end to end (host buffers through the storage callbacks)
+    for _ in range(2):
+        e2e_step()
+    barrier()
+    t0 = time.perf_counter()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    ev1.record(stream)
+    barrier()
+    e2e_ms = max_over_ranks(max(ev0.elapsed_time(ev1), (time.perf_counter() - t0) * 1e3))
+    clk = clocks.stop()
+    dev.profile_stop(os.devnull)
+
+    value = GLOBAL_BATCH * args.steps / (ms / 1e3)
+    e2e_value = GLOBAL_BATCH * args.steps / (e2e_ms / 1e3)
+    pk, pk_src = peaks()
+    tf32_peak = pk.get("bf16_tflops_sustained", pk["bf16_tflops"]) / 2.0
+    three_tf32_peak = tf32_peak / 3.0
+    mm_flop_per_step = 2.0 * rows * (N_HID * D_IN * D_HID + D_HID * D_OUT)
+    mm_ms_per_step = (us_mm / 1e3) / args.steps if args.steps else 0.0
+    achieved = (mm_flop_per_step / (mm_ms_per_step / 1e3)) / 1e12 if mm_ms_per_step else 0.0
+    line = {
+        "metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1) input, Kaiming-normal weights, zero biases)",
+        "config": bench_config(world),
+        "e2e": {"value": e2e_value, "unit": "samples/s",
+                "h2d_bytes_per_step": rows * D_IN * 4 * world,
+                "d2h_bytes_per_step": world * rows * D_OUT * 4},
+        "gpu_launches": launches_timed,
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": three_tf32_peak, "unit": "TFLOP/s",
+                     "frac": achieved / three_tf32_peak if three_tf32_peak else None, "traffic": None,
+                     "kernel": "MATMUL op (per-op CUDA events inside the replayed graph)",
+                     "peak_note": f"3xTF32 effective = {pk_src} bf16 sustained / 2 (TF32 rate) / 3 (products)",
+                     "matmul_ms_per_step": mm_ms_per_step, "matmul_launches": n_mm},
+        "clocks": clk,
+        "device": dev.name,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline()
+    if rank == 0 and world == 1 and not args.no_sweep:
+        line["sweep"] = sweep(dev, MB, torch, local)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def sweep(dev, MB, torch, local):
+    """Short device-timed throughput of the other BASELINE op families (HBM GB/s, TFLOP/s)."""
+    out = {}
+    stream = torch.cuda.ExternalStream(dev.stream, device=torch.device("cuda", local))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def timeit(fn, reps=5):
+        fn()
+        dev.sync()
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        dev.sync()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    n = 1 << 28
+    x, y, r = dev.tensor((n,)), dev.tensor((n,)), dev.tensor((n,))
+    xv = torch.randn(n // 4, generator=torch.Generator().manual_seed(5)).numpy()
+    for t in (x, y):
+        for k in range(4):
+            t.write(xv, offset_elems=k * (n // 4))
+    dims, st = MB.i64x6([n, 1, 1, 1, 1, 1]), MB.i64x6(MB.strides6([n, 1, 1, 1, 1, 1]))
+    ms = timeit(lambda: dev.L.mag_cuda_binary_f32(dev.p, MB.OP["ADD"], r.data_ptr, x.data_ptr, y.data_ptr, dims, st, st, dims, st))
+    out["add_2^28_GBps"] = 12.0 * n / (ms / 1e3) / 1e9
+    ms = timeit(lambda: dev.L.mag_cuda_unary_f32(dev.p, MB.OP["SIGMOID"], r.data_ptr, x.data_ptr, n // 1024, 1024, 1024, 1024, 0.0))
+    out["sigmoid_2^28_GBps"] = 8.0 * n / (ms / 1e3) / 1e9
+    ms = timeit(lambda: dev.L.mag_cuda_reduce_f32(dev.p, MB.OP["SUM"], r.data_ptr, x.data_ptr, dims, st))
+    out["sum_2^28_GBps"] = 4.0 * n / (ms / 1e3) / 1e9
+    ms = timeit(lambda: dev.L.mag_cuda_softmax_rows_f32(dev.p, r.data_ptr, x.data_ptr, 4096, 32768))
+    out["softmax_rows_4096x32768_GBps"] = 8.0 * n / (ms / 1e3) / 1e9
+    m = 4096
+    ms = timeit(lambda: dev.L.mag_cuda_matmul_f32(dev.p, r.data_ptr, x.data_ptr, y.data_ptr, m, m, m), reps=2)
+    out["matmul_4096^3_TFLOPs"] = 2.0 * m ** 3 / (ms / 1e3) / 1e12
+    for t in (x, y, r):
+        t.free()
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,122 @@
+/*
+ * magnetron_cuda.h - C ABI of the B200 (sm_100a) compute backend for magnetron.
+ *
+ * Drop-in entry points
+ * --------------------
+ * The unchanged magnetron core, compiled with MAG_ENABLE_CUDA, declares and
+ * calls exactly these two functions (magnetron/magnetron.c:31-35, called from
+ * mag_compute_device_init / mag_compute_device_destroy at :883-926).  They
+ * replace the stub of the same name in magnetron/magnetron_cuda.cuh:14-15 /
+ * magnetron/magnetron_cuda.cu:39-60, which returned a device whose function
+ * pointers were never set.
+ *
+ * Extension entry points (mag_cuda_*)
+ * -----------------------------------
+ * Additive exports with plain pointers and sizes for what the core's API
+ * cannot express (deferred-graph execution, row reductions, normalised
+ * softmax, two-sided broadcast, batched matmul, fused dense layers, per-op
+ * device timing).  Device pointers are f32 buffers in this device's memory;
+ * work is enqueued on the device's stream (mag_cuda_stream).  Every function
+ * returns 0 on success or a nonzero code (a cudaError_t value, or
+ * MAG_CUDA_E_* below) and never aborts.
+ */
+#ifndef MAGNETRON_CUDA_H
+#define MAGNETRON_CUDA_H
+
+#include <stdint.h>
+#include <stddef.h>
+#include "mag_cuda_abi.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define MAG_CUDA_EXPORT __attribute__((visibility("default")))
+#else
+#define MAG_CUDA_EXPORT
+#endif
+
+/* Error codes beyond the cudaError_t range. */
+#define MAG_CUDA_E_INVALID 10001     /* bad argument (shape, size, null) */
+#define MAG_CUDA_E_DEVICE_WAIT 10002 /* a kernel's bounded wait expired (device status word) */
+#define MAG_CUDA_E_UNSUPPORTED 10003 /* op not available (e.g. the reference panics with NYI) */
+
+/* ---- drop-in device interface (magnetron/magnetron_cuda.cuh:14-15) ---- */
+
+/* Creates the CUDA compute device for a context.  The GPU is MAG_CUDA_DEVICE
+ * if set, else LOCAL_RANK, else the current device.  Returns NULL when no
+ * sm_100 GPU is usable, which makes the core fall back to the CPU device
+ * (magnetron/magnetron.c:895-899). */
+MAG_CUDA_EXPORT mag_compute_device_t* mag_init_device_cuda(mag_ctx_t* ctx);
+/* Releases the device created above (all tensors must be gone). */
+MAG_CUDA_EXPORT void mag_destroy_device_cuda(mag_compute_device_t* dvc);
+
+/* ---- device handle ---- */
+MAG_CUDA_EXPORT int mag_cuda_device_ordinal(mag_compute_device_t* dvc);
+MAG_CUDA_EXPORT void* mag_cuda_stream(mag_compute_device_t* dvc);          /* cudaStream_t */
+MAG_CUDA_EXPORT int mag_cuda_synchronize(mag_compute_device_t* dvc);       /* waits, reports async errors */
+MAG_CUDA_EXPORT int mag_cuda_last_error(mag_compute_device_t* dvc);        /* sticky error of the eager path */
+/* Bytes currently held by tensor storage of this device. */
+MAG_CUDA_EXPORT size_t mag_cuda_memory_in_use(mag_compute_device_t* dvc);
+
+/* ---- deferred graphs (no counterpart in the reference, which records
+ * op_inputs in MAG_EXEC_MODE_DEFERRED but never executes them,
+ * magnetron/magnetron.c:1785-1787) ---- */
+/* Runs every node that root depends on, inputs first.  The first call for a
+ * root captures the launch sequence into a CUDA graph; later calls with the
+ * same node set replay it.  Returns after enqueueing (asynchronous). */
+MAG_CUDA_EXPORT int mag_cuda_graph_exec(mag_compute_device_t* dvc, mag_tensor_t* root);
+/* Drops the cached graph of root (call before freeing the graph's tensors). */
+MAG_CUDA_EXPORT int mag_cuda_graph_release(mag_compute_device_t* dvc, mag_tensor_t* root);
+/* Executes one node eagerly, exactly as eager_exec_fwd would. */
+MAG_CUDA_EXPORT int mag_cuda_exec_node(mag_compute_device_t* dvc, mag_tensor_t* node);
+
+/* ---- plain-pointer forms of the core's ops (same arithmetic as eager_exec_fwd) ---- */
+/* Unary / scalar op (op = MAG_ABI_OP_*), rows x cols, row starts at ri*r_s1 / ri*x_s1. */
+MAG_CUDA_EXPORT int mag_cuda_unary_f32(mag_compute_device_t* dvc, int op, float* r, const float* x, int64_t rows,
+                                       int64_t cols, int64_t r_s1, int64_t x_s1, float xi);
+/* Binary tiling-broadcast op, shapes and strides in elements, 6 entries each. */
+MAG_CUDA_EXPORT int mag_cuda_binary_f32(mag_compute_device_t* dvc, int op, float* r, const float* x,
+                                        const float* y, const int64_t* x_dims, const int64_t* x_strides,
+                                        const int64_t* r_strides, const int64_t* y_dims, const int64_t* y_strides);
+/* Full reduction (SUM/MEAN/MIN/MAX) of a 6-D tensor into r[0]. */
+MAG_CUDA_EXPORT int mag_cuda_reduce_f32(mag_compute_device_t* dvc, int op, float* r, const float* x,
+                                        const int64_t* x_dims, const int64_t* x_strides);
+/* R[M,N] = X[M,K] Y[K,N], all row-major. */
+MAG_CUDA_EXPORT int mag_cuda_matmul_f32(mag_compute_device_t* dvc, float* r, const float* x, const float* y,
+                                        int64_t M, int64_t K, int64_t N);
+
+/* ---- extensions beyond the core's API ---- */
+/* r[i] = x[i mod x_d] (op) y[i mod y_d] per dim; r_dims[k] must be a multiple of both. */
+MAG_CUDA_EXPORT int mag_cuda_broadcast2_f32(mag_compute_device_t* dvc, int op, float* r, const float* x,
+                                            const float* y, const int64_t* r_dims, const int64_t* x_dims,
+                                            const int64_t* y_dims);
+/* Per-row SUM/MEAN/MIN/MAX of a rows x cols row-major matrix into r[rows]. */
+MAG_CUDA_EXPORT int mag_cuda_reduce_rows_f32(mag_compute_device_t* dvc, int op, float* r, const float* x,
+                                             int64_t rows, int64_t cols);
+/* Normalised softmax of each row: exp(x - max) / sum. */
+MAG_CUDA_EXPORT int mag_cuda_softmax_rows_f32(mag_compute_device_t* dvc, float* r, const float* x, int64_t rows,
+                                              int64_t cols);
+/* R[b] = X[b] Y[b] for b < batch, each M x K times K x N. */
+MAG_CUDA_EXPORT int mag_cuda_matmul_batched_f32(mag_compute_device_t* dvc, float* r, const float* x,
+                                                const float* y, int64_t batch, int64_t M, int64_t K, int64_t N);
+
+/* ---- per-op device timing (the core's profiler times only the enqueue) ---- */
+MAG_CUDA_EXPORT int mag_cuda_profile_start(mag_compute_device_t* dvc);
+/* Adds the device time of every op finished so far (eager ops and the op
+ * event nodes of graphs captured while profiling) to the per-op totals. */
+MAG_CUDA_EXPORT int mag_cuda_profile_collect(mag_compute_device_t* dvc);
+/* Per-op totals: executions and device microseconds. */
+MAG_CUDA_EXPORT int mag_cuda_profile_stats(mag_compute_device_t* dvc, int op, uint64_t* count, double* total_us);
+/* Collects, then prints or writes (csv_path != NULL) per-op device time in the
+ * core's table layout (magnetron/magnetron.c:1093-1111), and stops. */
+MAG_CUDA_EXPORT int mag_cuda_profile_stop(mag_compute_device_t* dvc, const char* csv_path);
+
+/* Number of kernels this library launched since load (launch accounting). */
+MAG_CUDA_EXPORT uint64_t mag_cuda_kernel_launches(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MAGNETRON_CUDA_H */

@@ -1,0 +1,215 @@
+// k_matmul_exact.cu - CUDA-core f32 matmul kernels.
+//
+// mag_blas_matmul_f32 (magnetron/magnetron_cpu.c:2151-2185) reads X as a
+// row-major M x K buffer and Y as K x N and accumulates, for each output,
+//   r = 0;  for k = 0..K-1:  r = r + X[i][k]*Y[k][j]
+// with the product and the sum rounded separately (the x86 build has no FMA).
+//
+// matmul_exact keeps exactly that order and rounding per output: a register
+// tiled kernel whose k loop runs in ascending order with __fmul_rn/__fadd_rn,
+// so its results are bit-identical to the reference.  Tile sizes are picked so
+// that the grid covers the GPU for small problems (the 2-layer MLP's
+// 256x784x256 product runs on 64 CTAs with 32x32 tiles).
+//
+// matmul_skinny serves M <= 16 (matrix-vector-like products, HBM-bound on
+// Y): K is split across CTAs so that all SMs stream Y, partial sums go to a
+// scratch buffer and a second kernel adds the K slices in a fixed order.  It
+// uses FMA and a different summation order, so it is accurate to f32
+// rounding (well inside 1e-5 relative) but not bit-identical.
+#include <cuda_runtime.h>
+#include <cstdint>
+#include "mcu_kernels.h"
+
+namespace {
+
+constexpr int kThreads = 256;
+
+int sm_count() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0) n = 148;
+    }
+    return n;
+}
+
+// BM x BN output tile per CTA, TM x TN per thread, BK-deep shared stages.
+template <int BM, int BN, int TM, int TN, int BK>
+__global__ void __launch_bounds__(kThreads) matmul_exact(float* __restrict__ r, const float* __restrict__ x,
+                                                         const float* __restrict__ y, int64_t M, int64_t K,
+                                                         int64_t N, int64_t r_ld, int accumulate) {
+    static_assert((BM / TM) * (BN / TN) == kThreads, "thread tiling");
+    __shared__ float As[BK][BM + 1];
+    __shared__ float Bs[BK][BN];
+    const int64_t b = blockIdx.z;
+    x += b * M * K;
+    y += b * K * N;
+    r += b * M * r_ld;
+    const int64_t m0 = (int64_t)blockIdx.y * BM;
+    const int64_t n0 = (int64_t)blockIdx.x * BN;
+    const int tx = threadIdx.x % (BN / TN);
+    const int ty = threadIdx.x / (BN / TN);
+    float acc[TM][TN];
+#pragma unroll
+    for (int i = 0; i < TM; ++i)
+#pragma unroll
+        for (int j = 0; j < TN; ++j) {
+            int64_t gi = m0 + ty * TM + i, gj = n0 + tx * TN + j;
+            acc[i][j] = (accumulate && gi < M && gj < N) ? r[gi * r_ld + gj] : 0.0f;
+        }
+    for (int64_t k0 = 0; k0 < K; k0 += BK) {
+        for (int t = threadIdx.x; t < BM * BK; t += kThreads) {
+            int mi = t / BK, ki = t % BK;
+            int64_t gm = m0 + mi, gk = k0 + ki;
+            As[ki][mi] = (gm < M && gk < K) ? x[gm * K + gk] : 0.0f;
+        }
+        for (int t = threadIdx.x; t < BN * BK; t += kThreads) {
+            int ki = t / BN, ni = t % BN;
+            int64_t gk = k0 + ki, gn = n0 + ni;
+            Bs[ki][ni] = (gk < K && gn < N) ? y[gk * N + gn] : 0.0f;
+        }
+        __syncthreads();
+        const int kk_end = (int)((K - k0) < BK ? (K - k0) : BK);
+        for (int kk = 0; kk < kk_end; ++kk) {
+            float a[TM], bv[TN];
+#pragma unroll
+            for (int i = 0; i < TM; ++i) a[i] = As[kk][ty * TM + i];
+#pragma unroll
+            for (int j = 0; j < TN; ++j) bv[j] = Bs[kk][tx * TN + j];
+#pragma unroll
+            for (int i = 0; i < TM; ++i)
+#pragma unroll
+                for (int j = 0; j < TN; ++j) acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(a[i], bv[j]));
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < TM; ++i)
+#pragma unroll
+        for (int j = 0; j < TN; ++j) {
+            int64_t gi = m0 + ty * TM + i, gj = n0 + tx * TN + j;
+            if (gi < M && gj < N) r[gi * r_ld + gj] = acc[i][j];
+        }
+}
+
+template <int BM, int BN, int TM, int TN>
+cudaError_t launch_exact(float* r, const float* x, const float* y, int64_t batch, int64_t M, int64_t K, int64_t N,
+                         int64_t r_ld, int accumulate, cudaStream_t st) {
+    dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + BM - 1) / BM), (unsigned)batch);
+    matmul_exact<BM, BN, TM, TN, 16><<<grid, kThreads, 0, st>>>(r, x, y, M, K, N, r_ld, accumulate);
+    return cudaGetLastError();
+}
+
+// ------------------------------------------------------------- skinny ---
+
+constexpr int kSkinnyRows = 16;
+constexpr int kSkinnyCols = kThreads * 4;
+
+// Partial product of X[0:M, k0:k0+KC] and Y[k0:k0+KC, cols]; thread owns 4 columns.
+__global__ void __launch_bounds__(kThreads) matmul_skinny_part(float* __restrict__ part, const float* __restrict__ x,
+                                                               const float* __restrict__ y, int M, int64_t K,
+                                                               int64_t N, int64_t kc) {
+    __shared__ float xs[kSkinnyRows][64];
+    const int64_t c = (int64_t)blockIdx.x * kSkinnyCols + 4 * threadIdx.x;
+    const int64_t k0 = (int64_t)blockIdx.y * kc;
+    const int64_t k1 = (k0 + kc < K) ? k0 + kc : K;
+    const bool vec = (N % 4 == 0) && (((uintptr_t)y & 15) == 0);
+    float acc[kSkinnyRows][4];
+#pragma unroll
+    for (int m = 0; m < kSkinnyRows; ++m) acc[m][0] = acc[m][1] = acc[m][2] = acc[m][3] = 0.0f;
+    for (int64_t kb = k0; kb < k1; kb += 64) {
+        const int kn = (int)((k1 - kb) < 64 ? (k1 - kb) : 64);
+        __syncthreads();
+        for (int t = threadIdx.x; t < kSkinnyRows * 64; t += kThreads) {
+            int m = t / 64, kk = t % 64;
+            xs[m][kk] = (m < M && kk < kn) ? x[(int64_t)m * K + kb + kk] : 0.0f;
+        }
+        __syncthreads();
+        if (c < N) {
+#pragma unroll 4
+            for (int kk = 0; kk < kn; ++kk) {
+                float4 yv;
+                const float* py = y + (kb + kk) * N + c;
+                if (vec && c + 3 < N) yv = __ldcs((const float4*)py);
+                else {
+                    yv.x = py[0];
+                    yv.y = c + 1 < N ? py[1] : 0.0f;
+                    yv.z = c + 2 < N ? py[2] : 0.0f;
+                    yv.w = c + 3 < N ? py[3] : 0.0f;
+                }
+#pragma unroll
+                for (int m = 0; m < kSkinnyRows; ++m) {
+                    float xv = xs[m][kk];
+                    acc[m][0] = fmaf(xv, yv.x, acc[m][0]);
+                    acc[m][1] = fmaf(xv, yv.y, acc[m][1]);
+                    acc[m][2] = fmaf(xv, yv.z, acc[m][2]);
+                    acc[m][3] = fmaf(xv, yv.w, acc[m][3]);
+                }
+            }
+        }
+    }
+    if (c < N) {
+        float* p = part + (int64_t)blockIdx.y * M * N;
+        for (int m = 0; m < M; ++m)
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+                if (c + q < N) p[(int64_t)m * N + c + q] = acc[m][q];
+    }
+}
+
+__global__ void __launch_bounds__(kThreads) matmul_skinny_sum(float* __restrict__ r, const float* __restrict__ part,
+                                                              int64_t MN, int nslices, int64_t N, int64_t r_ld) {
+    for (int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x; i < MN; i += (int64_t)gridDim.x * kThreads) {
+        float s = 0.0f;
+        for (int k = 0; k < nslices; ++k) s += part[(int64_t)k * MN + i];
+        r[(i / N) * r_ld + (i % N)] = s;
+    }
+}
+
+int64_t skinny_slices(int64_t K, int64_t N) {
+    int64_t colblocks = (N + kSkinnyCols - 1) / kSkinnyCols;
+    int64_t want = (2 * (int64_t)sm_count() + colblocks - 1) / colblocks;
+    int64_t maxs = (K + 63) / 64;
+    if (want > maxs) want = maxs;
+    if (want < 1) want = 1;
+    return want;
+}
+
+}  // namespace
+
+extern "C" int mcu_launch_matmul_exact(float* r, const float* x, const float* y, int64_t batch, int64_t M,
+                                       int64_t K, int64_t N, int64_t r_ld, int accumulate, cudaStream_t st) {
+    if (batch <= 0 || M <= 0 || N <= 0) return (int)cudaSuccess;
+    if (batch >= 65536 || (M + 15) / 16 >= 65536) return (int)cudaErrorInvalidValue;
+    const int64_t target = 2 * (int64_t)sm_count();
+    auto blocks = [&](int64_t bm, int64_t bn) { return batch * ((M + bm - 1) / bm) * ((N + bn - 1) / bn); };
+    cudaError_t e;
+    if (blocks(128, 128) >= target) e = launch_exact<128, 128, 8, 8>(r, x, y, batch, M, K, N, r_ld, accumulate, st);
+    else if (blocks(64, 64) >= target) e = launch_exact<64, 64, 4, 4>(r, x, y, batch, M, K, N, r_ld, accumulate, st);
+    else if (blocks(32, 32) >= target / 2) e = launch_exact<32, 32, 2, 2>(r, x, y, batch, M, K, N, r_ld, accumulate, st);
+    else e = launch_exact<16, 16, 1, 1>(r, x, y, batch, M, K, N, r_ld, accumulate, st);
+    return (int)e;
+}
+
+extern "C" size_t mcu_matmul_skinny_scratch_bytes(int64_t M, int64_t K, int64_t N) {
+    return (size_t)skinny_slices(K, N) * (size_t)M * (size_t)N * sizeof(float);
+}
+
+extern "C" int mcu_launch_matmul_skinny(float* r, const float* x, const float* y, int64_t M, int64_t K, int64_t N,
+                                        int64_t r_ld, void* scratch, cudaStream_t st) {
+    if (M <= 0 || N <= 0) return (int)cudaSuccess;
+    if (M > kSkinnyRows) return (int)cudaErrorInvalidValue;
+    int64_t slices = skinny_slices(K, N);
+    int64_t kc = (K + slices - 1) / slices;
+    slices = (K + kc - 1) / kc;
+    if (slices < 1) slices = 1;
+    dim3 grid((unsigned)((N + kSkinnyCols - 1) / kSkinnyCols), (unsigned)slices);
+    matmul_skinny_part<<<grid, kThreads, 0, st>>>((float*)scratch, x, y, (int)M, K, N, kc);
+    int64_t MN = M * N;
+    int64_t g = (MN + kThreads - 1) / kThreads;
+    if (g > 4 * sm_count()) g = 4 * sm_count();
+    matmul_skinny_sum<<<(unsigned)g, kThreads, 0, st>>>(r, (const float*)scratch, MN, (int)slices, N, r_ld);
+    return (int)cudaGetLastError();
+}

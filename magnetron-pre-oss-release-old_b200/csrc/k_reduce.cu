@@ -1,0 +1,415 @@
+// k_reduce.cu - reductions and the row softmax.
+//
+// Full-tensor SUM/MEAN/MIN/MAX follow mag_blas_{sum,mean,min,max}_f32
+// (magnetron/magnetron_cpu.c:1034-1152): the value goes to r[0]; sums are
+// accumulated in double (mag_vsum_f64_f32, :477-492) and rounded to f32 once,
+// MEAN divides the double sum by numel first; MIN/MAX use fminf/fmaxf.  The
+// GPU adds in a fixed tree order (per-thread, warp shuffle, per-block, then one
+// block over the block partials), so results are deterministic run to run.
+//
+// Row reductions and the normalised row softmax are extensions with the same
+// arithmetic per row.  The softmax keeps a whole row on chip: a thread-block
+// cluster of 1..8 CTAs splits the row, each CTA holds its slice in shared
+// memory, and the row max and the double sum are combined across the cluster
+// through distributed shared memory, so HBM sees one read and one write per
+// element (8 B/elem) and exp is evaluated once.
+#include <cuda_runtime.h>
+#include <cooperative_groups.h>
+#include <cstdint>
+#include <cfloat>
+#include "mcu_math.cuh"
+#include "mcu_kernels.h"
+
+namespace cg = cooperative_groups;
+using namespace mcu;
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kMaxPartials = 1024;
+
+int sm_count() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0) n = 148;
+    }
+    return n;
+}
+
+__device__ __forceinline__ double warp_sum(double v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_min(float v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v = fminf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+struct WSum { __device__ __forceinline__ double operator()(double v) const { return warp_sum(v); } };
+struct WMin { __device__ __forceinline__ float operator()(float v) const { return warp_min(v); } };
+struct WMax { __device__ __forceinline__ float operator()(float v) const { return warp_max(v); } };
+
+// Block-wide combine; every thread gets the result.
+template <typename T, typename F>
+__device__ __forceinline__ T block_combine(T v, F warp_fn, T* sh) {
+    v = warp_fn(v);
+    int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    __syncthreads();
+    if (l == 0) sh[w] = v;
+    __syncthreads();
+    int nw = blockDim.x >> 5;
+    T t = l < nw ? sh[l] : sh[0];
+    t = warp_fn(t);
+    return t;
+}
+
+struct Acc {
+    double sum;
+    float mn, mx;
+};
+
+__device__ __forceinline__ void acc_add(Acc& a, float v) {
+    a.sum += (double)v;
+    a.mn = fminf(a.mn, v);
+    a.mx = fmaxf(a.mx, v);
+}
+
+// Pass 1: each block folds a grid-stride share of the elements.
+// Canonical layout: elements are linear.  Otherwise rows of x_d0 elements
+// start at sum_k i_k*x_sk (k = 1..5).
+__global__ void __launch_bounds__(kThreads) reduce_pass1(const float* __restrict__ x, uint64_t n, int canonical,
+                                                         FastDiv d0, FastDiv d1, FastDiv d2, FastDiv d3, FastDiv d4,
+                                                         int64_t s1, int64_t s2, int64_t s3, int64_t s4, int64_t s5,
+                                                         double* __restrict__ psum, float* __restrict__ pmin,
+                                                         float* __restrict__ pmax) {
+    Acc a{0.0, INFINITY, -INFINITY};
+    uint64_t stride = (uint64_t)gridDim.x * kThreads;
+    uint64_t i = (uint64_t)blockIdx.x * kThreads + threadIdx.x;
+    if (canonical) {
+        const float4* x4 = (const float4*)x;
+        uint64_t n4 = ((uintptr_t)x & 15) == 0 ? n / 4 : 0;
+        for (uint64_t j = i; j < n4; j += stride) {
+            float4 v = __ldcs(x4 + j);
+            acc_add(a, v.x); acc_add(a, v.y); acc_add(a, v.z); acc_add(a, v.w);
+        }
+        for (uint64_t j = n4 * 4 + i; j < n; j += stride) acc_add(a, x[j]);
+    } else {
+        for (uint64_t j = i; j < n; j += stride) {
+            uint32_t q = (uint32_t)j;
+            uint32_t row = fdiv(q, d0);
+            uint32_t c = q - row * d0.d;
+            int64_t off = c;
+            uint32_t t;
+            t = fdiv(row, d1); off += (int64_t)(row - t * d1.d) * s1; row = t;
+            t = fdiv(row, d2); off += (int64_t)(row - t * d2.d) * s2; row = t;
+            t = fdiv(row, d3); off += (int64_t)(row - t * d3.d) * s3; row = t;
+            t = fdiv(row, d4); off += (int64_t)(row - t * d4.d) * s4; row = t;
+            off += (int64_t)row * s5;
+            acc_add(a, x[off]);
+        }
+    }
+    __shared__ double shd[32];
+    __shared__ float shf[32];
+    double s = block_combine(a.sum, WSum(), shd);
+    float mn = block_combine(a.mn, WMin(), shf);
+    float mx = block_combine(a.mx, WMax(), shf);
+    if (threadIdx.x == 0) {
+        psum[blockIdx.x] = s;
+        pmin[blockIdx.x] = mn;
+        pmax[blockIdx.x] = mx;
+    }
+}
+
+__global__ void __launch_bounds__(kThreads) reduce_pass2(int op, int nparts, double numel,
+                                                         const double* __restrict__ psum, const float* __restrict__ pmin,
+                                                         const float* __restrict__ pmax, float* __restrict__ r) {
+    Acc a{0.0, INFINITY, -INFINITY};
+    for (int i = threadIdx.x; i < nparts; i += kThreads) {
+        a.sum += psum[i];
+        a.mn = fminf(a.mn, pmin[i]);
+        a.mx = fmaxf(a.mx, pmax[i]);
+    }
+    __shared__ double shd[32];
+    __shared__ float shf[32];
+    double s = block_combine(a.sum, WSum(), shd);
+    float mn = block_combine(a.mn, WMin(), shf);
+    float mx = block_combine(a.mx, WMax(), shf);
+    if (threadIdx.x == 0) {
+        if (op == OP_SUM) r[0] = (float)s;
+        else if (op == OP_MEAN) r[0] = (float)(s / numel);
+        else if (op == OP_MIN) r[0] = mn;
+        else r[0] = mx;
+    }
+}
+
+// -------------------------------------------------------- row reductions ---
+
+template <int OP>
+__device__ __forceinline__ void row_fold(const float* __restrict__ p, uint32_t cols, int tid, int nthr, double& s,
+                                         float& m) {
+    bool vec = (cols % 4 == 0) && (((uintptr_t)p & 15) == 0);
+    if (vec) {
+        const float4* p4 = (const float4*)p;
+        for (uint32_t c = tid; c < cols / 4; c += nthr) {
+            float4 v = __ldcs(p4 + c);
+            if constexpr (OP == OP_SUM || OP == OP_MEAN) s += (double)v.x + (double)v.y + (double)v.z + (double)v.w;
+            else if constexpr (OP == OP_MIN) m = fminf(fminf(m, v.x), fminf(fminf(v.y, v.z), v.w));
+            else m = fmaxf(fmaxf(m, v.x), fmaxf(fmaxf(v.y, v.z), v.w));
+        }
+    } else {
+        for (uint32_t c = tid; c < cols; c += nthr) {
+            float v = p[c];
+            if constexpr (OP == OP_SUM || OP == OP_MEAN) s += (double)v;
+            else if constexpr (OP == OP_MIN) m = fminf(m, v);
+            else m = fmaxf(m, v);
+        }
+    }
+}
+
+template <int OP>
+__device__ __forceinline__ float row_result(double s, float m, uint32_t cols) {
+    if constexpr (OP == OP_SUM) return (float)s;
+    else if constexpr (OP == OP_MEAN) return (float)(s / (double)cols);
+    else return m;
+}
+
+// One warp per row (short rows).
+template <int OP>
+__global__ void __launch_bounds__(kThreads) reduce_rows_warp(float* __restrict__ r, const float* __restrict__ x,
+                                                             uint64_t rows, uint32_t cols) {
+    uint64_t w = ((uint64_t)blockIdx.x * kThreads + threadIdx.x) >> 5;
+    uint64_t nw = ((uint64_t)gridDim.x * kThreads) >> 5;
+    int l = threadIdx.x & 31;
+    for (; w < rows; w += nw) {
+        double s = 0.0;
+        float m = OP == OP_MIN ? INFINITY : -INFINITY;
+        row_fold<OP>(x + w * cols, cols, l, 32, s, m);
+        s = warp_sum(s);
+        m = OP == OP_MIN ? warp_min(m) : warp_max(m);
+        if (l == 0) r[w] = row_result<OP>(s, m, cols);
+    }
+}
+
+// One block per row (long rows).
+template <int OP>
+__global__ void __launch_bounds__(kThreads) reduce_rows_block(float* __restrict__ r, const float* __restrict__ x,
+                                                              uint64_t rows, uint32_t cols) {
+    __shared__ double shd[32];
+    __shared__ float shf[32];
+    for (uint64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+        double s = 0.0;
+        float m = OP == OP_MIN ? INFINITY : -INFINITY;
+        row_fold<OP>(x + row * cols, cols, threadIdx.x, kThreads, s, m);
+        s = block_combine(s, WSum(), shd);
+        m = OP == OP_MIN ? block_combine(m, WMin(), shf) : block_combine(m, WMax(), shf);
+        if (threadIdx.x == 0) r[row] = row_result<OP>(s, m, cols);
+    }
+}
+
+template <int OP>
+cudaError_t launch_rows_op(float* r, const float* x, int64_t rows, int64_t cols, cudaStream_t st) {
+    unsigned cap = (unsigned)sm_count() * 8;
+    if (cols < 2048) {
+        uint64_t g = ((uint64_t)rows * 32 + kThreads - 1) / kThreads;
+        reduce_rows_warp<OP><<<(unsigned)(g < cap ? g : cap), kThreads, 0, st>>>(r, x, (uint64_t)rows, (uint32_t)cols);
+    } else {
+        uint64_t g = (uint64_t)rows;
+        reduce_rows_block<OP><<<(unsigned)(g < cap ? g : cap), kThreads, 0, st>>>(r, x, (uint64_t)rows, (uint32_t)cols);
+    }
+    return cudaGetLastError();
+}
+
+// ----------------------------------------------------------- row softmax ---
+
+constexpr int kSoftmaxThreads = 512;
+
+// A cluster of C CTAs owns one row; CTA k keeps columns [k*chunk, (k+1)*chunk)
+// in shared memory.  Phase 1: row max.  Phase 2: e = exp(x - max) (reference
+// lane/tail split), kept in shared memory, with a double sum.  Phase 3: e/sum.
+__global__ void __launch_bounds__(kSoftmaxThreads) softmax_rows_cluster(float* __restrict__ r,
+                                                                        const float* __restrict__ x, uint32_t cols,
+                                                                        uint32_t chunk) {
+    extern __shared__ __align__(16) float sm[];
+    __shared__ float sh_max[32];
+    __shared__ double sh_sum[32];
+    __shared__ float slot_max;
+    __shared__ double slot_sum;
+    cg::cluster_group cluster = cg::this_cluster();
+    const uint32_t crank = cluster.block_rank();
+    const uint32_t csize = cluster.num_blocks();
+    const uint64_t row = blockIdx.x / csize;
+    const uint32_t c0 = crank * chunk;
+    const uint32_t n = (c0 + chunk <= cols) ? chunk : (cols > c0 ? cols - c0 : 0);
+    const float* px = x + row * cols + c0;
+    float* pr = r + row * cols + c0;
+    const uint32_t vec_end = cols & ~3u;
+    const bool vec = (n % 4 == 0) && (cols % 4 == 0) && ((((uintptr_t)px) | ((uintptr_t)pr)) & 15) == 0;
+
+    float m = -INFINITY;
+    if (vec) {
+        for (uint32_t c = threadIdx.x; c < n / 4; c += kSoftmaxThreads) {
+            float4 v = __ldcs((const float4*)px + c);
+            ((float4*)sm)[c] = v;
+            m = fmaxf(m, fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)));
+        }
+    } else {
+        for (uint32_t c = threadIdx.x; c < n; c += kSoftmaxThreads) {
+            float v = px[c];
+            sm[c] = v;
+            m = fmaxf(m, v);
+        }
+    }
+    m = block_combine(m, WMax(), sh_max);
+    if (threadIdx.x == 0) slot_max = m;
+    cluster.sync();
+    float gm = -INFINITY;
+    for (uint32_t k = 0; k < csize; ++k) gm = fmaxf(gm, *cluster.map_shared_rank(&slot_max, k));
+
+    double s = 0.0;
+    for (uint32_t c = threadIdx.x; c < n; c += kSoftmaxThreads) {
+        float t = fs(sm[c], gm);
+        float e = (c0 + c < vec_end) ? sse_expf(t) : (float)exp((double)t);
+        sm[c] = e;
+        s += (double)e;
+    }
+    s = block_combine(s, WSum(), sh_sum);
+    if (threadIdx.x == 0) slot_sum = s;
+    cluster.sync();
+    double gs = 0.0;
+    for (uint32_t k = 0; k < csize; ++k) gs += *cluster.map_shared_rank(&slot_sum, k);
+    const float fsum = (float)gs;
+
+    if (vec) {
+        for (uint32_t c = threadIdx.x; c < n / 4; c += kSoftmaxThreads) {
+            float4 v = ((float4*)sm)[c];
+            v.x = __fdiv_rn(v.x, fsum); v.y = __fdiv_rn(v.y, fsum);
+            v.z = __fdiv_rn(v.z, fsum); v.w = __fdiv_rn(v.w, fsum);
+            __stcs((float4*)pr + c, v);
+        }
+    } else {
+        for (uint32_t c = threadIdx.x; c < n; c += kSoftmaxThreads) pr[c] = __fdiv_rn(sm[c], fsum);
+    }
+    cluster.sync();  // peers may still read this CTA's slots
+}
+
+// Rows too long for a cluster's shared memory: three passes from HBM.
+__global__ void __launch_bounds__(kSoftmaxThreads) softmax_rows_global(float* __restrict__ r,
+                                                                       const float* __restrict__ x, uint64_t rows,
+                                                                       uint32_t cols) {
+    __shared__ float sh_max[32];
+    __shared__ double sh_sum[32];
+    const uint32_t vec_end = cols & ~3u;
+    for (uint64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+        const float* px = x + row * cols;
+        float* pr = r + row * cols;
+        float m = -INFINITY;
+        for (uint32_t c = threadIdx.x; c < cols; c += kSoftmaxThreads) m = fmaxf(m, px[c]);
+        m = block_combine(m, WMax(), sh_max);
+        double s = 0.0;
+        for (uint32_t c = threadIdx.x; c < cols; c += kSoftmaxThreads) {
+            float t = fs(px[c], m);
+            s += (double)((c < vec_end) ? sse_expf(t) : (float)exp((double)t));
+        }
+        s = block_combine(s, WSum(), sh_sum);
+        const float fsum = (float)s;
+        for (uint32_t c = threadIdx.x; c < cols; c += kSoftmaxThreads) {
+            float t = fs(px[c], m);
+            float e = (c < vec_end) ? sse_expf(t) : (float)exp((double)t);
+            pr[c] = __fdiv_rn(e, fsum);
+        }
+        __syncthreads();
+    }
+}
+
+}  // namespace
+
+extern "C" size_t mcu_reduce_scratch_bytes(void) {
+    return (size_t)kMaxPartials * (sizeof(double) + 2 * sizeof(float));
+}
+
+extern "C" int mcu_launch_reduce(int op, float* r, const float* x, const int64_t* xd, const int64_t* xs,
+                                 void* scratch, cudaStream_t st) {
+    uint64_t n = 1;
+    for (int k = 0; k < 6; ++k) {
+        if (xd[k] <= 0) return (int)cudaErrorInvalidValue;
+        n *= (uint64_t)xd[k];
+    }
+    int canonical = 1;
+    int64_t acc = 1;
+    for (int k = 0; k < 6; ++k) {
+        if (xd[k] != 1 && xs[k] != acc) canonical = 0;
+        acc *= xd[k];
+    }
+    if (!canonical && n >= (1ull << 32)) return (int)cudaErrorInvalidValue;
+    uint64_t want = (n + (uint64_t)kThreads * 16 - 1) / ((uint64_t)kThreads * 16);
+    int nparts = (int)(want < (uint64_t)sm_count() * 4 ? want : (uint64_t)sm_count() * 4);
+    if (nparts > kMaxPartials) nparts = kMaxPartials;
+    if (nparts < 1) nparts = 1;
+    double* psum = (double*)scratch;
+    float* pmin = (float*)(psum + kMaxPartials);
+    float* pmax = pmin + kMaxPartials;
+    FastDiv d[5];
+    for (int k = 0; k < 5; ++k) d[k] = make_fastdiv((uint32_t)(xd[k] < (1ll << 32) ? xd[k] : 1));
+    reduce_pass1<<<nparts, kThreads, 0, st>>>(x, n, canonical, d[0], d[1], d[2], d[3], d[4], xs[1], xs[2], xs[3],
+                                              xs[4], xs[5], psum, pmin, pmax);
+    reduce_pass2<<<1, kThreads, 0, st>>>(op, nparts, (double)n, psum, pmin, pmax, r);
+    return (int)cudaGetLastError();
+}
+
+extern "C" int mcu_launch_reduce_rows(int op, float* r, const float* x, int64_t rows, int64_t cols,
+                                      cudaStream_t st) {
+    if (rows <= 0 || cols <= 0) return (int)cudaSuccess;
+    if (cols >= (1ll << 32)) return (int)cudaErrorInvalidValue;
+    switch (op) {
+        case OP_SUM: return (int)launch_rows_op<OP_SUM>(r, x, rows, cols, st);
+        case OP_MEAN: return (int)launch_rows_op<OP_MEAN>(r, x, rows, cols, st);
+        case OP_MIN: return (int)launch_rows_op<OP_MIN>(r, x, rows, cols, st);
+        case OP_MAX: return (int)launch_rows_op<OP_MAX>(r, x, rows, cols, st);
+        default: return (int)cudaErrorInvalidValue;
+    }
+}
+
+extern "C" int mcu_launch_softmax_rows(float* r, const float* x, int64_t rows, int64_t cols, cudaStream_t st) {
+    if (rows <= 0 || cols <= 0) return (int)cudaSuccess;
+    if (cols >= (1ll << 31) || rows >= (1ll << 31)) return (int)cudaErrorInvalidValue;
+    const size_t kSlice = 32 * 1024;        // preferred bytes of row per CTA
+    const size_t kSliceMax = 192 * 1024;    // hard cap per CTA
+    int csize = 1;
+    size_t bytes = (size_t)cols * 4;
+    while (csize < 8 && (bytes + csize - 1) / csize > kSlice) csize *= 2;
+    size_t chunk = ((size_t)cols + csize - 1) / csize;
+    chunk = (chunk + 3) & ~(size_t)3;
+    if (chunk * 4 > kSliceMax || (uint64_t)rows * csize >= (1ull << 31)) {
+        int g = sm_count() * 4;
+        softmax_rows_global<<<(unsigned)(rows < g ? rows : g), kSoftmaxThreads, 0, st>>>(r, x, (uint64_t)rows,
+                                                                                       (uint32_t)cols);
+        return (int)cudaGetLastError();
+    }
+    size_t smem = chunk * 4;
+    cudaError_t e = cudaFuncSetAttribute(softmax_rows_cluster, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)kSliceMax);
+    if (e != cudaSuccess) return (int)e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(rows * csize));
+    cfg.blockDim = dim3(kSoftmaxThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)csize;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return (int)cudaLaunchKernelEx(&cfg, softmax_rows_cluster, r, x, (uint32_t)cols, (uint32_t)chunk);
+}

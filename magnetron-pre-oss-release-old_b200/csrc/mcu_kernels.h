@@ -1,0 +1,53 @@
+/*
+ * mcu_kernels.h - C-callable launchers of the sm_100a kernels.
+ *
+ * Every launcher enqueues on the given stream and returns a cudaError_t value
+ * (0 on success).  Tensors are f32, strides are in elements, dim 0 is the
+ * fastest dimension, exactly as in the magnetron core.
+ */
+#ifndef MCU_KERNELS_H
+#define MCU_KERNELS_H
+#include <stdint.h>
+#include <stddef.h>
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* k_elementwise.cu */
+int mcu_launch_unary(int op, float* r, const float* x, int64_t rows, int64_t cols, int64_t r_s1, int64_t x_s1,
+                     float xi, cudaStream_t st);
+int mcu_launch_binary(int op, float* r, const float* x, const float* y, const int64_t* x_dims,
+                      const int64_t* x_strides, const int64_t* r_strides, const int64_t* y_dims,
+                      const int64_t* y_strides, cudaStream_t st);
+int mcu_launch_bcast2(int op, float* r, const float* x, const float* y, const int64_t* r_dims,
+                      const int64_t* x_dims, const int64_t* y_dims, cudaStream_t st);
+
+/* k_reduce.cu: scratch needs mcu_reduce_scratch_bytes() bytes of device memory. */
+size_t mcu_reduce_scratch_bytes(void);
+int mcu_launch_reduce(int op, float* r, const float* x, const int64_t* x_dims, const int64_t* x_strides,
+                      void* scratch, cudaStream_t st);
+int mcu_launch_reduce_rows(int op, float* r, const float* x, int64_t rows, int64_t cols, cudaStream_t st);
+int mcu_launch_softmax_rows(float* r, const float* x, int64_t rows, int64_t cols, cudaStream_t st);
+
+/* k_matmul_exact.cu: R[b][i*r_ld + j] = (accumulate ? R : 0) + sum_k X[b][i*K+k]*Y[b][k*N+j],
+ * summed k = 0..K-1 in order with separately rounded multiply and add. */
+int mcu_launch_matmul_exact(float* r, const float* x, const float* y, int64_t batch, int64_t M, int64_t K,
+                            int64_t N, int64_t r_ld, int accumulate, cudaStream_t st);
+
+size_t mcu_matmul_skinny_scratch_bytes(int64_t M, int64_t K, int64_t N);
+int mcu_launch_matmul_skinny(float* r, const float* x, const float* y, int64_t M, int64_t K, int64_t N,
+                             int64_t r_ld, void* scratch, cudaStream_t st);
+
+/* k_matmul_tc.cu: 3xTF32 tcgen05 GEMM, R[M,N] = X[M,K] Y[K,N] (row-major).
+ * scratch needs mcu_matmul_tc_scratch_bytes(M, K, N) bytes. */
+size_t mcu_matmul_tc_scratch_bytes(int64_t M, int64_t K, int64_t N);
+int mcu_launch_matmul_tc(float* r, const float* x, const float* y, int64_t M, int64_t K, int64_t N,
+                         void* scratch, int* status, cudaStream_t st);
+int mcu_matmul_tc_supported(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,332 @@
+"""Python host mirror of the magnetron core's tensor/operator layer over the
+B200 backend's C ABI.
+
+The magnetron core hands its CUDA device a ``mag_tensor_t`` per result and
+calls ``eager_exec_fwd`` on it (magnetron/magnetron.c:1747-1789); tensors get
+their buffers from ``alloc_storage`` and move data with the storage callbacks
+(magnetron/magnetron.c:1653-1656, :1820-1830).  This module creates the same
+structs with ctypes, so Python code (tests, the benchmark, users without the C
+core) can drive ``libmagnetron_cuda.so`` through exactly the interface the
+core uses:
+
+    dev = Device()                       # mag_init_device_cuda
+    x = dev.tensor((4096, 65536)); x.write(host_array)
+    r = dev.op("SIGMOID", x)             # result ctor + eager_exec_fwd
+    r.read()                             # storage.cpy_device_host
+
+Shapes use the core's convention: dim 0 is the fastest (contiguous) dim, so a
+row-major (rows, cols) array is shape (cols, rows).  MATMUL is the exception:
+it reads its buffers as row-major [shape0][shape1] (magnetron/magnetron_cpu.c:2151-2185).
+
+There is no fallback: if the CUDA library is missing or no sm_100 GPU is
+present, constructing a Device raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libmagnetron_cuda.so")
+
+OPS = ["NOP", "CLONE", "VIEW", "TRANSPOSE", "PERMUTE", "MEAN", "MIN", "MAX", "SUM",
+       "ABS", "NEG", "LOG", "SQR", "SQRT", "SIN", "COS", "STEP", "SOFTMAX", "SOFTMAX_DV",
+       "SIGMOID", "SIGMOID_DV", "HARD_SIGMOID", "SILU", "SILU_DV", "TANH", "TANH_DV",
+       "RELU", "RELU_DV", "GELU", "GELU_DV", "ADD", "SUB", "MUL", "DIV",
+       "ADDS", "SUBS", "MULS", "DIVS", "MATMUL"]
+OP = {n: i for i, n in enumerate(OPS)}
+UNARY = set(OPS[OP["ABS"]:OP["GELU_DV"] + 1])
+SCALAR = {"ADDS", "SUBS", "MULS", "DIVS"}
+BINARY = {"ADD", "SUB", "MUL", "DIV"}
+REDUCE = {"MEAN", "MIN", "MAX", "SUM"}
+# ops whose result may alias the first input (mag_op_def inplace column, magnetron/magnetron.h:136-178)
+INPLACE_OK = UNARY | SCALAR | BINARY | {"MATMUL"}
+TFLAG_OWNER, TFLAG_VIEW = 1, 2
+
+E_INVALID, E_DEVICE_WAIT, E_UNSUPPORTED = 10001, 10002, 10003
+
+
+# ---------------------------------------------------------------- ABI structs
+class StorageBuffer(C.Structure):
+    pass
+
+
+SET_FN = C.CFUNCTYPE(None, C.POINTER(StorageBuffer), C.c_size_t, C.c_uint8)
+H2D_FN = C.CFUNCTYPE(None, C.POINTER(StorageBuffer), C.c_size_t, C.c_void_p, C.c_size_t)
+D2H_FN = C.CFUNCTYPE(None, C.POINTER(StorageBuffer), C.c_size_t, C.c_void_p, C.c_size_t)
+StorageBuffer._fields_ = [
+    ("base", C.c_uint64), ("size", C.c_size_t), ("alignment", C.c_size_t), ("host", C.c_void_p),
+    ("set", SET_FN), ("cpy_host_device", H2D_FN), ("cpy_device_host", D2H_FN),
+]
+
+EXEC_FN = C.CFUNCTYPE(None, C.c_void_p, C.c_void_p)
+ALLOC_FN = C.CFUNCTYPE(None, C.c_void_p, C.POINTER(StorageBuffer), C.c_size_t, C.c_size_t)
+FREE_FN = C.CFUNCTYPE(None, C.c_void_p, C.POINTER(StorageBuffer))
+
+
+class ComputeDevice(C.Structure):
+    _fields_ = [
+        ("name", C.c_char * 128), ("impl", C.c_void_p), ("is_async", C.c_bool), ("type", C.c_int32),
+        ("eager_exec_fwd", EXEC_FN), ("eager_exec_bwd", EXEC_FN),
+        ("alloc_storage", ALLOC_FN), ("free_storage", FREE_FN),
+    ]
+
+
+class TensorT(C.Structure):
+    _fields_ = [
+        ("rc_strong", C.c_uint32), ("rc_weak", C.c_uint32), ("ctx", C.c_void_p), ("rank", C.c_int64),
+        ("shape", C.c_int64 * 6), ("strides", C.c_int64 * 6), ("dtype", C.c_int32),
+        ("storage", StorageBuffer), ("numel", C.c_int64), ("flags", C.c_int32), ("op", C.c_int32),
+        ("op_inputs", C.c_void_p * 2), ("op_params", C.c_uint64 * 6), ("view_uplink", C.c_void_p),
+        ("view_offs", C.c_size_t), ("grad", C.c_void_p), ("pmon", C.c_uint64 * 3),
+        ("name", C.c_char * 64), ("ud", C.c_void_p),
+    ]
+
+
+assert C.sizeof(StorageBuffer) == 56 and C.sizeof(ComputeDevice) == 176 and C.sizeof(TensorT) == 384
+
+_lib = None
+
+
+def load_library(path: str = LIB_PATH):
+    """Loads libmagnetron_cuda.so (raises if it was not built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        raise RuntimeError(f"{path} is missing: build it with `make -C {HERE}` (no CPU fallback exists)")
+    L = C.CDLL(path)
+    vp, i64, f32p = C.c_void_p, C.c_int64, C.POINTER(C.c_float)
+    i64p = C.POINTER(C.c_int64)
+    sig = {
+        "mag_init_device_cuda": ([vp], vp),
+        "mag_destroy_device_cuda": ([vp], None),
+        "mag_cuda_device_ordinal": ([vp], C.c_int),
+        "mag_cuda_stream": ([vp], vp),
+        "mag_cuda_synchronize": ([vp], C.c_int),
+        "mag_cuda_last_error": ([vp], C.c_int),
+        "mag_cuda_memory_in_use": ([vp], C.c_size_t),
+        "mag_cuda_graph_exec": ([vp, vp], C.c_int),
+        "mag_cuda_graph_release": ([vp, vp], C.c_int),
+        "mag_cuda_exec_node": ([vp, vp], C.c_int),
+        "mag_cuda_unary_f32": ([vp, C.c_int, vp, vp, i64, i64, i64, i64, C.c_float], C.c_int),
+        "mag_cuda_binary_f32": ([vp, C.c_int, vp, vp, vp, i64p, i64p, i64p, i64p, i64p], C.c_int),
+        "mag_cuda_reduce_f32": ([vp, C.c_int, vp, vp, i64p, i64p], C.c_int),
+        "mag_cuda_matmul_f32": ([vp, vp, vp, vp, i64, i64, i64], C.c_int),
+        "mag_cuda_broadcast2_f32": ([vp, C.c_int, vp, vp, vp, i64p, i64p, i64p], C.c_int),
+        "mag_cuda_reduce_rows_f32": ([vp, C.c_int, vp, vp, i64, i64], C.c_int),
+        "mag_cuda_softmax_rows_f32": ([vp, vp, vp, i64, i64], C.c_int),
+        "mag_cuda_matmul_batched_f32": ([vp, vp, vp, vp, i64, i64, i64, i64], C.c_int),
+        "mag_cuda_profile_start": ([vp], C.c_int),
+        "mag_cuda_profile_stop": ([vp, C.c_char_p], C.c_int),
+        "mag_cuda_profile_collect": ([vp], C.c_int),
+        "mag_cuda_profile_stats": ([vp, C.c_int, C.POINTER(C.c_uint64), C.POINTER(C.c_double)], C.c_int),
+        "mag_cuda_kernel_launches": ([], C.c_uint64),
+    }
+    for name, (args, res) in sig.items():
+        fn = getattr(L, name)
+        fn.argtypes = args
+        fn.restype = res
+    _lib = L
+    return L
+
+
+def i64x6(v) -> C.Array:
+    return (C.c_int64 * 6)(*[int(t) for t in v])
+
+
+def pad6(shape):
+    shape = [int(s) for s in shape]
+    return shape + [1] * (6 - len(shape))
+
+
+def strides6(shape6):
+    s = [1] * 6
+    for i in range(1, 6):
+        s[i] = s[i - 1] * int(shape6[i - 1])
+    return s
+
+
+def f32_param(x: float) -> int:
+    return int(np.array([x], np.float32).view(np.uint32)[0])  # tag 0 = float (magnetron/magnetron.c:1126-1130)
+
+
+class CudaError(RuntimeError):
+    pass
+
+
+def check(rc: int, what: str):
+    if rc:
+        raise CudaError(f"{what} failed with code {rc}")
+
+
+# ------------------------------------------------------------------- tensors
+class Tensor:
+    """One ``mag_tensor_t`` owned by Python, with storage from the device."""
+
+    def __init__(self, dev: "Device", shape, view_of: "Tensor | None" = None):
+        self.dev = dev
+        self.t = TensorT()
+        self.inputs = []
+        shape6 = pad6(shape)
+        rank = len(shape)
+        t = self.t
+        t.rc_strong = 1
+        t.rank = rank
+        for i in range(6):
+            t.shape[i] = shape6[i]
+        for i, s in enumerate(strides6(shape6)):
+            t.strides[i] = s
+        t.dtype = 0
+        t.numel = int(np.prod(shape6))
+        t.op = 0
+        self.base = view_of.base if view_of is not None and view_of.base is not None else view_of
+        if view_of is not None:  # share the viewed tensor's storage (magnetron/magnetron.c:1654-1655)
+            t.flags = TFLAG_VIEW
+            t.storage = view_of.t.storage
+            t.view_uplink = C.addressof(view_of.t)
+            self.owner = False
+        else:
+            t.flags = TFLAG_OWNER
+            dev.dev.alloc_storage(dev.p, C.byref(t.storage), t.numel * 4, 4)
+            self.owner = True
+
+    @property
+    def ptr(self) -> int:
+        return C.addressof(self.t)
+
+    @property
+    def data_ptr(self) -> int:
+        return int(self.t.storage.base)
+
+    @property
+    def shape(self):
+        return tuple(int(self.t.shape[i]) for i in range(int(self.t.rank)))
+
+    @property
+    def numel(self) -> int:
+        return int(self.t.numel)
+
+    def write(self, a: np.ndarray, offset_elems: int = 0):
+        a = np.ascontiguousarray(a, np.float32)
+        st = self.t.storage
+        st.cpy_host_device(C.byref(self.t.storage), offset_elems * 4, a.ctypes.data, a.nbytes)
+
+    def read(self, n: int | None = None) -> np.ndarray:
+        n = self.numel if n is None else n
+        out = np.empty(n, np.float32)
+        st = self.t.storage
+        st.cpy_device_host(C.byref(self.t.storage), 0, out.ctypes.data, out.nbytes)
+        return out
+
+    def fill_zero(self):
+        st = self.t.storage
+        st.set(C.byref(self.t.storage), 0, 0)
+
+    def free(self):
+        if getattr(self, "owner", False) and self.t.storage.base:
+            self.dev.dev.free_storage(self.dev.p, C.byref(self.t.storage))
+        self.owner = False
+
+    def __del__(self):
+        try:
+            if self.dev.alive:
+                self.free()
+        except Exception:
+            pass
+
+
+class Device:
+    """The CUDA compute device, created through mag_init_device_cuda."""
+
+    def __init__(self):
+        L = load_library()
+        p = L.mag_init_device_cuda(None)
+        if not p:
+            raise CudaError("mag_init_device_cuda returned NULL: no usable sm_100 GPU")
+        self.L = L
+        self.p = p
+        self.dev = C.cast(p, C.POINTER(ComputeDevice)).contents
+        self.alive = True
+        self.eager = True
+
+    @property
+    def name(self) -> str:
+        return self.dev.name.decode()
+
+    @property
+    def stream(self) -> int:
+        return int(self.L.mag_cuda_stream(self.p) or 0)
+
+    def sync(self):
+        check(self.L.mag_cuda_synchronize(self.p), "synchronize")
+
+    def close(self):
+        if self.alive:
+            self.sync()
+            self.alive = False
+            self.L.mag_destroy_device_cuda(self.p)
+
+    def tensor(self, shape) -> Tensor:
+        return Tensor(self, shape)
+
+    def from_numpy(self, a: np.ndarray, shape=None) -> Tensor:
+        t = Tensor(self, shape if shape is not None else a.shape[::-1])
+        t.write(a.reshape(-1))
+        return t
+
+    # ---- the core's result constructors + eager execution (magnetron/magnetron.c:1447-1588, :1762-1789)
+    def op(self, name: str, *inputs: Tensor, xi: float | None = None, inplace: bool = False) -> Tensor:
+        x = inputs[0]
+        if inplace and name in INPLACE_OK:
+            r = Tensor(self, x.shape, view_of=x)
+        elif name in REDUCE:
+            r = Tensor(self, [1] + list(pad6(x.shape)[1:]))
+        elif name == "MATMUL":
+            r = Tensor(self, (x.t.shape[0], inputs[1].t.shape[1]))
+        elif name == "CLONE" or name in UNARY or name in SCALAR or name in BINARY:
+            r = Tensor(self, x.shape)
+        else:
+            raise ValueError(name)
+        if name in BINARY:
+            y = inputs[1]
+            if any(int(x.t.shape[i]) % int(y.t.shape[i]) for i in range(6)):
+                raise ValueError(f"{name}: shapes are not broadcastable (magnetron/magnetron.c:1266-1300)")
+        r.t.op = OP[name]
+        for i, t in enumerate(inputs):
+            r.t.op_inputs[i] = t.ptr
+        r.inputs = list(inputs)
+        if xi is not None:
+            r.t.op_params[0] = f32_param(xi)
+        if self.eager:
+            self.exec(r)
+        return r
+
+    def exec(self, r: Tensor):
+        self.dev.eager_exec_fwd(self.p, r.ptr)
+
+    def graph_exec(self, root: Tensor):
+        check(self.L.mag_cuda_graph_exec(self.p, root.ptr), "graph_exec")
+
+    def graph_release(self, root: Tensor):
+        self.L.mag_cuda_graph_release(self.p, root.ptr)
+
+    def launches(self) -> int:
+        return int(self.L.mag_cuda_kernel_launches())
+
+    # ---- per-op device timing
+    def profile_start(self):
+        check(self.L.mag_cuda_profile_start(self.p), "profile_start")
+
+    def profile_collect(self):
+        check(self.L.mag_cuda_profile_collect(self.p), "profile_collect")
+
+    def profile_stats(self, op: str):
+        n, us = C.c_uint64(0), C.c_double(0.0)
+        check(self.L.mag_cuda_profile_stats(self.p, OP[op], C.byref(n), C.byref(us)), "profile_stats")
+        return int(n.value), float(us.value)
+
+    def profile_stop(self, csv_path: str | None = None):
+        check(self.L.mag_cuda_profile_stop(self.p, csv_path.encode() if csv_path else None), "profile_stop")

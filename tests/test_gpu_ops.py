@@ -1,0 +1,289 @@
+"""Parity of every CUDA op family with the oracle, through the device vtable.
+
+Tolerances: bit-exact for IEEE-exact ops and for the vector lanes of the
+restated transcendentals; tails within 2 ulp; tanh within 2 ulp of the
+correctly rounded value; reductions, softmax and tensor-core matmul within
+1e-5 relative; the exact matmul path bit-exact.
+"""
+import itertools
+
+import numpy as np
+import pytest
+
+import mag_b200 as MB
+from harness import oracle, bits_equal, ulp_diff
+from oracle import pad6
+from gpu_util import device, run_op, assert_unary_parity
+
+pytestmark = pytest.mark.gpu
+
+UNARY = ["ABS", "NEG", "LOG", "SQR", "SQRT", "SIN", "COS", "STEP", "SOFTMAX", "SOFTMAX_DV", "SIGMOID",
+         "SIGMOID_DV", "HARD_SIGMOID", "SILU", "TANH", "TANH_DV", "RELU", "RELU_DV", "GELU"]
+SWEEP = [s for s in itertools.product([1, 2, 3, 4, 5, 7], [1, 3, 6], [1, 2, 5], [1, 4], [1, 2], [1, 3])][::7]
+
+
+def _x(n, seed, op):
+    s = oracle().stream(seed)
+    if op in ("LOG", "SQRT"):
+        return s.uniform(n, 0.0, 4.0)
+    return s.uniform(n, -8.0, 8.0)
+
+
+@pytest.mark.parametrize("op", UNARY)
+def test_unary_shape_sweep(op):
+    dev = device()
+    o = oracle()
+    for i, sh in enumerate(SWEEP):
+        s6 = pad6(sh)
+        n = int(np.prod(s6))
+        x = _x(n, 1000 + i, op)
+        got, r, ts = run_op(dev, op, [x], [sh])
+        assert_unary_parity(op, x, got, o.unary(op, x, s6), s6)
+
+
+@pytest.mark.parametrize("op", ["ADDS", "SUBS", "MULS", "DIVS"])
+def test_scalar_ops(op):
+    dev = device()
+    o = oracle()
+    for i, sh in enumerate(SWEEP[:20]):
+        s6 = pad6(sh)
+        x = _x(int(np.prod(s6)), 2000 + i, op)
+        xi = 0.221 * (i + 1)
+        got, _, _ = run_op(dev, op, [x], [sh], xi=xi)
+        assert bits_equal(got, o.unary(op, x, s6, xi)).all()
+
+
+@pytest.mark.parametrize("op", ["ADD", "SUB", "MUL", "DIV"])
+def test_binary_same_and_broadcast(op):
+    """Same-shape and tiling-broadcast sweeps (test/compute_cpu.cpp:174-338 style)."""
+    dev = device()
+    o = oracle()
+    cases = []
+    for i, sh in enumerate(SWEEP[:24]):
+        cases.append((sh, sh))
+    for f in (2, 3):
+        for sh in [(1, 2, 1), (2, 1, 3), (3, 2, 2, 1, 1, 2), (4, 1, 1, 2)]:
+            cases.append((tuple(d * f for d in sh), sh))
+    cases += [((16, 8), (16, 1)), ((16, 8), (1, 8)), ((256, 4, 3), (256, 1, 3)), ((64, 6), (8, 3))]
+    for i, (xs, ys) in enumerate(cases):
+        x6, y6 = pad6(xs), pad6(ys)
+        s = o.stream(3000 + i)
+        x = s.uniform(int(np.prod(x6)), -3.0, 3.0)
+        y = s.uniform(int(np.prod(y6)), 0.5, 5.0) if op == "DIV" else s.uniform(int(np.prod(y6)), -5.0, 5.0)
+        got, _, _ = run_op(dev, op, [x, y], [xs, ys])
+        assert bits_equal(got, o.binary(op, x, x6, y, y6)).all(), (xs, ys)
+
+
+def test_inplace_ops_alias_the_input():
+    dev = device()
+    o = oracle()
+    x = _x(96, 4000, "ADD")
+    y = _x(96, 4001, "ADD")
+    tx, ty = dev.tensor((8, 12)), dev.tensor((8, 12))
+    tx.write(x)
+    ty.write(y)
+    r = dev.op("MUL", tx, ty, inplace=True)
+    assert r.data_ptr == tx.data_ptr
+    want = o.binary("MUL", x, pad6((8, 12)), y, pad6((8, 12)))
+    assert bits_equal(tx.read(), want).all()
+    r2 = dev.op("SIGMOID", tx, inplace=True)
+    assert bits_equal(r2.read(), o.unary("SIGMOID", want, pad6((8, 12)))).all()
+
+
+def test_strided_unary_reads_rows_at_s1():
+    """A transposed view still reads each row contiguously from ri*s1 (magnetron/magnetron_cpu.c:1163-1174)."""
+    dev = device()
+    x = _x(12, 4100, "ABS")
+    tx = dev.tensor((3, 4))
+    tx.write(x)
+    v = MB.Tensor(dev, (4, 3), view_of=tx)  # transpose: swap shape/strides like the core does
+    v.t.shape[0], v.t.shape[1] = 4, 3
+    v.t.strides[0], v.t.strides[1] = 3, 1
+    r = dev.tensor((4, 3))
+    r.t.op = MB.OP["NEG"]
+    r.t.op_inputs[0] = v.ptr
+    dev.exec(r)
+    got = r.read()
+    want = np.zeros(12, np.float32)
+    for ri in range(3):
+        want[ri * 4:ri * 4 + 4] = -x[ri * 1:ri * 1 + 4]
+    assert bits_equal(got, want).all()
+
+
+@pytest.mark.parametrize("op", ["SUM", "MEAN", "MIN", "MAX"])
+def test_full_reductions(op):
+    dev = device()
+    o = oracle()
+    for i, sh in enumerate([(4, 1, 3, 2), (7, 3, 2), (1,), (1000, 33), (4097, 5, 3), (8, 8, 8, 8, 8, 8)]):
+        s6 = pad6(sh)
+        x = o.stream(5000 + i).uniform(int(np.prod(s6)), -1.0, 1.0)
+        got, r, _ = run_op(dev, op, [x], [sh])
+        want = o.reduce(op, x, s6)
+        assert got.size == int(np.prod(s6[1:]))
+        assert np.all(got[1:] == 0.0)  # the rest of the (1, d1..d5) result stays zero
+        assert abs(got[0] - want) <= 1e-6 * max(1.0, abs(want)), (op, sh, got[0], want)
+
+
+def test_matmul_exact_path_is_bit_identical():
+    dev = device()
+    o = oracle()
+    for i, (m, k, n) in enumerate([(2, 2, 2), (256, 784, 256), (256, 256, 10), (33, 65, 17), (130, 70, 129)]):
+        s = o.stream(6000 + i)
+        x = s.uniform(m * k, -1.0, 1.0)
+        y = s.uniform(k * n, -1.0, 1.0)
+        got, _, _ = run_op(dev, "MATMUL", [x, y], [(m, k), (k, n)])
+        assert bits_equal(got, o.matmul(x, y, m, k, n)).all(), (m, k, n)
+
+
+def test_matmul_known_answers():
+    """test/compute_cpu.cpp:380-452."""
+    dev = device()
+    A = np.array([1.6354027, -1.3607267, 1.8556793, 1.1689897], np.float32)
+    B = np.array([-0.6105532, 0.10695228, -1.0069681, -0.40955952], np.float32)
+    got, _, _ = run_op(dev, "MATMUL", [A, B], [(2, 2), (2, 2)])
+    np.testing.assert_allclose(got, [0.3717081, 0.7322086, -2.3101263, -0.28030172], rtol=4 * 2**-23)
+    got, _, _ = run_op(dev, "MATMUL", [np.arange(1, 7, dtype=np.float32), np.array([0.5, -1.0], np.float32)],
+                       [(3, 2), (2,)])
+    assert list(got) == [-1.5, -2.5, -3.5]
+
+
+def _normwise_ok(got, x, y, m, k, n, tol=1e-5):
+    x64 = x.reshape(m, k).astype(np.float64)
+    y64 = y.reshape(k, n).astype(np.float64)
+    exact = x64 @ y64
+    bound = np.abs(x64) @ np.abs(y64)
+    err = np.abs(got.reshape(m, n).astype(np.float64) - exact)
+    return float((err / np.maximum(bound, 1e-30)).max()) <= tol
+
+
+@pytest.mark.parametrize("m", [1, 8, 16])
+def test_matmul_skinny(m):
+    dev = device()
+    o = oracle()
+    k, n = 4096, 4096
+    s = o.stream(7000 + m)
+    x = s.normal(m * k, 0.0, k ** -0.5) if (m * k) % 2 == 0 else s.uniform(m * k, -1, 1)
+    y = s.normal(k * n, 0.0, k ** -0.5)
+    got, _, _ = run_op(dev, "MATMUL", [x, y], [(m, k), (k, n)])
+    assert _normwise_ok(got, x, y, m, k, n)
+
+
+def test_matmul_batched_extension():
+    dev = device()
+    o = oracle()
+    b, m, k, n = 4, 33, 40, 28
+    s = o.stream(7100)
+    x = s.uniform(b * m * k, -1, 1)
+    y = s.uniform(b * k * n, -1, 1)
+    tx, ty, tr = dev.tensor((b * m * k,)), dev.tensor((b * k * n,)), dev.tensor((b * m * n,))
+    tx.write(x)
+    ty.write(y)
+    MB.check(dev.L.mag_cuda_matmul_batched_f32(dev.p, tr.data_ptr, tx.data_ptr, ty.data_ptr, b, m, k, n), "bmm")
+    dev.sync()
+    got = _raw(dev, tr.data_ptr, b * m * n)
+    assert bits_equal(got, o.matmul_batched(x, y, b, m, k, n)).all()
+
+
+class _CudaArray:
+    """Minimal __cuda_array_interface__ over a raw device pointer (read-only view)."""
+
+    def __init__(self, ptr, n):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (ptr, False), "version": 3,
+                                         "stream": None}
+
+
+def _raw(dev, ptr, n):
+    import torch
+    return torch.as_tensor(_CudaArray(ptr, n), device=f"cuda:{dev.L.mag_cuda_device_ordinal(dev.p)}").cpu().numpy()
+
+
+@pytest.mark.parametrize("op", ["SUM", "MEAN", "MIN", "MAX"])
+def test_row_reductions(op):
+    dev = device()
+    o = oracle()
+    for i, (rows, cols) in enumerate([(7, 5), (300, 1024), (3, 5000), (2, 65536)]):
+        x = o.stream(8000 + i).uniform(rows * cols, -1, 1)
+        tx, tr = dev.tensor((rows * cols,)), dev.tensor((rows,))
+        tx.write(x)
+        MB.check(dev.L.mag_cuda_reduce_rows_f32(dev.p, MB.OP[op], tr.data_ptr, tx.data_ptr, rows, cols), op)
+        dev.sync()
+        got = _raw(dev, tr.data_ptr, rows)
+        want = o.reduce_rows(op, x, rows, cols)
+        assert np.all(np.abs(got - want) <= 1e-6 * np.maximum(1.0, np.abs(want))), (op, rows, cols)
+
+
+def test_softmax_rows():
+    dev = device()
+    o = oracle()
+    for i, (rows, cols) in enumerate([(5, 10), (64, 1024), (3, 32768), (2, 262144), (3, 1000003)]):
+        x = o.stream(8100 + i).uniform(rows * cols, -6, 6)
+        tx, tr = dev.tensor((rows * cols,)), dev.tensor((rows * cols,))
+        tx.write(x)
+        MB.check(dev.L.mag_cuda_softmax_rows_f32(dev.p, tr.data_ptr, tx.data_ptr, rows, cols), "softmax")
+        dev.sync()
+        got = _raw(dev, tr.data_ptr, rows * cols)
+        want = o.softmax_rows(x, rows, cols)
+        rel = np.abs(got - want) / np.maximum(np.abs(want), 1e-30)
+        assert rel.max() <= 1e-5, (rows, cols, rel.max())
+
+
+def test_broadcast2_small_exact():
+    dev = device()
+    o = oracle()
+    xd, yd = [4, 1, 3, 1, 2, 1], [4, 2, 1, 5, 1, 3]
+    rd = [4, 2, 3, 5, 2, 3]
+    s = o.stream(8200)
+    x = s.uniform(int(np.prod(xd)), -2, 2)
+    y = s.uniform(int(np.prod(yd)), 0.5, 2)
+    tx, ty, tr = dev.tensor((x.size,)), dev.tensor((y.size,)), dev.tensor((int(np.prod(rd)),))
+    tx.write(x)
+    ty.write(y)
+    for op in ["ADD", "SUB", "MUL", "DIV"]:
+        MB.check(dev.L.mag_cuda_broadcast2_f32(dev.p, MB.OP[op], tr.data_ptr, tx.data_ptr, ty.data_ptr,
+                                               MB.i64x6(rd), MB.i64x6(xd), MB.i64x6(yd)), op)
+        dev.sync()
+        got = _raw(dev, tr.data_ptr, int(np.prod(rd)))
+        assert bits_equal(got, o.bcast2(op, x, xd, y, yd, rd)).all(), op
+
+
+def test_lazy_zero_contract():
+    """New storage reads as zero (magnetron/magnetron_cpu.c:2336-2349), partial writes keep the rest zero."""
+    dev = device()
+    t = dev.tensor((1000,))
+    assert np.all(t.read() == 0)
+    t.write(np.ones(10, np.float32), offset_elems=5)
+    got = t.read()
+    assert np.all(got[5:15] == 1) and np.all(got[:5] == 0) and np.all(got[15:] == 0)
+    t.fill_zero()
+    assert np.all(t.read() == 0)
+
+
+def test_deferred_graph_replays_with_new_inputs():
+    """Deferred mode: build the 2-layer MLP DAG once, execute it as a CUDA graph twice."""
+    dev = device()
+    o = oracle()
+    dev.eager = False
+    try:
+        X, W1, B1 = dev.tensor((16, 8)), dev.tensor((8, 12)), dev.tensor((16, 12))
+        h = dev.op("MATMUL", X, W1)
+        h2 = dev.op("ADD", h, B1)
+        h3 = dev.op("SIGMOID", h2)
+        out = dev.op("SOFTMAX", h3)
+    finally:
+        dev.eager = True
+    s = o.stream(9000)
+    w1 = s.uniform(8 * 12, -1, 1)
+    b1 = s.uniform(16 * 12, -1, 1)
+    W1.write(w1)
+    B1.write(b1)
+    for rep in range(2):
+        x = s.uniform(16 * 8, 0, 1)
+        X.write(x)
+        dev.graph_exec(out)
+        got = out.read()
+        a = o.matmul(x, w1, 16, 8, 12)
+        a = o.binary("ADD", a, pad6((16, 12)), b1, pad6((16, 12)))
+        a = o.unary("SIGMOID", a, pad6((16, 12)))
+        a = o.unary("SOFTMAX", a, pad6((16, 12)))
+        assert bits_equal(got, a).all(), rep
+    dev.graph_release(out)
