@@ -60,15 +60,16 @@ struct WMin { __device__ __forceinline__ float operator()(float v) const { retur
 struct WMax { __device__ __forceinline__ float operator()(float v) const { return warp_max(v); } };
 
 // Block-wide combine; every thread gets the result.
+// `identity` fills the lanes beyond the number of warps.
 template <typename T, typename F>
-__device__ __forceinline__ T block_combine(T v, F warp_fn, T* sh) {
+__device__ __forceinline__ T block_combine(T v, F warp_fn, T* sh, T identity) {
     v = warp_fn(v);
     int w = threadIdx.x >> 5, l = threadIdx.x & 31;
     __syncthreads();
     if (l == 0) sh[w] = v;
     __syncthreads();
     int nw = blockDim.x >> 5;
-    T t = l < nw ? sh[l] : sh[0];
+    T t = l < nw ? sh[l] : identity;
     t = warp_fn(t);
     return t;
 }
@@ -120,9 +121,9 @@ __global__ void __launch_bounds__(kThreads) reduce_pass1(const float* __restrict
     }
     __shared__ double shd[32];
     __shared__ float shf[32];
-    double s = block_combine(a.sum, WSum(), shd);
-    float mn = block_combine(a.mn, WMin(), shf);
-    float mx = block_combine(a.mx, WMax(), shf);
+    double s = block_combine(a.sum, WSum(), shd, 0.0);
+    float mn = block_combine(a.mn, WMin(), shf, (float)INFINITY);
+    float mx = block_combine(a.mx, WMax(), shf, -(float)INFINITY);
     if (threadIdx.x == 0) {
         psum[blockIdx.x] = s;
         pmin[blockIdx.x] = mn;
@@ -141,9 +142,9 @@ __global__ void __launch_bounds__(kThreads) reduce_pass2(int op, int nparts, dou
     }
     __shared__ double shd[32];
     __shared__ float shf[32];
-    double s = block_combine(a.sum, WSum(), shd);
-    float mn = block_combine(a.mn, WMin(), shf);
-    float mx = block_combine(a.mx, WMax(), shf);
+    double s = block_combine(a.sum, WSum(), shd, 0.0);
+    float mn = block_combine(a.mn, WMin(), shf, (float)INFINITY);
+    float mx = block_combine(a.mx, WMax(), shf, -(float)INFINITY);
     if (threadIdx.x == 0) {
         if (op == OP_SUM) r[0] = (float)s;
         else if (op == OP_MEAN) r[0] = (float)(s / numel);
@@ -210,8 +211,8 @@ __global__ void __launch_bounds__(kThreads) reduce_rows_block(float* __restrict_
         double s = 0.0;
         float m = OP == OP_MIN ? INFINITY : -INFINITY;
         row_fold<OP>(x + row * cols, cols, threadIdx.x, kThreads, s, m);
-        s = block_combine(s, WSum(), shd);
-        m = OP == OP_MIN ? block_combine(m, WMin(), shf) : block_combine(m, WMax(), shf);
+        s = block_combine(s, WSum(), shd, 0.0);
+        m = OP == OP_MIN ? block_combine(m, WMin(), shf, (float)INFINITY) : block_combine(m, WMax(), shf, -(float)INFINITY);
         if (threadIdx.x == 0) r[row] = row_result<OP>(s, m, cols);
     }
 }
@@ -269,7 +270,7 @@ __global__ void __launch_bounds__(kSoftmaxThreads) softmax_rows_cluster(float* _
             m = fmaxf(m, v);
         }
     }
-    m = block_combine(m, WMax(), sh_max);
+    m = block_combine(m, WMax(), sh_max, -(float)INFINITY);
     if (threadIdx.x == 0) slot_max = m;
     cluster.sync();
     float gm = -INFINITY;
@@ -282,7 +283,7 @@ __global__ void __launch_bounds__(kSoftmaxThreads) softmax_rows_cluster(float* _
         sm[c] = e;
         s += (double)e;
     }
-    s = block_combine(s, WSum(), sh_sum);
+    s = block_combine(s, WSum(), sh_sum, 0.0);
     if (threadIdx.x == 0) slot_sum = s;
     cluster.sync();
     double gs = 0.0;
@@ -314,13 +315,13 @@ __global__ void __launch_bounds__(kSoftmaxThreads) softmax_rows_global(float* __
         float* pr = r + row * cols;
         float m = -INFINITY;
         for (uint32_t c = threadIdx.x; c < cols; c += kSoftmaxThreads) m = fmaxf(m, px[c]);
-        m = block_combine(m, WMax(), sh_max);
+        m = block_combine(m, WMax(), sh_max, -(float)INFINITY);
         double s = 0.0;
         for (uint32_t c = threadIdx.x; c < cols; c += kSoftmaxThreads) {
             float t = fs(px[c], m);
             s += (double)((c < vec_end) ? sse_expf(t) : (float)exp((double)t));
         }
-        s = block_combine(s, WSum(), sh_sum);
+        s = block_combine(s, WSum(), sh_sum, 0.0);
         const float fsum = (float)s;
         for (uint32_t c = threadIdx.x; c < cols; c += kSoftmaxThreads) {
             float t = fs(px[c], m);
