@@ -188,7 +188,7 @@ struct RowParams {
     uint64_t nseg;
     uint32_t cols;
     int y_mode;       // 0: y column == c*ys0, 1: y column fixed (y_d0 == 1), 2: c % y_d0
-    int x_mod;        // x column wraps modulo x_d0
+    int x_mod;        // x column wraps modulo x_d0 (row indices always wrap modulo x's dims)
 };
 
 __device__ __forceinline__ uint32_t mod_by(uint32_t v, const FastDiv& f) { return v - fdiv(v, f) * f.d; }
@@ -212,7 +212,7 @@ __global__ void __launch_bounds__(kThreads) binary_rows(float* __restrict__ r, c
                 uint32_t ik = row - nq * p.dim[k].d;
                 row = nq;
                 ro += (int64_t)ik * p.rs[k];
-                xo += (int64_t)(p.x_mod ? mod_by(ik, p.xdim[k]) : ik) * p.xs[k];
+                xo += (int64_t)mod_by(ik, p.xdim[k]) * p.xs[k];
                 yo += (int64_t)mod_by(ik, p.ydim[k]) * p.ys[k];
             }
         }
@@ -277,7 +277,6 @@ cudaError_t launch_rows(float* r, const float* x, const float* y, const int64_t*
     if (p.nseg >= (1ull << 32)) return cudaErrorInvalidValue;
     p.cols = (uint32_t)dims[0];
     p.x_mod = x_mod && xd[0] != dims[0] ? 1 : 0;
-    if (!x_mod) p.xdim[0] = make_fastdiv((uint32_t)dims[0]);
     p.y_mode = yd[0] == dims[0] ? 0 : (yd[0] == 1 ? 1 : 2);
     bool vec = dims[0] % 4 == 0 && (((uintptr_t)r | (uintptr_t)x) & 15) == 0 && xs[0] == 1 && rs[0] == 1;
     if (x_mod) vec = vec && xd[0] % 4 == 0;

@@ -32,7 +32,8 @@ def lane_mask(shape6):
 
 
 def assert_unary_parity(op, x, got, ref, shape6):
-    """Bit-exact on vector lanes; tails within 2 ulp of glibc; tanh/gelu by tolerance."""
+    """Bit-exact on vector lanes; tails within 2 ulp of glibc; tanh/gelu by tolerance;
+    tanh' within 8 ulp (it squares and inverts libm coshf, magnetron/magnetron_cpu.c:901-909)."""
     if op == "TANH":
         cr = tanh_cr(x)
         assert ulp_diff(got, cr).max() <= 2, op
@@ -42,6 +43,11 @@ def assert_unary_parity(op, x, got, ref, shape6):
         a = 1.0 + 0.044715 * (x64 * x64)
         cr = 0.5 * (x64 * (1.0 + np.tanh(0.7978845608028654 * (x64 * a))))
         assert np.all(np.abs(got - cr) <= 1e-6 * np.maximum(1.0, np.abs(x64))), op
+        return
+    if op == "TANH_DV":
+        # the reference squares and inverts glibc's coshf; the GPU rounds a double cosh once
+        d = ulp_diff(got, ref)
+        assert np.all((d <= 8) | (np.isnan(got) & np.isnan(ref))), (op, int(d.max()))
         return
     lanes = lane_mask(shape6)
     eq = bits_equal(got, ref)
