@@ -57,6 +57,9 @@ MAG_CUDA_EXPORT int mag_cuda_device_ordinal(mag_compute_device_t* dvc);
 MAG_CUDA_EXPORT void* mag_cuda_stream(mag_compute_device_t* dvc);          /* cudaStream_t */
 MAG_CUDA_EXPORT int mag_cuda_synchronize(mag_compute_device_t* dvc);       /* waits, reports async errors */
 MAG_CUDA_EXPORT int mag_cuda_last_error(mag_compute_device_t* dvc);        /* sticky error of the eager path */
+/* MATMUL algorithm: 0 = automatic (default, or MAG_CUDA_MATMUL=exact|tc), 1 = the
+ * bit-exact CUDA-core kernel, 2 = the 3xTF32 tensor-core kernel where the shape allows. */
+MAG_CUDA_EXPORT int mag_cuda_set_matmul_mode(mag_compute_device_t* dvc, int mode);
 /* Bytes currently held by tensor storage of this device. */
 MAG_CUDA_EXPORT size_t mag_cuda_memory_in_use(mag_compute_device_t* dvc);
 

@@ -640,6 +640,13 @@ static void ext_out(mcu_device* d, void* p, size_t bytes) {
 }
 
 int mag_cuda_device_ordinal(mag_compute_device_t* dvc) { return dev_of(dvc)->ordinal; }
+
+int mag_cuda_set_matmul_mode(mag_compute_device_t* dvc, int mode) {
+    if (mode < 0 || mode > 2) return MAG_CUDA_E_INVALID;
+    if (mode == 2 && !mcu_matmul_tc_supported()) return MAG_CUDA_E_UNSUPPORTED;
+    dev_of(dvc)->matmul_mode = mode;
+    return 0;
+}
 void* mag_cuda_stream(mag_compute_device_t* dvc) { return (void*)dev_of(dvc)->stream; }
 size_t mag_cuda_memory_in_use(mag_compute_device_t* dvc) { return dev_of(dvc)->bytes_live; }
 int mag_cuda_last_error(mag_compute_device_t* dvc) { return dev_of(dvc)->sticky_error; }

@@ -1,11 +1,470 @@
-// k_matmul_tc.cu - placeholder until the tcgen05 3xTF32 GEMM lands.
+// k_matmul_tc.cu - f32 matmul on the sm_100a tensor cores with a 3xTF32 split.
+//
+// R[M,N] = X[M,K] Y[K,N], all row-major f32 (the buffer interpretation of
+// mag_blas_matmul_f32, magnetron/magnetron_cpu.c:2151-2185).  A TF32 product
+// keeps 11 significant bits, so each operand is split into two TF32 numbers,
+// x = hi + lo with hi = rna_tf32(x) and lo = rna_tf32(x - hi) (Ootomo & Yokota,
+// "Recovering single precision accuracy from Tensor Cores while surpassing the
+// FP32 theoretical peak performance", 2022), and the product is accumulated as
+// lo*hi + hi*lo + hi*hi in f32 in tensor memory; the dropped lo*lo term is
+// about 2^-22 relative, so results stay within f32 rounding of the exact
+// product (the matmul tolerance is 1e-5 relative, norm-wise).
+//
+// Kernels
+//   split_rows     X -> Xhi, Xlo     [M][Kp]    (Kp = K rounded up to 32, zero padded)
+//   split_cols_t   Y -> Yhi^T, Ylo^T [N][Kp]    (transposed so both operands are K-major)
+//   gemm_3xtf32    persistent, warp-specialised:
+//     warp 0      TMA producer: 128B-swizzled 128x32 (X) and BNx32 (Y) tiles, hi and lo,
+//                 into a STAGES-deep shared-memory ring (mbarrier complete_tx)
+//     warp 1      TMEM allocator; lane 0 issues tcgen05.mma kind::tf32 (M=128, N=BN, K=8),
+//                 three per k-step, and tcgen05.commit to free ring slots / publish tiles
+//     warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns -> registers -> global,
+//                 from one of two TMEM accumulators so it overlaps the next tile's MMAs
+// Every mbarrier wait is bounded: on expiry the kernel records a status code,
+// all roles leave their loops, and TMEM is released before the CTA exits.
+// No load uses cluster multicast; the same kernel serves multi-GPU runs.
+#include <cuda.h>
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
 #include <cstdint>
 #include "mcu_kernels.h"
 
-extern "C" int mcu_matmul_tc_supported(void) { return 0; }
-extern "C" size_t mcu_matmul_tc_scratch_bytes(int64_t, int64_t, int64_t) { return 0; }
-extern "C" int mcu_launch_matmul_tc(float*, const float*, const float*, int64_t, int64_t, int64_t, void*, int*,
-                                    cudaStream_t) {
-    return (int)cudaErrorNotSupported;
+namespace {
+
+constexpr int BM = 128;          // UMMA M (one CTA, TMEM lanes 0..127)
+constexpr int BK = 32;           // f32 per 128-byte swizzle row
+constexpr int kEpiWarps = 4;
+constexpr int kThreads = 32 * (2 + kEpiWarps);
+constexpr uint32_t kWaitLimit = 1u << 22;
+
+int sm_count() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0) n = 148;
+    }
+    return n;
+}
+
+// ------------------------------------------------------------ PTX wrappers
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+struct Abort {
+    volatile int* flag;  // shared: set once any role gives up
+    int* status;         // global status word
+};
+
+// Bounded wait on the phase of `parity`.  False when this or another role gave up.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const Abort& ab, int code) {
+    for (uint32_t i = 0;; ++i) {
+        if (mbar_test(bar, parity)) return true;
+        if (*ab.flag) return false;
+        if (i >= kWaitLimit) {
+            *ab.flag = 1;
+            atomicCAS(ab.status, 0, code);
+            return false;
+        }
+        if (i > 32) __nanosleep(64);
+    }
+}
+
+__device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* bar, void* dst, int c0, int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::
+            "r"(smem_u32(dst)),
+        "l"((uint64_t)map), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// D(tmem) (+)= A(smem) * B(smem)^T, kind::tf32, issued by one thread.
+__device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+// Arrives on `bar` once every tcgen05.mma issued so far by this thread has completed.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, 128B swizzle, 8-row atoms 1024 B apart.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)1 << 16;             // leading byte offset (unused for swizzled K-major)
+    d |= (uint64_t)(1024 >> 4) << 32;   // stride byte offset between 8-row atoms
+    d |= (uint64_t)1 << 46;             // descriptor version for tcgen05
+    d |= (uint64_t)2 << 61;             // SWIZZLE_128B
+    return d;
+}
+
+// Instruction descriptor, kind::tf32: D f32, A/B tf32, both K-major, M=128, N=BN.
+__host__ __device__ constexpr uint32_t idesc_tf32(int n) {
+    return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+          "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+          "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// ------------------------------------------------------------ tile order
+// Groups of kGroupM row-blocks sweep all column blocks, so a wave of CTAs
+// shares few X panels and the Y panels stay hot in L2.
+constexpr int kGroupM = 16;
+
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb, int& nb) {
+    const int per_group = kGroupM * num_n;
+    const int g = t / per_group;
+    const int first = g * kGroupM;
+    const int gsz = min(num_m - first, kGroupM);
+    const int local = t - g * per_group;
+    mb = first + local % gsz;
+    nb = local / gsz;
+}
+
+// ------------------------------------------------------------ the GEMM
+template <int BN, int STAGES>
+struct Cfg {
+    static constexpr int A_BYTES = BM * BK * 4;
+    static constexpr int B_BYTES = BN * BK * 4;
+    static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
+    static constexpr int TMEM_COLS = 2 * BN;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 512;
+    static_assert(TMEM_COLS <= 512, "two accumulators must fit TMEM");
+};
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_3xtf32(const __grid_constant__ CUtensorMap map_xhi, const __grid_constant__ CUtensorMap map_xlo,
+                const __grid_constant__ CUtensorMap map_yhi, const __grid_constant__ CUtensorMap map_ylo,
+                float* __restrict__ r, int M, int N, int Kp, int64_t ldr, int* status) {
+    using C = Cfg<BN, STAGES>;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t* ring = smem;
+    uint64_t* full = (uint64_t*)(smem + STAGES * C::STAGE_BYTES);
+    uint64_t* empty = full + STAGES;
+    uint64_t* acc_full = empty + STAGES;
+    uint64_t* acc_empty = acc_full + 2;
+    uint64_t* drain = acc_empty + 2;
+    uint32_t* tmem_slot = (uint32_t*)(drain + 1);
+    volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int num_m = (M + BM - 1) / BM;
+    const int num_n = (N + BN - 1) / BN;
+    const int tiles = num_m * num_n;
+    const int nk = Kp / BK;
+    Abort ab{abort_flag, status};
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&acc_full[a], 1);
+            mbar_init(&acc_empty[a], 32 * kEpiWarps);
+        }
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"((uint32_t)C::TMEM_COLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {  // ---- TMA producer
+            asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&map_xhi) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&map_xlo) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&map_yhi) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&map_ylo) : "memory");
+            uint32_t it = 0;
+            for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+                int mb, nb;
+                tile_coords(t, num_m, num_n, mb, nb);
+                for (int kb = 0; kb < nk; ++kb, ++it) {
+                    const uint32_t s = it % STAGES, round = it / STAGES;
+                    if (!mbar_wait(&empty[s], (round & 1) ^ 1, ab, 1)) goto done;
+                    uint8_t* st = ring + s * C::STAGE_BYTES;
+                    mbar_expect_tx(&full[s], C::STAGE_BYTES);
+                    tma_load_2d(&map_xhi, &full[s], st, kb * BK, mb * BM);
+                    tma_load_2d(&map_xlo, &full[s], st + C::A_BYTES, kb * BK, mb * BM);
+                    tma_load_2d(&map_yhi, &full[s], st + 2 * C::A_BYTES, kb * BK, nb * BN);
+                    tma_load_2d(&map_ylo, &full[s], st + 2 * C::A_BYTES + C::B_BYTES, kb * BK, nb * BN);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {  // ---- MMA issuer
+            constexpr uint32_t idesc = idesc_tf32(BN);
+            uint32_t it = 0, tc = 0;
+            for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++tc) {
+                const uint32_t a = tc & 1, around = tc >> 1;
+                if (!mbar_wait(&acc_empty[a], (around & 1) ^ 1, ab, 2)) goto done;
+                tc_fence_after();
+                const uint32_t d = tmem_base + a * BN;
+                for (int kb = 0; kb < nk; ++kb, ++it) {
+                    const uint32_t s = it % STAGES, round = it / STAGES;
+                    if (!mbar_wait(&full[s], round & 1, ab, 3)) goto done;
+                    tc_fence_after();
+                    const uint32_t base = smem_u32(ring + s * C::STAGE_BYTES);
+#pragma unroll
+                    for (int kk = 0; kk < BK / 8; ++kk) {
+                        const uint64_t xhi = sw128_desc(base + kk * 32);
+                        const uint64_t xlo = sw128_desc(base + C::A_BYTES + kk * 32);
+                        const uint64_t yhi = sw128_desc(base + 2 * C::A_BYTES + kk * 32);
+                        const uint64_t ylo = sw128_desc(base + 2 * C::A_BYTES + C::B_BYTES + kk * 32);
+                        umma_tf32(d, xlo, yhi, idesc, (kb | kk) != 0);
+                        umma_tf32(d, xhi, ylo, idesc, 1);
+                        umma_tf32(d, xhi, yhi, idesc, 1);
+                    }
+                    umma_commit(&empty[s]);
+                }
+                umma_commit(&acc_full[a]);
+            }
+        }
+    } else {  // ---- epilogue warps: TMEM lanes 32*(warp%4) .. +31
+        const int q = warp & 3;
+        uint32_t tc = 0;
+        for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++tc) {
+            int mb, nb;
+            tile_coords(t, num_m, num_n, mb, nb);
+            const uint32_t a = tc & 1, around = tc >> 1;
+            if (!mbar_wait(&acc_full[a], around & 1, ab, 4)) break;
+            tc_fence_after();
+            const int row = mb * BM + q * 32 + lane;
+            const int col0 = nb * BN;
+            float* out = r + (int64_t)row * ldr + col0;
+            const bool row_ok = row < M;
+            const bool vec = ((ldr & 3) == 0) && ((((uintptr_t)r) & 15) == 0);
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t v[32];
+                tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + a * BN + c * 32, v);
+                const int cb = col0 + c * 32;
+                if (row_ok) {
+                    if (vec && cb + 32 <= N) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 4)
+                            *(float4*)(out + c * 32 + j) = make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]),
+                                                                       __uint_as_float(v[j + 2]),
+                                                                       __uint_as_float(v[j + 3]));
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (cb + j < N) out[c * 32 + j] = __uint_as_float(v[j]);
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&acc_empty[a]);
+        }
+    }
+done:
+    __syncthreads();
+    if (warp == 1) {
+        if (*abort_flag && lane == 0) {
+            // let MMAs still in flight finish before the accumulator is released
+            umma_commit(drain);
+            for (uint32_t i = 0; i < kWaitLimit && !mbar_test(drain, 0); ++i) __nanosleep(64);
+        }
+        __syncwarp();
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                     "r"((uint32_t)C::TMEM_COLS));
+    }
+}
+
+// ------------------------------------------------------------ split kernels
+__device__ __forceinline__ float rna_tf32(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r);
+}
+
+// X[M][K] -> hi/lo [M][Kp]; one thread per 4 consecutive k.
+__global__ void __launch_bounds__(256) split_rows(const float* __restrict__ x, float* __restrict__ hi,
+                                                  float* __restrict__ lo, int64_t M, int64_t K, int64_t Kp) {
+    const int64_t q = Kp / 4;
+    const int64_t n = M * q;
+    const bool vec = (K % 4 == 0) && ((((uintptr_t)x) & 15) == 0);
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t m = i / q, k = (i - m * q) * 4;
+        float v[4];
+        if (vec && k + 4 <= K) {
+            float4 t = __ldcs((const float4*)(x + m * K + k));
+            v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+        } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) v[j] = (k + j < K) ? x[m * K + k + j] : 0.0f;
+        }
+        float4 h, l;
+        h.x = rna_tf32(v[0]); l.x = rna_tf32(v[0] - h.x);
+        h.y = rna_tf32(v[1]); l.y = rna_tf32(v[1] - h.y);
+        h.z = rna_tf32(v[2]); l.z = rna_tf32(v[2] - h.z);
+        h.w = rna_tf32(v[3]); l.w = rna_tf32(v[3] - h.w);
+        *(float4*)(hi + m * Kp + k) = h;
+        *(float4*)(lo + m * Kp + k) = l;
+    }
+}
+
+// Y[K][N] -> hi/lo transposed [N][Kp] through a 32x32 shared tile.
+__global__ void __launch_bounds__(256) split_cols_t(const float* __restrict__ y, float* __restrict__ hi,
+                                                    float* __restrict__ lo, int64_t K, int64_t N, int64_t Kp) {
+    __shared__ float tile[32][33];
+    const int64_t k0 = (int64_t)blockIdx.y * 32, n0 = (int64_t)blockIdx.x * 32;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+    for (int j = ty; j < 32; j += 8) {
+        const int64_t k = k0 + j, n = n0 + tx;
+        tile[j][tx] = (k < K && n < N) ? y[k * N + n] : 0.0f;
+    }
+    __syncthreads();
+    for (int j = ty; j < 32; j += 8) {
+        const int64_t n = n0 + j, k = k0 + tx;
+        if (n < N && k < Kp) {
+            const float v = tile[tx][j];
+            const float h = rna_tf32(v);
+            hi[n * Kp + k] = h;
+            lo[n * Kp + k] = rna_tf32(v - h);
+        }
+    }
+}
+
+// ------------------------------------------------------------ host side
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        cudaDriverEntryPointQueryResult q;
+        void* p = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
+    }
+    return fn;
+}
+
+// 2-D map over a [rows][Kp] f32 array, box = box_rows x 32, 128-byte swizzle.
+bool make_map(CUtensorMap* m, const float* base, int64_t rows, int64_t kp, int box_rows) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)kp, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(kp * 4)};
+    cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void*)base, dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+int64_t round_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
+
+struct Layout {
+    int64_t kp;
+    size_t xhi, xlo, yhi, ylo, total;
+};
+
+Layout layout(int64_t M, int64_t K, int64_t N) {
+    Layout l;
+    l.kp = round_up(K < 1 ? 1 : K, BK);
+    size_t xs = (size_t)round_up(M * l.kp * 4, 1024), ys = (size_t)round_up(N * l.kp * 4, 1024);
+    l.xhi = 0;
+    l.xlo = xs;
+    l.yhi = 2 * xs;
+    l.ylo = 2 * xs + ys;
+    l.total = 2 * xs + 2 * ys;
+    return l;
+}
+
+constexpr int kBN = 256;
+constexpr int kStages = 2;
+
+}  // namespace
+
+extern "C" int mcu_matmul_tc_supported(void) {
+    if (getenv("MAG_CUDA_NO_TC")) return 0;
+    return encode_fn() != nullptr;
+}
+
+extern "C" size_t mcu_matmul_tc_scratch_bytes(int64_t M, int64_t K, int64_t N) { return layout(M, K, N).total; }
+
+extern "C" int mcu_launch_matmul_tc(float* r, const float* x, const float* y, int64_t M, int64_t K, int64_t N,
+                                    void* scratch, int* status, cudaStream_t st) {
+    if (M <= 0 || N <= 0) return (int)cudaSuccess;
+    if (M >= (1ll << 31) || N >= (1ll << 31) || K >= (1ll << 21) || !scratch) return (int)cudaErrorInvalidValue;
+    const Layout l = layout(M, K, N);
+    char* base = (char*)scratch;
+    float* xhi = (float*)(base + l.xhi);
+    float* xlo = (float*)(base + l.xlo);
+    float* yhi = (float*)(base + l.yhi);
+    float* ylo = (float*)(base + l.ylo);
+    {
+        int64_t n = M * (l.kp / 4);
+        int64_t g = (n + 255) / 256;
+        if (g > 8 * sm_count()) g = 8 * sm_count();
+        split_rows<<<(unsigned)g, 256, 0, st>>>(x, xhi, xlo, M, K, l.kp);
+        dim3 grid((unsigned)((N + 31) / 32), (unsigned)(l.kp / 32));
+        split_cols_t<<<grid, 256, 0, st>>>(y, yhi, ylo, K, N, l.kp);
+    }
+    CUtensorMap mxh, mxl, myh, myl;
+    if (!make_map(&mxh, xhi, M, l.kp, BM) || !make_map(&mxl, xlo, M, l.kp, BM) ||
+        !make_map(&myh, yhi, N, l.kp, kBN) || !make_map(&myl, ylo, N, l.kp, kBN))
+        return (int)cudaErrorInvalidValue;
+    using C = Cfg<kBN, kStages>;
+    auto kern = gemm_3xtf32<kBN, kStages>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (e != cudaSuccess) return (int)e;
+    const int64_t tiles = ((M + BM - 1) / BM) * ((N + kBN - 1) / kBN);
+    const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
+    kern<<<grid, kThreads, C::SMEM, st>>>(mxh, mxl, myh, myl, r, (int)M, (int)N, (int)l.kp, (int64_t)N, status);
+    return (int)cudaGetLastError();
 }

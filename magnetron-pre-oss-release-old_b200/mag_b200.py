@@ -104,6 +104,7 @@ def load_library(path: str = LIB_PATH):
         "mag_init_device_cuda": ([vp], vp),
         "mag_destroy_device_cuda": ([vp], None),
         "mag_cuda_device_ordinal": ([vp], C.c_int),
+        "mag_cuda_set_matmul_mode": ([vp, C.c_int], C.c_int),
         "mag_cuda_stream": ([vp], vp),
         "mag_cuda_synchronize": ([vp], C.c_int),
         "mag_cuda_last_error": ([vp], C.c_int),
