@@ -287,3 +287,38 @@ def test_deferred_graph_replays_with_new_inputs():
         a = o.unary("SOFTMAX", a, pad6((16, 12)))
         assert bits_equal(got, a).all(), rep
     dev.graph_release(out)
+
+
+@pytest.mark.parametrize("mkn", [(128, 32, 256), (300, 100, 700), (1000, 777, 300), (2048, 1024, 4096),
+                                 (256, 4096, 1000), (4096, 4096, 4096)])
+def test_matmul_tensor_core_normwise(mkn):
+    """3xTF32 tcgen05 path through the vtable; within 1e-5 of the exact product, norm-wise."""
+    m, k, n = mkn
+    dev = device()
+    o = oracle()
+    s = o.stream(7300 + m + n)
+    x = s.uniform(m * k, -1.0, 1.0)
+    y = s.uniform(k * n, -1.0, 1.0)
+    MB.check(dev.L.mag_cuda_set_matmul_mode(dev.p, 2), "tc mode")
+    try:
+        got, _, _ = run_op(dev, "MATMUL", [x, y], [(m, k), (k, n)])
+    finally:
+        dev.L.mag_cuda_set_matmul_mode(dev.p, 0)
+    assert dev.L.mag_cuda_synchronize(dev.p) == 0
+    assert _normwise_ok(got, x, y, m, k, n)
+
+
+def test_matmul_tensor_core_large_k_sampled():
+    """K = 16384 through the automatic path: norm-wise against the exact product,
+    and sampled rows against the oracle's sequential f32 product relative to max|C|."""
+    dev = device()
+    o = oracle()
+    m, k, n = 256, 16384, 512
+    s = o.stream(7400)
+    x = s.normal(m * k, 0.0, k ** -0.5)
+    y = s.normal(k * n, 0.0, k ** -0.5)
+    got, _, _ = run_op(dev, "MATMUL", [x, y], [(m, k), (k, n)])
+    assert _normwise_ok(got, x, y, m, k, n)
+    rows = o.matmul_rows(x, y, 17, 3, k, n)
+    ref_err = np.abs(rows - got.reshape(m, n)[17:20].reshape(-1))
+    assert float(ref_err.max()) <= 2e-4 * float(np.abs(rows).max())
