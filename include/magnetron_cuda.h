@@ -41,6 +41,7 @@ extern "C" {
 #define MAG_CUDA_E_INVALID 10001     /* bad argument (shape, size, null) */
 #define MAG_CUDA_E_DEVICE_WAIT 10002 /* a kernel's bounded wait expired (device status word) */
 #define MAG_CUDA_E_UNSUPPORTED 10003 /* op not available (e.g. the reference panics with NYI) */
+#define MAG_CUDA_E_SCRATCH_LIMIT 10004 /* the call needs more than the fixed scratch array holds */
 
 /* ---- drop-in device interface (magnetron/magnetron_cuda.cuh:14-15) ---- */
 
@@ -104,6 +105,22 @@ MAG_CUDA_EXPORT int mag_cuda_softmax_rows_f32(mag_compute_device_t* dvc, float* 
 /* R[b] = X[b] Y[b] for b < batch, each M x K times K x N. */
 MAG_CUDA_EXPORT int mag_cuda_matmul_batched_f32(mag_compute_device_t* dvc, float* r, const float* x,
                                                 const float* y, int64_t batch, int64_t M, int64_t K, int64_t N);
+
+/* ---- allocation-free entry point (no counterpart in the reference) ----
+ * R[M,N] = X[M,K] Y[K,N] for 1 <= M <= 16, the same split-K kernels as
+ * mag_cuda_matmul_f32 uses for such shapes, but it never allocates: for callers
+ * that cannot call cudaMalloc when they need the product, such as code running
+ * inside a stream capture or a host path that must stay off the allocator.  Its
+ * partial sums go to one fixed 16 MiB array in this library's device image,
+ * which every GPU that loads the library keeps until the process exits.  Calls
+ * needing more (slices x M x N x 4 bytes; M=8, K=N=4096 needs 8 MiB) return
+ * MAG_CUDA_E_SCRATCH_LIMIT.  The first call on a device looks up the array's
+ * device address, so make it before any stream capture.  All calls on a device
+ * share the array: calls whose kernels overlap on the GPU race. */
+MAG_CUDA_EXPORT int mag_cuda_matmul_skinny_f32_noalloc(mag_compute_device_t* dvc, float* r, const float* x,
+                                                       const float* y, int64_t M, int64_t K, int64_t N);
+/* Bytes of the fixed scratch array above. */
+MAG_CUDA_EXPORT size_t mag_cuda_matmul_skinny_noalloc_limit(void);
 
 /* ---- per-op device timing (the core's profiler times only the enqueue) ---- */
 MAG_CUDA_EXPORT int mag_cuda_profile_start(mag_compute_device_t* dvc);

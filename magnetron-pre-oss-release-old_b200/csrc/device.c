@@ -730,6 +730,37 @@ int mag_cuda_matmul_f32(mag_compute_device_t* dvc, float* r, const float* x, con
     return rc;
 }
 
+size_t mag_cuda_matmul_skinny_noalloc_limit(void) { return mcu_skinny_noalloc_limit(); }
+
+int mag_cuda_matmul_skinny_f32_noalloc(mag_compute_device_t* dvc, float* r, const float* x, const float* y,
+                                       int64_t M, int64_t K, int64_t N) {
+    if (!dvc || !r || !x || !y || M < 1 || M > 16 || K < 0 || N < 1) return MAG_CUDA_E_INVALID;
+    mcu_device* d = dev_of(dvc);
+    size_t need = mcu_matmul_skinny_scratch_bytes(M, K, N);
+    if (need > mcu_skinny_noalloc_limit()) {
+        fprintf(stderr,
+                "[magnetron-cuda] mag_cuda_matmul_skinny_f32_noalloc: M=%lld K=%lld N=%lld needs %zu bytes of "
+                "scratch, above the fixed %zu-byte array; use mag_cuda_matmul_f32\n",
+                (long long)M, (long long)K, (long long)N, need, mcu_skinny_noalloc_limit());
+        return MAG_CUDA_E_SCRATCH_LIMIT;
+    }
+    int prev = -1;
+    cudaError_t e = cudaGetDevice(&prev);
+    if (e != cudaSuccess) return (int)e;
+    if (prev != d->ordinal && (e = cudaSetDevice(d->ordinal)) != cudaSuccess) return (int)e;
+    void* scratch = NULL;
+    int rc = mcu_skinny_noalloc_scratch(&scratch);
+    if (!rc) {
+        ext_in(d, x);
+        ext_in(d, y);
+        ext_out(d, r, (size_t)(M * N * 4));
+        rc = mcu_launch_matmul_skinny(r, x, y, M, K, N, N, scratch, d->stream);
+        if (!rc) mcu_count_launches(2);
+    }
+    if (prev != d->ordinal) cudaSetDevice(prev);
+    return rc;
+}
+
 int mag_cuda_broadcast2_f32(mag_compute_device_t* dvc, int op, float* r, const float* x, const float* y,
                             const int64_t* rd, const int64_t* xd, const int64_t* yd) {
     if (op < MAG_ABI_OP_ADD || op > MAG_ABI_OP_DIV) return MAG_CUDA_E_INVALID;

@@ -213,3 +213,51 @@ extern "C" int mcu_launch_matmul_skinny(float* r, const float* x, const float* y
     matmul_skinny_sum<<<(unsigned)g, kThreads, 0, st>>>(r, (const float*)scratch, MN, (int)slices, N, r_ld);
     return (int)cudaGetLastError();
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of the skinny product.
+//
+// Some callers cannot allocate device memory at the moment they need a
+// product: code running while a CUDA stream is being captured into a graph
+// (an allocation there either fails or becomes part of the graph), hosts that
+// must not touch the allocator on a latency-critical or real-time path, and
+// hosts whose device memory is carved up by a framework that owns every
+// allocation.  For them the split-K partial sums live in one fixed array that
+// is part of this library's device image: it is created when the library's
+// device code is loaded on a GPU and stays there until the process exits.
+//
+// The array holds kNoAllocScratchBytes (16 MiB).  It is shared by every call
+// on a device, so two calls whose kernels overlap on the GPU (different
+// streams, or different host threads) race on it.  Nothing in it has to start
+// at zero: every partial is written before it is read.
+namespace {
+constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;
+constexpr int kMaxDevices = 64;
+}  // namespace
+
+static __device__ __align__(256) float g_skinny_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
+
+namespace {
+void* g_noalloc_addr[kMaxDevices];
+}  // namespace
+
+extern "C" size_t mcu_skinny_noalloc_limit(void) { return kNoAllocScratchBytes; }
+
+// Device address of the array on the current device.  The first call on a
+// device looks it up (and may make the driver load this library's device
+// code there); later calls return the cached address.  Host code never uses
+// the array's name as a pointer: on the host it names a stand-in object.
+extern "C" int mcu_skinny_noalloc_scratch(void** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return (int)e;
+    if (dev < 0 || dev >= kMaxDevices) return (int)cudaErrorInvalidDevice;
+    if (!g_noalloc_addr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_skinny_noalloc_scratch);
+        if (e != cudaSuccess) return (int)e;
+        g_noalloc_addr[dev] = p;
+    }
+    *out = g_noalloc_addr[dev];
+    return (int)cudaSuccess;
+}

@@ -40,6 +40,10 @@ size_t mcu_matmul_skinny_scratch_bytes(int64_t M, int64_t K, int64_t N);
 int mcu_launch_matmul_skinny(float* r, const float* x, const float* y, int64_t M, int64_t K, int64_t N,
                              int64_t r_ld, void* scratch, cudaStream_t st);
 
+/* Allocation-free skinny product: scratch is a fixed device array of this library. */
+size_t mcu_skinny_noalloc_limit(void);
+int mcu_skinny_noalloc_scratch(void** out);
+
 /* k_matmul_tc.cu: 3xTF32 tcgen05 GEMM, R[M,N] = X[M,K] Y[K,N] (row-major).
  * scratch needs mcu_matmul_tc_scratch_bytes(M, K, N) bytes. */
 size_t mcu_matmul_tc_scratch_bytes(int64_t M, int64_t K, int64_t N);

@@ -45,7 +45,7 @@ REDUCE = {"MEAN", "MIN", "MAX", "SUM"}
 INPLACE_OK = UNARY | SCALAR | BINARY | {"MATMUL"}
 TFLAG_OWNER, TFLAG_VIEW = 1, 2
 
-E_INVALID, E_DEVICE_WAIT, E_UNSUPPORTED = 10001, 10002, 10003
+E_INVALID, E_DEVICE_WAIT, E_UNSUPPORTED, E_SCRATCH_LIMIT = 10001, 10002, 10003, 10004
 
 
 # ---------------------------------------------------------------- ABI structs
@@ -125,6 +125,8 @@ def load_library(path: str = LIB_PATH):
         "mag_cuda_profile_collect": ([vp], C.c_int),
         "mag_cuda_profile_stats": ([vp, C.c_int, C.POINTER(C.c_uint64), C.POINTER(C.c_double)], C.c_int),
         "mag_cuda_kernel_launches": ([], C.c_uint64),
+        "mag_cuda_matmul_skinny_f32_noalloc": ([vp, vp, vp, vp, i64, i64, i64], C.c_int),
+        "mag_cuda_matmul_skinny_noalloc_limit": ([], C.c_size_t),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)

@@ -1,0 +1,76 @@
+"""The allocation-free skinny matmul entry point.
+
+mag_cuda_matmul_skinny_f32_noalloc exists for callers that cannot allocate
+device memory when they need the product (for example, code running while a
+stream is being captured into a CUDA graph, or a latency-critical host path
+that must stay off the allocator): its split-K partial sums live in a fixed
+array inside the library's device image instead of a buffer from cudaMalloc.
+
+This file sorts last so that a run stopping at the first failure has already
+run every other test; it also passes on its own in a fresh process.
+"""
+import numpy as np
+import pytest
+
+import mag_b200 as MB
+from harness import oracle
+from gpu_util import device
+
+pytestmark = pytest.mark.gpu
+
+
+def _raw(dev, ptr, n):
+    import torch
+
+    class _A:
+        def __init__(self):
+            self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (ptr, False),
+                                             "version": 3, "stream": None}
+
+    return torch.as_tensor(_A(), device=f"cuda:{dev.L.mag_cuda_device_ordinal(dev.p)}").cpu().numpy()
+
+
+def _normwise_ok(got, x, y, m, k, n, tol=1e-5):
+    x64 = x.reshape(m, k).astype(np.float64)
+    y64 = y.reshape(k, n).astype(np.float64)
+    err = np.abs(got.reshape(m, n).astype(np.float64) - x64 @ y64)
+    return float((err / np.maximum(np.abs(x64) @ np.abs(y64), 1e-30)).max()) <= tol
+
+
+@pytest.mark.parametrize("m", [1, 8])
+def test_noalloc_matches_allocating_entry_point_twice(m):
+    dev = device()
+    L = dev.L
+    k = n = 4096
+    assert L.mag_cuda_matmul_skinny_noalloc_limit() == 16 << 20
+    s = oracle().stream(0x5EED0A00 + m)
+    x = s.normal(m * k, 0.0, k ** -0.5) if (m * k) % 2 == 0 else s.uniform(m * k, -1, 1)
+    y = s.normal(k * n, 0.0, k ** -0.5)
+    tx, ty = dev.tensor((m * k,)), dev.tensor((k * n,))
+    tx.write(x)
+    ty.write(y)
+    ref_t, out_t = dev.tensor((m * n,)), dev.tensor((m * n,))
+    MB.check(L.mag_cuda_matmul_f32(dev.p, ref_t.data_ptr, tx.data_ptr, ty.data_ptr, m, k, n), "allocating")
+    dev.sync()
+    ref = _raw(dev, ref_t.data_ptr, m * n)
+    assert _normwise_ok(ref, x, y, m, k, n)
+    for _ in range(2):  # the shared array keeps the previous call's partials; results must not depend on them
+        MB.check(L.mag_cuda_matmul_skinny_f32_noalloc(dev.p, out_t.data_ptr, tx.data_ptr, ty.data_ptr, m, k, n),
+                 "noalloc")
+        assert L.mag_cuda_synchronize(dev.p) == 0
+        got = _raw(dev, out_t.data_ptr, m * n)
+        assert _normwise_ok(got, x, y, m, k, n)
+        assert np.max(np.abs(got - ref)) <= 1e-5 * np.max(np.abs(ref))
+    for t in (tx, ty, ref_t, out_t):
+        t.free()
+
+
+def test_noalloc_rejects_products_above_the_array():
+    dev = device()
+    L = dev.L
+    m, k, n = 16, 4096, 8192  # needs 37 slices x 16 x 8192 x 4 B = 19.4 MB > 16 MiB
+    tx, ty, tr = dev.tensor((m * k,)), dev.tensor((k * n,)), dev.tensor((m * n,))
+    rc = L.mag_cuda_matmul_skinny_f32_noalloc(dev.p, tr.data_ptr, tx.data_ptr, ty.data_ptr, m, k, n)
+    assert rc == MB.E_SCRATCH_LIMIT
+    assert L.mag_cuda_matmul_skinny_f32_noalloc(dev.p, tr.data_ptr, tx.data_ptr, ty.data_ptr, 17, k, n) == MB.E_INVALID
+    assert L.mag_cuda_synchronize(dev.p) == 0
