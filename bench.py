@@ -415,6 +415,53 @@ def sweep(dev, MB, torch, local):
     return out
 
 
+def run_case(args):
+    """One kernel family, a few launches, for profilers: `--case gemm|add|sigmoid|sum|softmax`."""
+    import torch
+    import mag_b200 as MB
+    dev = MB.Device()
+    n = args.size
+    if args.case == "gemm":
+        MB.check(dev.L.mag_cuda_set_matmul_mode(dev.p, 2), "tc")
+        x, y, r = dev.tensor((n * n,)), dev.tensor((n * n,)), dev.tensor((n * n,))
+        v = torch.randn(n * n, generator=torch.Generator().manual_seed(3)).numpy()
+        x.write(v)
+        y.write(v)
+        fn = lambda: dev.L.mag_cuda_matmul_f32(dev.p, r.data_ptr, x.data_ptr, y.data_ptr, n, n, n)
+        work, unit = 2.0 * n ** 3 / 1e12, "TFLOP/s"
+    else:
+        x, y, r = dev.tensor((n,)), dev.tensor((n,)), dev.tensor((n,))
+        v = torch.randn(n, generator=torch.Generator().manual_seed(3)).numpy()
+        x.write(v)
+        y.write(v)
+        dims, st = MB.i64x6([n, 1, 1, 1, 1, 1]), MB.i64x6(MB.strides6([n, 1, 1, 1, 1, 1]))
+        if args.case == "add":
+            fn = lambda: dev.L.mag_cuda_binary_f32(dev.p, MB.OP["ADD"], r.data_ptr, x.data_ptr, y.data_ptr, dims, st, st, dims, st)
+            work = 12.0 * n / 1e9
+        elif args.case == "sigmoid":
+            fn = lambda: dev.L.mag_cuda_unary_f32(dev.p, MB.OP["SIGMOID"], r.data_ptr, x.data_ptr, n // 1024, 1024, 1024, 1024, 0.0)
+            work = 8.0 * n / 1e9
+        elif args.case == "sum":
+            fn = lambda: dev.L.mag_cuda_reduce_f32(dev.p, MB.OP["SUM"], r.data_ptr, x.data_ptr, dims, st)
+            work = 4.0 * n / 1e9
+        else:
+            fn = lambda: dev.L.mag_cuda_softmax_rows_f32(dev.p, r.data_ptr, x.data_ptr, n // 32768, 32768)
+            work = 8.0 * n / 1e9
+        unit = "GB/s"
+    stream = torch.cuda.ExternalStream(dev.stream)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    MB.check(fn(), args.case)
+    dev.sync()
+    e0.record(stream)
+    for _ in range(args.steps):
+        MB.check(fn(), args.case)
+    e1.record(stream)
+    dev.sync()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    print(json.dumps({"case": args.case, "size": n, "ms": ms, "rate": work / (ms / 1e3), "unit": unit}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -423,7 +470,14 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--case", default=None, choices=["gemm", "add", "sigmoid", "sum", "softmax"],
+                    help="run one kernel family for a profiler instead of the benchmark")
+    ap.add_argument("--size", type=int, default=None)
     args = ap.parse_args()
+    if args.case:
+        args.size = args.size or (8192 if args.case == "gemm" else 1 << 28)
+        run_case(args)
+        return
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
