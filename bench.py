@@ -517,6 +517,181 @@ def run_case(args):
     print(json.dumps({"case": args.case, "size": n, "ms": ms, "rate": work / (ms / 1e3), "unit": unit}))
 
 
+def run_sweep_full(args):
+    """Every other BASELINE configuration on one GPU: elementwise/broadcast/unary (config 2),
+    row reductions and softmax (config 3), the matmul sweep (config 4), each with its roofline
+    fraction, and single-thread reference CPU rates for the sizes the CPU finishes quickly."""
+    import torch
+    import mag_b200 as MB
+    dev = MB.Device()
+    pk, pk_src = peaks()
+    hbm = pk["hbm_gbs"]
+    tf = pk.get("bf16_tflops_sustained", pk["bf16_tflops"]) / 2.0 / 3.0
+    stream = torch.cuda.ExternalStream(dev.stream)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    rows_out = []
+    gen = torch.Generator().manual_seed(11)
+    chunk = torch.randn(1 << 24, generator=gen).pin_memory()
+
+    def filled(n, fn=None):
+        t = dev.tensor((n,))
+        src = chunk if fn is None else fn(chunk)
+        src = src.contiguous().pin_memory() if fn is not None else src
+        step = src.numel()
+        for off in range(0, n, step):
+            m = min(step, n - off)
+            t.write(src[:m].numpy(), offset_elems=off)
+        return t
+
+    def timeit(fn, reps):
+        MB.check(fn(), "warm")
+        dev.sync()
+        e0.record(stream)
+        for _ in range(reps):
+            MB.check(fn(), "op")
+        e1.record(stream)
+        dev.sync()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    def rec(group, name, ms, work, unit, peak):
+        rate = work / (ms / 1e3)
+        rows_out.append({"group": group, "case": name, "ms": round(ms, 4), "rate": round(rate, 1), "unit": unit,
+                         "frac": round(rate / peak, 3) if peak else None})
+        print(json.dumps(rows_out[-1]), flush=True)
+
+    def dims_strides(shape):
+        d = MB.pad6(shape)
+        return MB.i64x6(d), MB.i64x6(MB.strides6(d))
+
+    # ---- config 2: binary, same shape
+    for lg in (20, 24, 28):
+        n = 1 << lg
+        x, y, r = filled(n), filled(n, lambda c: c.abs() + 0.5), dev.tensor((n,))
+        d, s_ = dims_strides((n,))
+        for op in ("ADD", "SUB", "MUL", "DIV"):
+            ms = timeit(lambda: dev.L.mag_cuda_binary_f32(dev.p, MB.OP[op], r.data_ptr, x.data_ptr, y.data_ptr,
+                                                          d, s_, s_, d, s_), 20 if lg < 28 else 5)
+            rec("elementwise", f"{op} 2^{lg}", ms, 12.0 * n / 1e9, "GB/s", hbm)
+        for t in (x, y, r):
+            t.free()
+    # ---- config 2: tiling broadcast (reference-legal) and two-sided broadcast (extension)
+    xs, ys = (256, 8, 64, 32, 16, 8), (256, 1, 64, 1, 16, 1)
+    nx, ny = int(np.prod(xs)), int(np.prod(ys))
+    x, y, r = filled(nx), filled(ny), dev.tensor((nx,))
+    dx, sx = dims_strides(xs)
+    dy, sy = dims_strides(ys)
+    ms = timeit(lambda: dev.L.mag_cuda_binary_f32(dev.p, MB.OP["ADD"], r.data_ptr, x.data_ptr, y.data_ptr,
+                                                  dx, sx, sx, dy, sy), 5)
+    rec("elementwise", "ADD tiling [8,16,32,64,8,256]+[1,16,1,64,1,256]", ms, 4.0 * (2 * nx + ny) / 1e9, "GB/s", hbm)
+    for t in (x, y, r):
+        t.free()
+    xs, ys, rs = (256, 1, 64, 1, 16, 8), (256, 128, 1, 32, 16, 1), (256, 128, 64, 32, 16, 8)
+    nx, ny, nr = int(np.prod(xs)), int(np.prod(ys)), int(np.prod(rs))
+    x, y, r = filled(nx), filled(ny), dev.tensor((nr,))
+    ms = timeit(lambda: dev.L.mag_cuda_broadcast2_f32(dev.p, MB.OP["ADD"], r.data_ptr, x.data_ptr, y.data_ptr,
+                                                      MB.i64x6(rs), MB.i64x6(xs), MB.i64x6(ys)), 3)
+    rec("elementwise", "ADD two-sided [8,16,1,64,1,256]+[1,16,32,1,128,256] (2^33 out)", ms,
+        4.0 * (nx + ny + nr) / 1e9, "GB/s", hbm)
+    for t in (x, y, r):
+        t.free()
+    # ---- config 2: unary at 2^28
+    n = 1 << 28
+    x, xa, xl, r = filled(n), filled(n, lambda c: c.abs()), filled(n, lambda c: c.abs() + 1.0), dev.tensor((n,))
+    for op in ("ABS", "NEG", "LOG", "SQR", "SQRT", "SOFTMAX", "SIGMOID", "TANH", "RELU", "GELU"):
+        src = xl if op == "LOG" else (xa if op == "SQRT" else x)
+        ms = timeit(lambda: dev.L.mag_cuda_unary_f32(dev.p, MB.OP[op], r.data_ptr, src.data_ptr, n // 4096, 4096,
+                                                     4096, 4096, 0.0), 5)
+        rec("unary", f"{op} 2^28", ms, 8.0 * n / 1e9, "GB/s", hbm)
+    for t in (xa, xl):
+        t.free()
+    # ---- config 3: row reductions, softmax, full reductions
+    for rows, cols in ((65536, 1024), (4096, 32768), (1024, 262144)):
+        out = dev.tensor((rows * cols,))
+        for op in ("SUM", "MEAN", "MIN", "MAX"):
+            ms = timeit(lambda: dev.L.mag_cuda_reduce_rows_f32(dev.p, MB.OP[op], out.data_ptr, x.data_ptr, rows, cols), 5)
+            rec("reduce", f"row {op} ({rows},{cols})", ms, (4.0 * rows * cols + 4.0 * rows) / 1e9, "GB/s", hbm)
+        ms = timeit(lambda: dev.L.mag_cuda_softmax_rows_f32(dev.p, out.data_ptr, x.data_ptr, rows, cols), 5)
+        rec("reduce", f"row softmax ({rows},{cols})", ms, 8.0 * rows * cols / 1e9, "GB/s", hbm)
+        out.free()
+    d, s_ = dims_strides((n,))
+    for op in ("SUM", "MIN", "MAX"):
+        ms = timeit(lambda: dev.L.mag_cuda_reduce_f32(dev.p, MB.OP[op], r.data_ptr, x.data_ptr, d, s_), 5)
+        rec("reduce", f"full {op} 2^28", ms, 4.0 * n / 1e9, "GB/s", hbm)
+    for t in (x, r):
+        t.free()
+    # ---- config 4: matmul
+    for m in (1024, 4096, 8192, 16384):
+        a = filled(m * m, lambda c: c * (m ** -0.25))
+        c_ = dev.tensor((m * m,))
+        ms = timeit(lambda: dev.L.mag_cuda_matmul_f32(dev.p, c_.data_ptr, a.data_ptr, a.data_ptr, m, m, m),
+                    5 if m < 16384 else 2)
+        rec("matmul", f"square {m}^3 (3xTF32 tcgen05)", ms, 2.0 * m ** 3 / 1e12, "TFLOP/s", tf)
+        a.free()
+        c_.free()
+    k = nn = 4096
+    b = filled(k * nn, lambda c: c * (k ** -0.25))
+    for m in (1, 8, 64):
+        a = filled(m * k, lambda c: c * (k ** -0.25))
+        c_ = dev.tensor((m * nn,))
+        ms = timeit(lambda: dev.L.mag_cuda_matmul_f32(dev.p, c_.data_ptr, a.data_ptr, b.data_ptr, m, k, nn), 10)
+        rec("matmul", f"skinny M={m} K=N=4096 (HBM: Y once)", ms, 4.0 * (m * k + k * nn + m * nn) / 1e9, "GB/s", hbm)
+        a.free()
+        c_.free()
+    b.free()
+    bt, mm = 64, 512
+    a, c_ = filled(bt * mm * mm, lambda c: c * (mm ** -0.25)), dev.tensor((bt * mm * mm,))
+    ms = timeit(lambda: dev.L.mag_cuda_matmul_batched_f32(dev.p, c_.data_ptr, a.data_ptr, a.data_ptr, bt, mm, mm, mm), 5)
+    rec("matmul", "batched 64 x [512x512 . 512x512] (bit-exact CUDA-core path)", ms, 2.0 * bt * mm ** 3 / 1e12,
+        "TFLOP/s", None)
+    a.free()
+    c_.free()
+    # ---- reference CPU, single thread, on this host
+    cpu = []
+    if not args.no_cpu_baseline:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        from oracle import RefLib, REF_SO
+        if os.path.exists(REF_SO):
+            R = RefLib()
+            n = 1 << 24
+            v = np.random.default_rng(1).standard_normal(n).astype(np.float32)
+            tx, ty = R.tensor_nd((n,)), R.tensor_nd((n,))
+            R.write(tx, v)
+            R.write(ty, np.abs(v) + 0.5)
+
+            def cpu_time(fn, reps=3):
+                ts = []
+                for _ in range(reps):
+                    t0 = time.perf_counter()
+                    out = fn()
+                    ts.append(time.perf_counter() - t0)
+                    R.free(out)
+                return statistics.median(ts)
+            for op in ("ADD", "DIV"):
+                dt = cpu_time(lambda: R.op(op, tx, ty))
+                cpu.append({"case": f"{op} 2^24", "rate": 12.0 * n / dt / 1e9, "unit": "GB/s"})
+            for op in ("SIGMOID", "GELU"):
+                dt = cpu_time(lambda: R.op(op, tx))
+                cpu.append({"case": f"{op} 2^24", "rate": 8.0 * n / dt / 1e9, "unit": "GB/s"})
+            dt = cpu_time(lambda: R.op("SUM", tx))
+            cpu.append({"case": "full SUM 2^24", "rate": 4.0 * n / dt / 1e9, "unit": "GB/s"})
+            m = 1024
+            ta, tb = R.tensor_nd((m, m)), R.tensor_nd((m, m))
+            R.write(ta, v[:m * m])
+            R.write(tb, v[:m * m])
+            dt = cpu_time(lambda: R.op("MATMUL", ta, tb), reps=1)
+            cpu.append({"case": "MATMUL 1024^3", "rate": 2.0 * m ** 3 / dt / 1e12, "unit": "TFLOP/s"})
+            R.close()
+            for c in cpu:
+                c["rate"] = round(c["rate"], 4)
+                print(json.dumps({"cpu_reference_1thread": c}), flush=True)
+    if args.out:
+        with open(args.out, "w") as f:
+            json.dump({"gpu": rows_out, "cpu_reference_1thread": cpu, "peaks": {"hbm_gbs": hbm, "3xtf32_tflops": tf,
+                                                                                 "source": pk_src},
+                       "device": dev.name}, f, indent=1)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -528,7 +703,12 @@ def main():
     ap.add_argument("--case", default=None, choices=["gemm", "add", "sigmoid", "sum", "softmax"],
                     help="run one kernel family for a profiler instead of the benchmark")
     ap.add_argument("--size", type=int, default=None)
+    ap.add_argument("--sweep-full", action="store_true", help="measure every other BASELINE configuration")
+    ap.add_argument("--out", default=None)
     args = ap.parse_args()
+    if args.sweep_full:
+        run_sweep_full(args)
+        return
     if args.case:
         args.size = args.size or (8192 if args.case == "gemm" else 1 << 28)
         run_case(args)
