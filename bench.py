@@ -6,8 +6,9 @@ row softmax.  Weights are Kaiming-normal (std sqrt(2/4096)), biases zero, the
 input N(0, 1), all seeded synthetic data.  Each layer is the reference's op
 sequence MATMUL -> ADD(bias) -> GELU (magnetron/magnetron_cpu.c:2151, :1616,
 :942-1000), built as a deferred graph of magnetron tensors and executed by
-this backend as one CUDA graph; the softmax is the backend's row-softmax
-extension.  The batch is sharded by rows over one process per GPU; logits are
+this backend as one CUDA graph in which each layer is one tensor-core GEMM
+(bias, GELU and the next layer's operand split in its epilogue); the softmax
+is the backend's row-softmax extension.  The batch is sharded by rows over one process per GPU; logits are
 collected with an NCCL all-gather.
 
 One step = one forward over the whole batch.  `value` is whole-job samples/s
@@ -324,7 +325,7 @@ def run_ours(args):
     dev.sync()
 
     def step():
-        dev.graph_exec(z)
+        dev.graph_exec(z, fused=True)
         MB.check(dev.L.mag_cuda_softmax_rows_f32(dev.p, P.data_ptr, z.data_ptr, rows, D_OUT), "softmax")
         if world > 1:
             with torch.cuda.stream(stream):

@@ -71,7 +71,13 @@ MAG_CUDA_EXPORT size_t mag_cuda_memory_in_use(mag_compute_device_t* dvc);
  * root captures the launch sequence into a CUDA graph; later calls with the
  * same node set replay it.  Returns after enqueueing (asynchronous). */
 MAG_CUDA_EXPORT int mag_cuda_graph_exec(mag_compute_device_t* dvc, mag_tensor_t* root);
-/* Drops the cached graph of root (call before freeing the graph's tensors). */
+/* As mag_cuda_graph_exec, and fuses dense layers, MATMUL -> ADD(same-shape bias)
+ * [-> GELU], into one tensor-core GEMM per layer (bias, GELU and the next
+ * layer's operand split in its epilogue).  After the call the root and every
+ * tensor outside such chains hold their values; the MATMUL and ADD results
+ * inside a fused chain are not written. */
+MAG_CUDA_EXPORT int mag_cuda_graph_exec_fused(mag_compute_device_t* dvc, mag_tensor_t* root);
+/* Drops the cached graphs of root (call before freeing the graph's tensors). */
 MAG_CUDA_EXPORT int mag_cuda_graph_release(mag_compute_device_t* dvc, mag_tensor_t* root);
 /* Executes one node eagerly, exactly as eager_exec_fwd would. */
 MAG_CUDA_EXPORT int mag_cuda_exec_node(mag_compute_device_t* dvc, mag_tensor_t* node);

@@ -72,6 +72,7 @@ typedef struct mcu_block {
 
 typedef struct mcu_graph {
     mag_tensor_t* root;
+    int fused;
     uint64_t sig;
     size_t n_nodes;
     cudaGraphExec_t exec;
@@ -359,7 +360,7 @@ static int matmul_path(mcu_device* d, int64_t M, int64_t K, int64_t N) {
     if (d->matmul_mode == 1) return MM_EXACT;
     int tc_ok = mcu_matmul_tc_supported() && M >= 128 && N >= 64 && K >= 32;
     if (d->matmul_mode == 2 && tc_ok) return MM_TC;
-    if (M <= 16 && K * N >= ((int64_t)1 << 20)) return MM_SKINNY;
+    if (M <= 64 && K * N >= ((int64_t)1 << 20)) return MM_SKINNY;
     if (tc_ok && (double)M * (double)N * (double)K >= 1.0e9) return MM_TC;
     return MM_EXACT;
 }
@@ -891,38 +892,191 @@ static int is_compute(const mag_tensor_t* t) {
            t->op != MAG_ABI_OP_PERMUTE;
 }
 
-int mag_cuda_graph_exec(mag_compute_device_t* dvc, mag_tensor_t* root) {
+/* ---- fusion planner for deferred graphs ----
+ * Recognises dense layers, MATMUL -> ADD(same-shape bias) [-> GELU], whose
+ * intermediates have no other consumer inside the graph, and runs each as one
+ * tensor-core GEMM whose epilogue adds the bias, applies GELU and, when the
+ * next node is a MATMUL reading this layer's output, also writes that
+ * MATMUL's tf32 hi/lo operand split (so it skips its split pass).  Only the
+ * fused chain's final tensor is written; the MATMUL and ADD results inside a
+ * chain are not materialised. */
+
+enum { PLAN_NORMAL = 0, PLAN_FUSED = 1, PLAN_SKIP = 2 };
+
+typedef struct mcu_plan_item {
+    int kind;
+    mag_tensor_t* out;      /* fused: tensor whose storage receives the layer output */
+    mag_tensor_t* bias;     /* fused: same-shape bias tensor or NULL */
+    int act;                /* fused: 0 none, 1 GELU */
+    int a_split;            /* -1, or activation split buffer holding A's hi/lo */
+    int out_split;          /* -1, or activation split buffer receiving out's hi/lo */
+} mcu_plan_item;
+
+static int same_shape_canonical(const mag_tensor_t* a, const mag_tensor_t* b) {
+    for (int k = 0; k < 6; ++k)
+        if (a->shape[k] != b->shape[k]) return 0;
+    return is_canonical(a) && is_canonical(b);
+}
+
+static int tc_matmul_ok(mcu_device* d, const mag_tensor_t* m) {
+    if (m->op != MAG_ABI_OP_MATMUL) return 0;
+    const mag_tensor_t* x = m->op_inputs[0];
+    const mag_tensor_t* y = m->op_inputs[1];
+    if (!x || !y || x->shape[2] != 1 || x->shape[3] != 1 || y->shape[2] != 1 || y->shape[3] != 1) return 0;
+    const int64_t M = x->shape[0], K = x->shape[1], N = y->shape[1];
+    if (m->storage.base == x->storage.base || m->storage.base == y->storage.base) return 0;
+    if (m->shape[1] != N || (size_t)(M * N * 4) != m->storage.size) return 0;
+    return matmul_path(d, M, K, N) == MM_TC;
+}
+
+static size_t find_index(mag_tensor_t** nodes, size_t n, const mag_tensor_t* t) {
+    for (size_t i = 0; i < n; ++i)
+        if (nodes[i] == t) return i;
+    return n;
+}
+
+/* Fills plan[n]; returns the bytes of one activation split buffer (0: none needed). */
+static size_t plan_fusion(mcu_device* d, mag_tensor_t** nodes, size_t n, mag_tensor_t* root, mcu_plan_item* plan) {
+    int* users = (int*)calloc(n, sizeof(int));
+    size_t* user_of = (size_t*)malloc(n * sizeof(size_t));
+    for (size_t i = 0; i < n; ++i) {
+        plan[i] = (mcu_plan_item){PLAN_NORMAL, NULL, NULL, 0, -1, -1};
+        user_of[i] = n;
+    }
+    for (size_t i = 0; i < n; ++i)
+        for (int k = 0; k < MAG_ABI_MAX_INPUTS; ++k) {
+            mag_tensor_t* in = nodes[i]->op_inputs[k];
+            if (!in) continue;
+            size_t j = find_index(nodes, n, in);
+            if (j < n) {
+                users[j]++;
+                user_of[j] = i;
+            }
+        }
+    size_t split_bytes = 0;
+    for (size_t i = 0; i < n; ++i) {
+        mag_tensor_t* m = nodes[i];
+        if (plan[i].kind != PLAN_NORMAL || !tc_matmul_ok(d, m) || m == root || users[i] != 1) continue;
+        size_t ia = user_of[i];
+        mag_tensor_t* a = nodes[ia];
+        if (a->op != MAG_ABI_OP_ADD || a->op_inputs[0] != m || a->op_inputs[1] == m) continue;
+        mag_tensor_t* b = a->op_inputs[1];
+        if (!same_shape_canonical(a, m) || !same_shape_canonical(b, m) || a->storage.size != m->storage.size) continue;
+        plan[i].kind = PLAN_FUSED;
+        plan[i].bias = b;
+        plan[i].out = a;
+        plan[ia].kind = PLAN_SKIP;
+        size_t last = ia;
+        if (a != root && users[ia] == 1) {
+            size_t ig = user_of[ia];
+            mag_tensor_t* g = nodes[ig];
+            if (g->op == MAG_ABI_OP_GELU && g->op_inputs[0] == a && same_shape_canonical(g, m) &&
+                g->storage.size == m->storage.size && m->shape[0] % 4 == 0) {
+                plan[i].act = 1;
+                plan[i].out = g;
+                plan[ig].kind = PLAN_SKIP;
+                last = ig;
+            }
+        }
+        /* the next MATMUL reads this layer's output: hand it the split operand */
+        mag_tensor_t* out = plan[i].out;
+        const int64_t N = m->shape[1];
+        if (out != root && users[last] == 1 && N % 32 == 0) {
+            size_t in2 = user_of[last];
+            mag_tensor_t* m2 = nodes[in2];
+            if (m2->op_inputs[0] == out && m2->op_inputs[1] != out && tc_matmul_ok(d, m2)) {
+                int buf = plan[i].a_split == 0 ? 1 : 0;
+                plan[i].out_split = buf;
+                plan[in2].a_split = buf;
+                size_t bytes = (size_t)(m->shape[0] * ((N + 31) / 32 * 32)) * 4 * 2;
+                if (bytes > split_bytes) split_bytes = bytes;
+            }
+        }
+    }
+    free(users);
+    free(user_of);
+    return split_bytes;
+}
+
+/* Runs one planned MATMUL (fused or with a pre-split operand). */
+static int exec_planned_matmul(mcu_device* d, mag_tensor_t* m, const mcu_plan_item* it, char* scratch,
+                               size_t split_off, size_t split_bytes) {
+    mag_tensor_t* x = m->op_inputs[0];
+    mag_tensor_t* y = m->op_inputs[1];
+    const int64_t M = x->shape[0], K = x->shape[1], N = y->shape[1];
+    mag_tensor_t* out = it->kind == PLAN_FUSED ? it->out : m;
+    if (it->a_split < 0) materialize(d, x->storage.base);
+    materialize(d, y->storage.base);
+    if (it->bias) materialize(d, it->bias->storage.base);
+    result_written(d, out->storage.base, (size_t)(M * N * 4) == out->storage.size);
+    mcu_tc_epilogue ep;
+    memset(&ep, 0, sizeof(ep));
+    const size_t half = split_bytes / 2;
+    if (it->a_split >= 0) {
+        char* b = scratch + split_off + (size_t)it->a_split * split_bytes;
+        ep.a_hi = (const float*)b;
+        ep.a_lo = (const float*)(b + half);
+    }
+    if (it->kind == PLAN_FUSED) {
+        ep.bias = it->bias ? fptr(it->bias) : NULL;
+        ep.act = it->act;
+        if (it->out_split >= 0) {
+            char* b = scratch + split_off + (size_t)it->out_split * split_bytes;
+            ep.out_hi = (float*)b;
+            ep.out_lo = (float*)(b + half);
+            ep.kp_out = (N + 31) / 32 * 32;
+        }
+    }
+    int rc = mcu_launch_matmul_tc_ex(fptr(out), fptr(x), fptr(y), M, K, N, scratch, d->d_status, d->stream, &ep);
+    if (!rc) mcu_count_launches(it->a_split >= 0 ? 2 : 3);
+    return rc;
+}
+
+static int graph_exec_impl(mag_compute_device_t* dvc, mag_tensor_t* root, int fuse) {
     if (!dvc || !root) return MAG_CUDA_E_INVALID;
     mcu_device* d = dev_of(dvc);
     size_t n = 0;
     mag_tensor_t** nodes = topo_order(root, &n);
     uint64_t sig = graph_signature(nodes, n);
     mcu_graph* g = d->graphs;
-    while (g && g->root != root) g = g->next;
+    while (g && (g->root != root || g->fused != fuse)) g = g->next;
     if (g && g->sig == sig) {
         free(nodes);
         g->ran = g->n_ev > 0;
         mcu_count_launches((int)g->n_kernels);
         return (int)cudaGraphLaunch(g->exec, d->stream);
     }
-    if (g) mag_cuda_graph_release(dvc, root);
+    if (g) {
+        mcu_graph** pp = &d->graphs;
+        while (*pp != g) pp = &(*pp)->next;
+        *pp = g->next;
+        cudaStreamSynchronize(d->stream);
+        graph_free(g);
+    }
+    mcu_plan_item* plan = (mcu_plan_item*)calloc(n ? n : 1, sizeof(mcu_plan_item));
+    for (size_t i = 0; i < n; ++i) plan[i] = (mcu_plan_item){PLAN_NORMAL, NULL, NULL, 0, -1, -1};
+    size_t split_bytes = fuse ? plan_fusion(d, nodes, n, root, plan) : 0;
     /* leaves are materialised outside the capture so replays never clear data the caller wrote later */
     size_t scratch = 0;
     for (size_t i = 0; i < n; ++i) {
         if (!is_compute(nodes[i])) materialize(d, nodes[i]->storage.base);
-        else {
+        else if (plan[i].kind != PLAN_SKIP) {
             size_t s = node_scratch_bytes(d, nodes[i]);
             if (s > scratch) scratch = s;
         }
     }
+    const size_t split_off = (scratch + 1023) & ~(size_t)1023;
+    const size_t total = split_bytes ? split_off + 2 * split_bytes : scratch;
     g = (mcu_graph*)calloc(1, sizeof(mcu_graph));
     g->root = root;
+    g->fused = fuse;
     g->sig = sig;
     g->n_nodes = n;
-    if (scratch) {
-        cudaError_t e = cudaMalloc(&g->scratch, scratch);
+    if (total) {
+        cudaError_t e = cudaMalloc(&g->scratch, total);
         if (e != cudaSuccess) {
             free(g);
+            free(plan);
             free(nodes);
             return (int)e;
         }
@@ -932,7 +1086,7 @@ int mag_cuda_graph_exec(mag_compute_device_t* dvc, mag_tensor_t* root) {
     d->capturing = 1;
     d->graph_scratch = g->scratch;
     size_t saved_bytes = d->scratch_bytes;
-    d->scratch_bytes = scratch;
+    d->scratch_bytes = total;
     if (d->profiling) {
         g->ev_op = (int*)calloc(n, sizeof(int));
         g->ev_a = (cudaEvent_t*)calloc(n, sizeof(cudaEvent_t));
@@ -942,7 +1096,7 @@ int mag_cuda_graph_exec(mag_compute_device_t* dvc, mag_tensor_t* root) {
     MCU_CHECK(cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeThreadLocal));
     int rc = 0;
     for (size_t i = 0; i < n && !rc; ++i) {
-        if (!is_compute(nodes[i])) continue;
+        if (!is_compute(nodes[i]) || plan[i].kind == PLAN_SKIP) continue;
         if (d->profiling) {
             size_t k = g->n_ev++;
             g->ev_op[k] = nodes[i]->op;
@@ -950,7 +1104,10 @@ int mag_cuda_graph_exec(mag_compute_device_t* dvc, mag_tensor_t* root) {
             MCU_CHECK(cudaEventCreate(&g->ev_b[k]));
             MCU_CHECK(cudaEventRecordWithFlags(g->ev_a[k], d->stream, cudaEventRecordExternal));
         }
-        rc = exec_node(d, nodes[i]);
+        if (plan[i].kind == PLAN_FUSED || plan[i].a_split >= 0)
+            rc = exec_planned_matmul(d, nodes[i], &plan[i], (char*)g->scratch, split_off, split_bytes);
+        else
+            rc = exec_node(d, nodes[i]);
         if (d->profiling) MCU_CHECK(cudaEventRecordWithFlags(g->ev_b[g->n_ev - 1], d->stream, cudaEventRecordExternal));
     }
     cudaError_t ce = cudaStreamEndCapture(d->stream, &graph);
@@ -960,6 +1117,7 @@ int mag_cuda_graph_exec(mag_compute_device_t* dvc, mag_tensor_t* root) {
     d->graph_scratch = NULL;
     d->scratch_bytes = saved_bytes;
     free(nodes);
+    free(plan);
     if (rc || ce != cudaSuccess) {
         if (ce == cudaSuccess) cudaGraphDestroy(graph);
         g->exec = NULL;
@@ -980,16 +1138,27 @@ int mag_cuda_graph_exec(mag_compute_device_t* dvc, mag_tensor_t* root) {
     return (int)cudaGraphLaunch(g->exec, d->stream);
 }
 
+int mag_cuda_graph_exec(mag_compute_device_t* dvc, mag_tensor_t* root) { return graph_exec_impl(dvc, root, 0); }
+
+int mag_cuda_graph_exec_fused(mag_compute_device_t* dvc, mag_tensor_t* root) {
+    return graph_exec_impl(dvc, root, 1);
+}
+
 int mag_cuda_graph_release(mag_compute_device_t* dvc, mag_tensor_t* root) {
     mcu_device* d = dev_of(dvc);
-    mcu_graph** pp = &d->graphs;
-    while (*pp && (*pp)->root != root) pp = &(*pp)->next;
-    if (!*pp) return MAG_CUDA_E_INVALID;
-    mcu_graph* g = *pp;
-    *pp = g->next;
+    int found = 0;
     cudaStreamSynchronize(d->stream);
-    graph_free(g);
-    return 0;
+    for (mcu_graph** pp = &d->graphs; *pp;) {
+        if ((*pp)->root == root) {
+            mcu_graph* g = *pp;
+            *pp = g->next;
+            graph_free(g);
+            found = 1;
+        } else {
+            pp = &(*pp)->next;
+        }
+    }
+    return found ? 0 : MAG_CUDA_E_INVALID;
 }
 
 /* --------------------------------------------------------- profiling --- */

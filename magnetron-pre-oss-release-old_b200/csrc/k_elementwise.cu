@@ -12,8 +12,9 @@
 //
 // Layout: all three share HBM-streaming kernels: a linear path with 128-bit
 // loads/stores for contiguous operands, and a row-segment path where one warp
-// owns a 128-column segment of a row and lane 0's row decomposition is
-// broadcast with a shuffle, so per-element index work is one modulo at most.
+// owns a 512-column segment of a row (all of its loads issued before the
+// stores) and lane 0's row decomposition is broadcast with a shuffle, so
+// per-element index work is one modulo at most.
 #include <cuda_runtime.h>
 #include <cstdint>
 #include "mcu_math.cuh"
@@ -44,10 +45,18 @@ unsigned grid_for(uint64_t work_items, unsigned per_block) {
     return (unsigned)g;
 }
 
+// Out of line so a runtime lane/tail choice is a branch, not both evaluated.
+template <int OP>
+__device__ __noinline__ float tail_call(float x) { return tail_op<OP>(x); }
+
 template <int OP>
 __device__ __forceinline__ float uapply(float x, float xi, bool lane) {
-    if constexpr (is_lane_op(OP)) return lane ? lane_op<OP>(x) : tail_op<OP>(x);
-    else return exact_op<OP>(x, xi);
+    if constexpr (is_lane_op(OP)) {
+        if (lane) return lane_op<OP>(x);
+        return tail_call<OP>(x);
+    } else {
+        return exact_op<OP>(x, xi);
+    }
 }
 
 // ---------------------------------------------------------------- unary ---
@@ -193,6 +202,8 @@ struct RowParams {
 
 __device__ __forceinline__ uint32_t mod_by(uint32_t v, const FastDiv& f) { return v - fdiv(v, f) * f.d; }
 
+constexpr uint32_t kRowSeg = 512;  // columns per warp iteration (4 steps of 32 lanes x 4)
+
 template <int OP, bool VEC>
 __global__ void __launch_bounds__(kThreads) binary_rows(float* __restrict__ r, const float* __restrict__ x,
                                                         const float* __restrict__ y, const RowParams p) {
@@ -221,26 +232,37 @@ __global__ void __launch_bounds__(kThreads) binary_rows(float* __restrict__ r, c
         yo = __shfl_sync(0xffffffffu, yo, 0);
         seg = __shfl_sync(0xffffffffu, seg, 0);
         if constexpr (VEC) {
-            uint32_t c = seg * 128u + 4u * (uint32_t)lane_id;
-            if (c < p.cols) {
-                uint32_t xc = p.x_mod ? mod_by(c, p.xdim[0]) : c;
-                float4 a = *(const float4*)(x + xo + xc);
-                float4 b;
-                if (p.y_mode == 1) {
-                    float t = y[yo];
-                    b = make_float4(t, t, t, t);
-                } else {
-                    uint32_t yc = p.y_mode == 0 ? c : mod_by(c, p.ydim[0]);
-                    b = *(const float4*)(y + yo + yc);
-                }
-                float4 o;
-                o.x = binop<OP>(a.x, b.x); o.y = binop<OP>(a.y, b.y); o.z = binop<OP>(a.z, b.z); o.w = binop<OP>(a.w, b.w);
-                __stcs((float4*)(r + ro + c), o);
-            }
-        } else {
+            float4 a[4], b[4];
+            uint32_t cs[4];
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
-                uint32_t c = seg * 128u + (uint32_t)lane_id + 32u * u;
+                const uint32_t c = seg * kRowSeg + 128u * u + 4u * (uint32_t)lane_id;
+                cs[u] = c;
+                if (c < p.cols) {
+                    const uint32_t xc = p.x_mod ? mod_by(c, p.xdim[0]) : c;
+                    a[u] = *(const float4*)(x + xo + xc);
+                    if (p.y_mode == 1) {
+                        const float t = y[yo];
+                        b[u] = make_float4(t, t, t, t);
+                    } else {
+                        const uint32_t yc = p.y_mode == 0 ? c : mod_by(c, p.ydim[0]);
+                        b[u] = *(const float4*)(y + yo + yc);
+                    }
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                if (cs[u] < p.cols) {
+                    float4 o;
+                    o.x = binop<OP>(a[u].x, b[u].x); o.y = binop<OP>(a[u].y, b[u].y);
+                    o.z = binop<OP>(a[u].z, b[u].z); o.w = binop<OP>(a[u].w, b[u].w);
+                    __stcs((float4*)(r + ro + cs[u]), o);
+                }
+            }
+        } else {
+#pragma unroll 4
+            for (int u = 0; u < 16; ++u) {
+                uint32_t c = seg * kRowSeg + (uint32_t)lane_id + 32u * u;
                 if (c < p.cols) {
                     uint32_t xc = p.x_mod ? mod_by(c, p.xdim[0]) : c;
                     int64_t yc = p.y_mode == 0 ? (int64_t)c * p.ys[0]
@@ -271,7 +293,7 @@ cudaError_t launch_rows(float* r, const float* x, const float* y, const int64_t*
         p.ydim[k] = make_fastdiv((uint32_t)yd[k]);
         if (k) rows *= (uint64_t)dims[k];
     }
-    uint64_t spr = ((uint64_t)dims[0] + 127) / 128;
+    uint64_t spr = ((uint64_t)dims[0] + kRowSeg - 1) / kRowSeg;
     p.segs_per_row = make_fastdiv((uint32_t)spr);
     p.nseg = rows * spr;
     if (p.nseg >= (1ull << 32)) return cudaErrorInvalidValue;

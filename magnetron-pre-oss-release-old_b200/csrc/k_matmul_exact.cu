@@ -11,7 +11,7 @@
 // that the grid covers the GPU for small problems (the 2-layer MLP's
 // 256x784x256 product runs on 64 CTAs with 32x32 tiles).
 //
-// matmul_skinny serves M <= 16 (matrix-vector-like products, HBM-bound on
+// matmul_skinny serves M <= 64 (matrix-vector-like products, HBM-bound on
 // Y): K is split across CTAs so that all SMs stream Y, partial sums go to a
 // scratch buffer and a second kernel adds the K slices in a fixed order.  It
 // uses FMA and a different summation order, so it is accurate to f32
@@ -104,58 +104,81 @@ cudaError_t launch_exact(float* r, const float* x, const float* y, int64_t batch
 
 // ------------------------------------------------------------- skinny ---
 
-constexpr int kSkinnyRows = 16;
-constexpr int kSkinnyCols = kThreads * 4;
+constexpr int kSkinnyRows = 16;           // rows per CTA (M up to 64 uses up to 4 row blocks)
+constexpr int kSkinnyCols = kThreads * 4; // each thread owns 4 columns
+constexpr int kSkinnyKc = 64;             // k rows per slice (multiple of 8)
 
-// Partial product of X[0:M, k0:k0+KC] and Y[k0:k0+KC, cols]; thread owns 4 columns.
+// Partial product of X[m0:m0+MR, slice] and Y[slice, cols]; Y rows are
+// fetched 8 at a time before any FMA so every thread keeps 8 128-bit loads
+// in flight.
+template <int MR>
 __global__ void __launch_bounds__(kThreads) matmul_skinny_part(float* __restrict__ part, const float* __restrict__ x,
                                                                const float* __restrict__ y, int M, int64_t K,
                                                                int64_t N, int64_t kc) {
-    __shared__ float xs[kSkinnyRows][64];
+    __shared__ float xs[MR][kSkinnyKc];
     const int64_t c = (int64_t)blockIdx.x * kSkinnyCols + 4 * threadIdx.x;
     const int64_t k0 = (int64_t)blockIdx.y * kc;
     const int64_t k1 = (k0 + kc < K) ? k0 + kc : K;
-    const bool vec = (N % 4 == 0) && (((uintptr_t)y & 15) == 0);
-    float acc[kSkinnyRows][4];
+    const int m0 = blockIdx.z * MR;
+    const bool vec = (N % 4 == 0) && (((uintptr_t)y & 15) == 0) && (c + 3 < N);
+    for (int t = threadIdx.x; t < MR * kSkinnyKc; t += kThreads) {
+        const int m = t / kSkinnyKc, kk = t % kSkinnyKc;
+        xs[m][kk] = (m0 + m < M && k0 + kk < k1) ? x[(int64_t)(m0 + m) * K + k0 + kk] : 0.0f;
+    }
+    __syncthreads();
+    float acc[MR][4];
 #pragma unroll
-    for (int m = 0; m < kSkinnyRows; ++m) acc[m][0] = acc[m][1] = acc[m][2] = acc[m][3] = 0.0f;
-    for (int64_t kb = k0; kb < k1; kb += 64) {
-        const int kn = (int)((k1 - kb) < 64 ? (k1 - kb) : 64);
-        __syncthreads();
-        for (int t = threadIdx.x; t < kSkinnyRows * 64; t += kThreads) {
-            int m = t / 64, kk = t % 64;
-            xs[m][kk] = (m < M && kk < kn) ? x[(int64_t)m * K + kb + kk] : 0.0f;
+    for (int m = 0; m < MR; ++m) acc[m][0] = acc[m][1] = acc[m][2] = acc[m][3] = 0.0f;
+    if (c < N) {
+        auto load = [&](int64_t k) -> float4 {
+            const float* py = y + k * N + c;
+            if (vec) return __ldcs((const float4*)py);
+            float4 t;
+            t.x = py[0];
+            t.y = c + 1 < N ? py[1] : 0.0f;
+            t.z = c + 2 < N ? py[2] : 0.0f;
+            t.w = c + 3 < N ? py[3] : 0.0f;
+            return t;
+        };
+        int64_t k = k0;
+        for (; k + 8 <= k1; k += 8) {
+            float4 yv[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) yv[u] = load(k + u);
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+#pragma unroll
+                for (int m = 0; m < MR; ++m) {
+                    const float xv = xs[m][k - k0 + u];
+                    acc[m][0] = fmaf(xv, yv[u].x, acc[m][0]);
+                    acc[m][1] = fmaf(xv, yv[u].y, acc[m][1]);
+                    acc[m][2] = fmaf(xv, yv[u].z, acc[m][2]);
+                    acc[m][3] = fmaf(xv, yv[u].w, acc[m][3]);
+                }
         }
-        __syncthreads();
-        if (c < N) {
-#pragma unroll 4
-            for (int kk = 0; kk < kn; ++kk) {
-                float4 yv;
-                const float* py = y + (kb + kk) * N + c;
-                if (vec && c + 3 < N) yv = __ldcs((const float4*)py);
-                else {
-                    yv.x = py[0];
-                    yv.y = c + 1 < N ? py[1] : 0.0f;
-                    yv.z = c + 2 < N ? py[2] : 0.0f;
-                    yv.w = c + 3 < N ? py[3] : 0.0f;
-                }
+        for (; k < k1; ++k) {
+            const float4 yv = load(k);
 #pragma unroll
-                for (int m = 0; m < kSkinnyRows; ++m) {
-                    float xv = xs[m][kk];
-                    acc[m][0] = fmaf(xv, yv.x, acc[m][0]);
-                    acc[m][1] = fmaf(xv, yv.y, acc[m][1]);
-                    acc[m][2] = fmaf(xv, yv.z, acc[m][2]);
-                    acc[m][3] = fmaf(xv, yv.w, acc[m][3]);
-                }
+            for (int m = 0; m < MR; ++m) {
+                const float xv = xs[m][k - k0];
+                acc[m][0] = fmaf(xv, yv.x, acc[m][0]);
+                acc[m][1] = fmaf(xv, yv.y, acc[m][1]);
+                acc[m][2] = fmaf(xv, yv.z, acc[m][2]);
+                acc[m][3] = fmaf(xv, yv.w, acc[m][3]);
             }
         }
-    }
-    if (c < N) {
         float* p = part + (int64_t)blockIdx.y * M * N;
-        for (int m = 0; m < M; ++m)
 #pragma unroll
-            for (int q = 0; q < 4; ++q)
-                if (c + q < N) p[(int64_t)m * N + c + q] = acc[m][q];
+        for (int m = 0; m < MR; ++m) {
+            if (m0 + m >= M) break;
+            if (vec) {
+                *(float4*)(p + (int64_t)(m0 + m) * N + c) = make_float4(acc[m][0], acc[m][1], acc[m][2], acc[m][3]);
+            } else {
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    if (c + q < N) p[(int64_t)(m0 + m) * N + c + q] = acc[m][q];
+            }
+        }
     }
 }
 
@@ -168,13 +191,22 @@ __global__ void __launch_bounds__(kThreads) matmul_skinny_sum(float* __restrict_
     }
 }
 
-int64_t skinny_slices(int64_t K, int64_t N) {
-    int64_t colblocks = (N + kSkinnyCols - 1) / kSkinnyCols;
-    int64_t want = (2 * (int64_t)sm_count() + colblocks - 1) / colblocks;
-    int64_t maxs = (K + 63) / 64;
-    if (want > maxs) want = maxs;
-    if (want < 1) want = 1;
-    return want;
+// K slices so that about two CTAs per SM stream Y.
+int64_t skinny_slices(int64_t M, int64_t K, int64_t N) {
+    const int64_t colblocks = (N + kSkinnyCols - 1) / kSkinnyCols;
+    const int64_t rowblocks = (M + kSkinnyRows - 1) / kSkinnyRows;
+    int64_t want = (2 * (int64_t)sm_count() + colblocks * rowblocks - 1) / (colblocks * rowblocks);
+    int64_t kc = (K + want - 1) / (want < 1 ? 1 : want);
+    kc = (kc + 7) / 8 * 8;
+    if (kc > kSkinnyKc) kc = kSkinnyKc;
+    if (kc < 8) kc = 8;
+    int64_t slices = (K + kc - 1) / kc;
+    return slices < 1 ? 1 : slices;
+}
+
+int64_t skinny_kc(int64_t K, int64_t slices) {
+    int64_t kc = (K + slices - 1) / slices;
+    return (kc + 7) / 8 * 8;
 }
 
 }  // namespace
@@ -194,23 +226,31 @@ extern "C" int mcu_launch_matmul_exact(float* r, const float* x, const float* y,
 }
 
 extern "C" size_t mcu_matmul_skinny_scratch_bytes(int64_t M, int64_t K, int64_t N) {
-    return (size_t)skinny_slices(K, N) * (size_t)M * (size_t)N * sizeof(float);
+    return (size_t)skinny_slices(M, K, N) * (size_t)M * (size_t)N * sizeof(float);
 }
 
 extern "C" int mcu_launch_matmul_skinny(float* r, const float* x, const float* y, int64_t M, int64_t K, int64_t N,
                                         int64_t r_ld, void* scratch, cudaStream_t st) {
     if (M <= 0 || N <= 0) return (int)cudaSuccess;
-    if (M > kSkinnyRows) return (int)cudaErrorInvalidValue;
-    int64_t slices = skinny_slices(K, N);
-    int64_t kc = (K + slices - 1) / slices;
-    slices = (K + kc - 1) / kc;
-    if (slices < 1) slices = 1;
-    dim3 grid((unsigned)((N + kSkinnyCols - 1) / kSkinnyCols), (unsigned)slices);
-    matmul_skinny_part<<<grid, kThreads, 0, st>>>((float*)scratch, x, y, (int)M, K, N, kc);
+    if (M > 4 * kSkinnyRows) return (int)cudaErrorInvalidValue;
+    int64_t slices = skinny_slices(M, K, N);
+    const int64_t kc = skinny_kc(K, slices);
+    slices = K > 0 ? (K + kc - 1) / kc : 1;
+    const unsigned rowblocks = (unsigned)((M + kSkinnyRows - 1) / kSkinnyRows);
+    const int mr = M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : M <= 8 ? 8 : 16;
+    dim3 grid((unsigned)((N + kSkinnyCols - 1) / kSkinnyCols), (unsigned)slices, mr == 16 ? rowblocks : 1);
+    float* part = (float*)scratch;
+    switch (mr) {
+        case 1: matmul_skinny_part<1><<<grid, kThreads, 0, st>>>(part, x, y, (int)M, K, N, kc); break;
+        case 2: matmul_skinny_part<2><<<grid, kThreads, 0, st>>>(part, x, y, (int)M, K, N, kc); break;
+        case 4: matmul_skinny_part<4><<<grid, kThreads, 0, st>>>(part, x, y, (int)M, K, N, kc); break;
+        case 8: matmul_skinny_part<8><<<grid, kThreads, 0, st>>>(part, x, y, (int)M, K, N, kc); break;
+        default: matmul_skinny_part<16><<<grid, kThreads, 0, st>>>(part, x, y, (int)M, K, N, kc); break;
+    }
     int64_t MN = M * N;
     int64_t g = (MN + kThreads - 1) / kThreads;
     if (g > 4 * sm_count()) g = 4 * sm_count();
-    matmul_skinny_sum<<<(unsigned)g, kThreads, 0, st>>>(r, (const float*)scratch, MN, (int)slices, N, r_ld);
+    matmul_skinny_sum<<<(unsigned)g, kThreads, 0, st>>>(r, part, MN, (int)slices, N, r_ld);
     return (int)cudaGetLastError();
 }
 

@@ -173,11 +173,34 @@ struct Cfg {
     static_assert(TMEM_COLS <= 512, "two accumulators must fit TMEM");
 };
 
-template <int BN, int STAGES>
+// Epilogue of a fused dense layer: out = act(acc + bias) and, for the next
+// product, its tf32 hi/lo split in [M][Kp_out] layout.
+struct Epi {
+    const float* bias;  // same row-major index as the result, or null
+    float* out_hi;      // split output (null: none)
+    float* out_lo;
+    int64_t kp_out;
+    int act;            // 0 none, 1 GELU (the reference's vector-lane formula)
+};
+
+__device__ __forceinline__ float rna_tf32_dev(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r);
+}
+
+__device__ __forceinline__ float gelu_lane(float x) {
+    // GELU lane of mag_vgelu_f32 (magnetron/magnetron_cpu.c:985-993), tanh by tanhf
+    const float a = __fadd_rn(1.0f, __fmul_rn(0.044715f, __fmul_rn(x, x)));
+    const float b = __fadd_rn(1.0f, tanhf(__fmul_rn(0.79788456080286535587989211986876f, __fmul_rn(x, a))));
+    return __fmul_rn(0.5f, __fmul_rn(x, b));
+}
+
+template <int BN, int STAGES, bool FUSED>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_3xtf32(const __grid_constant__ CUtensorMap map_xhi, const __grid_constant__ CUtensorMap map_xlo,
                 const __grid_constant__ CUtensorMap map_yhi, const __grid_constant__ CUtensorMap map_ylo,
-                float* __restrict__ r, int M, int N, int Kp, int64_t ldr, int* status) {
+                float* __restrict__ r, int M, int N, int Kp, int64_t ldr, int* status, const Epi epi) {
     using C = Cfg<BN, STAGES>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -291,18 +314,54 @@ __global__ void __launch_bounds__(kThreads, 1)
                 uint32_t v[32];
                 tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + a * BN + c * 32, v);
                 const int cb = col0 + c * 32;
-                if (row_ok) {
-                    if (vec && cb + 32 <= N) {
+                if (!row_ok) continue;
+                if constexpr (FUSED) {
+                    const bool full = cb + 32 <= N;
+                    if (epi.bias) {
+                        const float* pb = epi.bias + (int64_t)row * N + cb;
+                        if (full && vec) {
 #pragma unroll
-                        for (int j = 0; j < 32; j += 4)
-                            *(float4*)(out + c * 32 + j) = make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]),
-                                                                       __uint_as_float(v[j + 2]),
-                                                                       __uint_as_float(v[j + 3]));
-                    } else {
+                            for (int j = 0; j < 32; j += 4) {
+                                const float4 b4 = __ldcs((const float4*)(pb + j));
+                                v[j] = __float_as_uint(__fadd_rn(__uint_as_float(v[j]), b4.x));
+                                v[j + 1] = __float_as_uint(__fadd_rn(__uint_as_float(v[j + 1]), b4.y));
+                                v[j + 2] = __float_as_uint(__fadd_rn(__uint_as_float(v[j + 2]), b4.z));
+                                v[j + 3] = __float_as_uint(__fadd_rn(__uint_as_float(v[j + 3]), b4.w));
+                            }
+                        } else {
 #pragma unroll
-                        for (int j = 0; j < 32; ++j)
-                            if (cb + j < N) out[c * 32 + j] = __uint_as_float(v[j]);
+                            for (int j = 0; j < 32; ++j)
+                                if (cb + j < N) v[j] = __float_as_uint(__fadd_rn(__uint_as_float(v[j]), pb[j]));
+                        }
                     }
+                    if (epi.act == 1) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(gelu_lane(__uint_as_float(v[j])));
+                    }
+                    if (epi.out_hi && full) {
+                        float* ph = epi.out_hi + (int64_t)row * epi.kp_out + cb;
+                        float* pl = epi.out_lo + (int64_t)row * epi.kp_out + cb;
+#pragma unroll
+                        for (int j = 0; j < 32; j += 4) {
+                            float4 h, l;
+                            h.x = rna_tf32_dev(__uint_as_float(v[j]));     l.x = rna_tf32_dev(__uint_as_float(v[j]) - h.x);
+                            h.y = rna_tf32_dev(__uint_as_float(v[j + 1])); l.y = rna_tf32_dev(__uint_as_float(v[j + 1]) - h.y);
+                            h.z = rna_tf32_dev(__uint_as_float(v[j + 2])); l.z = rna_tf32_dev(__uint_as_float(v[j + 2]) - h.z);
+                            h.w = rna_tf32_dev(__uint_as_float(v[j + 3])); l.w = rna_tf32_dev(__uint_as_float(v[j + 3]) - h.w);
+                            *(float4*)(ph + j) = h;
+                            *(float4*)(pl + j) = l;
+                        }
+                    }
+                }
+                if (vec && cb + 32 <= N) {
+#pragma unroll
+                    for (int j = 0; j < 32; j += 4)
+                        *(float4*)(out + c * 32 + j) = make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]),
+                                                                   __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (cb + j < N) out[c * 32 + j] = __uint_as_float(v[j]);
                 }
             }
             tc_fence_before();
@@ -437,8 +496,8 @@ extern "C" int mcu_matmul_tc_supported(void) {
 
 extern "C" size_t mcu_matmul_tc_scratch_bytes(int64_t M, int64_t K, int64_t N) { return layout(M, K, N).total; }
 
-extern "C" int mcu_launch_matmul_tc(float* r, const float* x, const float* y, int64_t M, int64_t K, int64_t N,
-                                    void* scratch, int* status, cudaStream_t st) {
+extern "C" int mcu_launch_matmul_tc_ex(float* r, const float* x, const float* y, int64_t M, int64_t K, int64_t N,
+                                       void* scratch, int* status, cudaStream_t st, const mcu_tc_epilogue* ep) {
     if (M <= 0 || N <= 0) return (int)cudaSuccess;
     if (M >= (1ll << 31) || N >= (1ll << 31) || K >= (1ll << 21) || !scratch) return (int)cudaErrorInvalidValue;
     const Layout l = layout(M, K, N);
@@ -447,11 +506,17 @@ extern "C" int mcu_launch_matmul_tc(float* r, const float* x, const float* y, in
     float* xlo = (float*)(base + l.xlo);
     float* yhi = (float*)(base + l.yhi);
     float* ylo = (float*)(base + l.ylo);
-    {
+    const bool presplit = ep && ep->a_hi && ep->a_lo;
+    if (presplit) {
+        xhi = (float*)ep->a_hi;
+        xlo = (float*)ep->a_lo;
+    } else {
         int64_t n = M * (l.kp / 4);
         int64_t g = (n + 255) / 256;
         if (g > 8 * sm_count()) g = 8 * sm_count();
         split_rows<<<(unsigned)g, 256, 0, st>>>(x, xhi, xlo, M, K, l.kp);
+    }
+    {
         dim3 grid((unsigned)((N + 31) / 32), (unsigned)(l.kp / 32));
         split_cols_t<<<grid, 256, 0, st>>>(y, yhi, ylo, K, N, l.kp);
     }
@@ -460,11 +525,31 @@ extern "C" int mcu_launch_matmul_tc(float* r, const float* x, const float* y, in
         !make_map(&myh, yhi, N, l.kp, kBN) || !make_map(&myl, ylo, N, l.kp, kBN))
         return (int)cudaErrorInvalidValue;
     using C = Cfg<kBN, kStages>;
-    auto kern = gemm_3xtf32<kBN, kStages>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-    if (e != cudaSuccess) return (int)e;
     const int64_t tiles = ((M + BM - 1) / BM) * ((N + kBN - 1) / kBN);
     const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
-    kern<<<grid, kThreads, C::SMEM, st>>>(mxh, mxl, myh, myl, r, (int)M, (int)N, (int)l.kp, (int64_t)N, status);
+    Epi epi{};
+    const bool fused = ep && (ep->bias || ep->act || ep->out_hi);
+    if (fused) {
+        if (ep->out_hi && (N % 32 != 0 || ep->kp_out != round_up(N, BK))) return (int)cudaErrorInvalidValue;
+        epi.bias = ep->bias;
+        epi.out_hi = ep->out_hi;
+        epi.out_lo = ep->out_lo;
+        epi.kp_out = ep->kp_out;
+        epi.act = ep->act;
+        auto kern = gemm_3xtf32<kBN, kStages, true>;
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+        if (e != cudaSuccess) return (int)e;
+        kern<<<grid, kThreads, C::SMEM, st>>>(mxh, mxl, myh, myl, r, (int)M, (int)N, (int)l.kp, (int64_t)N, status, epi);
+    } else {
+        auto kern = gemm_3xtf32<kBN, kStages, false>;
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+        if (e != cudaSuccess) return (int)e;
+        kern<<<grid, kThreads, C::SMEM, st>>>(mxh, mxl, myh, myl, r, (int)M, (int)N, (int)l.kp, (int64_t)N, status, epi);
+    }
     return (int)cudaGetLastError();
+}
+
+extern "C" int mcu_launch_matmul_tc(float* r, const float* x, const float* y, int64_t M, int64_t K, int64_t N,
+                                    void* scratch, int* status, cudaStream_t st) {
+    return mcu_launch_matmul_tc_ex(r, x, y, M, K, N, scratch, status, st, nullptr);
 }

@@ -8,11 +8,10 @@
 // block over the block partials), so results are deterministic run to run.
 //
 // Row reductions and the normalised row softmax are extensions with the same
-// arithmetic per row.  The softmax keeps a whole row on chip: a thread-block
-// cluster of 1..8 CTAs splits the row, each CTA holds its slice in shared
-// memory, and the row max and the double sum are combined across the cluster
-// through distributed shared memory, so HBM sees one read and one write per
-// element (8 B/elem) and exp is evaluated once.
+// arithmetic per row.  The softmax keeps a whole row on chip (registers of one
+// warp, or of a thread-block cluster of up to 16 CTAs that combine the row max
+// and the double sum through distributed shared memory), so HBM sees one read
+// and one write per element (8 B/elem) and exp is evaluated once.
 #include <cuda_runtime.h>
 #include <cooperative_groups.h>
 #include <cstdint>
@@ -231,16 +230,106 @@ cudaError_t launch_rows_op(float* r, const float* x, int64_t rows, int64_t cols,
 }
 
 // ----------------------------------------------------------- row softmax ---
+//
+// Rows stay in registers between the three phases (max, exp + double sum,
+// divide), so HBM sees one read and one write per element.  Short rows
+// (<= 2048) get one warp each; longer rows are split into slices of 16384
+// elements, one 256-thread CTA per slice, and the slices of a row form a
+// thread-block cluster that combines the row max and sum through distributed
+// shared memory.
 
-constexpr int kSoftmaxThreads = 512;
+constexpr int kWarpRowMax = 2048;  // rows up to this length get one warp (16 float4 per lane at most)
+constexpr int kSliceThreads = 256;
+constexpr int kSliceVec = 16;     // float4 per thread: 16384 elements per CTA
+constexpr int kSlice = kSliceThreads * 4 * kSliceVec;
 
-// A cluster of C CTAs owns one row; CTA k keeps columns [k*chunk, (k+1)*chunk)
-// in shared memory.  Phase 1: row max.  Phase 2: e = exp(x - max) (reference
-// lane/tail split), kept in shared memory, with a double sum.  Phase 3: e/sum.
-__global__ void __launch_bounds__(kSoftmaxThreads) softmax_rows_cluster(float* __restrict__ r,
-                                                                        const float* __restrict__ x, uint32_t cols,
-                                                                        uint32_t chunk) {
-    extern __shared__ __align__(16) float sm[];
+// The reference's scalar tail calls libm expf; kept out of line so the common
+// vector-lane path is never if-converted into evaluating it.
+__device__ __noinline__ float exp_tail(float t) { return (float)exp((double)t); }
+
+__device__ __forceinline__ float softmax_exp(float t, uint32_t c, uint32_t vec_end) {
+    if (c < vec_end) return sse_expf(t);
+    return exp_tail(t);
+}
+
+__device__ __forceinline__ float4 neg_inf4() { return make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY); }
+__device__ __forceinline__ float max4(float4 v) { return fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)); }
+
+// e = exp(v - m) per component (reference lane/tail split by column), zero past the row end.
+__device__ __forceinline__ float4 exp4(float4 v, float m, uint32_t c, uint32_t cols, uint32_t vec_end, double& s) {
+    float4 e;
+    if (c + 3 < vec_end) {  // all four are vector lanes
+        e.x = sse_expf(fs(v.x, m));
+        e.y = sse_expf(fs(v.y, m));
+        e.z = sse_expf(fs(v.z, m));
+        e.w = sse_expf(fs(v.w, m));
+        s += (double)e.x + (double)e.y + (double)e.z + (double)e.w;
+        return e;
+    }
+    e.x = c < cols ? softmax_exp(fs(v.x, m), c, vec_end) : 0.0f;
+    e.y = c + 1 < cols ? softmax_exp(fs(v.y, m), c + 1, vec_end) : 0.0f;
+    e.z = c + 2 < cols ? softmax_exp(fs(v.z, m), c + 2, vec_end) : 0.0f;
+    e.w = c + 3 < cols ? softmax_exp(fs(v.w, m), c + 3, vec_end) : 0.0f;
+    s += (double)e.x + (double)e.y + (double)e.z + (double)e.w;
+    return e;
+}
+
+__device__ __forceinline__ float4 div4(float4 e, float d) {
+    return make_float4(__fdiv_rn(e.x, d), __fdiv_rn(e.y, d), __fdiv_rn(e.z, d), __fdiv_rn(e.w, d));
+}
+
+// Loads 4 consecutive elements starting at column c (c % 4 == 0 on the vector path).
+__device__ __forceinline__ float4 load4(const float* px, uint32_t c, uint32_t cols, bool vec) {
+    if (vec) return c < cols ? __ldcs((const float4*)(px + c)) : neg_inf4();
+    float4 t;
+    t.x = c < cols ? px[c] : -INFINITY;
+    t.y = c + 1 < cols ? px[c + 1] : -INFINITY;
+    t.z = c + 2 < cols ? px[c + 2] : -INFINITY;
+    t.w = c + 3 < cols ? px[c + 3] : -INFINITY;
+    return t;
+}
+
+__device__ __forceinline__ void store4(float* pr, uint32_t c, uint32_t cols, bool vec, float4 v) {
+    if (vec) {
+        if (c < cols) __stcs((float4*)(pr + c), v);
+        return;
+    }
+    if (c < cols) pr[c] = v.x;
+    if (c + 1 < cols) pr[c + 1] = v.y;
+    if (c + 2 < cols) pr[c + 2] = v.z;
+    if (c + 3 < cols) pr[c + 3] = v.w;
+}
+
+// One warp per row; lane holds columns 4*(lane + 32*i) .. +3.
+template <int V>
+__global__ void __launch_bounds__(256) softmax_rows_warp(float* __restrict__ r, const float* __restrict__ x,
+                                                         uint64_t rows, uint32_t cols) {
+    const int lane = threadIdx.x & 31;
+    const uint64_t nw = ((uint64_t)gridDim.x * blockDim.x) >> 5;
+    const uint32_t vec_end = cols & ~3u;
+    for (uint64_t row = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < rows; row += nw) {
+        const float* px = x + row * cols;
+        float* pr = r + row * cols;
+        const bool vec = (cols % 4 == 0) && ((((uintptr_t)px) | ((uintptr_t)pr)) & 15) == 0;
+        float4 v[V];
+#pragma unroll
+        for (int i = 0; i < V; ++i) v[i] = load4(px, (uint32_t)(lane + 32 * i) * 4, cols, vec);
+        float m = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < V; ++i) m = fmaxf(m, max4(v[i]));
+        m = warp_max(m);
+        double s = 0.0;
+#pragma unroll
+        for (int i = 0; i < V; ++i) v[i] = exp4(v[i], m, (uint32_t)(lane + 32 * i) * 4, cols, vec_end, s);
+        const float fsum = (float)warp_sum(s);
+#pragma unroll
+        for (int i = 0; i < V; ++i) store4(pr, (uint32_t)(lane + 32 * i) * 4, cols, vec, div4(v[i], fsum));
+    }
+}
+
+// One CTA per 16384-element slice; the cluster spans the row.
+__global__ void __launch_bounds__(kSliceThreads) softmax_rows_slices(float* __restrict__ r,
+                                                                     const float* __restrict__ x, uint32_t cols) {
     __shared__ float sh_max[32];
     __shared__ double sh_sum[32];
     __shared__ float slot_max;
@@ -249,61 +338,40 @@ __global__ void __launch_bounds__(kSoftmaxThreads) softmax_rows_cluster(float* _
     const uint32_t crank = cluster.block_rank();
     const uint32_t csize = cluster.num_blocks();
     const uint64_t row = blockIdx.x / csize;
-    const uint32_t c0 = crank * chunk;
-    const uint32_t n = (c0 + chunk <= cols) ? chunk : (cols > c0 ? cols - c0 : 0);
-    const float* px = x + row * cols + c0;
-    float* pr = r + row * cols + c0;
+    const uint32_t c0 = crank * (uint32_t)kSlice;
+    const float* px = x + row * cols;
+    float* pr = r + row * cols;
     const uint32_t vec_end = cols & ~3u;
-    const bool vec = (n % 4 == 0) && (cols % 4 == 0) && ((((uintptr_t)px) | ((uintptr_t)pr)) & 15) == 0;
-
+    const bool vec = (cols % 4 == 0) && ((((uintptr_t)px) | ((uintptr_t)pr)) & 15) == 0;
+    float4 v[kSliceVec];
+#pragma unroll
+    for (int i = 0; i < kSliceVec; ++i) v[i] = load4(px, c0 + (uint32_t)(threadIdx.x + kSliceThreads * i) * 4, cols, vec);
     float m = -INFINITY;
-    if (vec) {
-        for (uint32_t c = threadIdx.x; c < n / 4; c += kSoftmaxThreads) {
-            float4 v = __ldcs((const float4*)px + c);
-            ((float4*)sm)[c] = v;
-            m = fmaxf(m, fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)));
-        }
-    } else {
-        for (uint32_t c = threadIdx.x; c < n; c += kSoftmaxThreads) {
-            float v = px[c];
-            sm[c] = v;
-            m = fmaxf(m, v);
-        }
-    }
+#pragma unroll
+    for (int i = 0; i < kSliceVec; ++i) m = fmaxf(m, max4(v[i]));
     m = block_combine(m, WMax(), sh_max, -(float)INFINITY);
     if (threadIdx.x == 0) slot_max = m;
     cluster.sync();
     float gm = -INFINITY;
     for (uint32_t k = 0; k < csize; ++k) gm = fmaxf(gm, *cluster.map_shared_rank(&slot_max, k));
-
     double s = 0.0;
-    for (uint32_t c = threadIdx.x; c < n; c += kSoftmaxThreads) {
-        float t = fs(sm[c], gm);
-        float e = (c0 + c < vec_end) ? sse_expf(t) : (float)exp((double)t);
-        sm[c] = e;
-        s += (double)e;
-    }
+#pragma unroll
+    for (int i = 0; i < kSliceVec; ++i)
+        v[i] = exp4(v[i], gm, c0 + (uint32_t)(threadIdx.x + kSliceThreads * i) * 4, cols, vec_end, s);
     s = block_combine(s, WSum(), sh_sum, 0.0);
     if (threadIdx.x == 0) slot_sum = s;
     cluster.sync();
     double gs = 0.0;
     for (uint32_t k = 0; k < csize; ++k) gs += *cluster.map_shared_rank(&slot_sum, k);
     const float fsum = (float)gs;
-
-    if (vec) {
-        for (uint32_t c = threadIdx.x; c < n / 4; c += kSoftmaxThreads) {
-            float4 v = ((float4*)sm)[c];
-            v.x = __fdiv_rn(v.x, fsum); v.y = __fdiv_rn(v.y, fsum);
-            v.z = __fdiv_rn(v.z, fsum); v.w = __fdiv_rn(v.w, fsum);
-            __stcs((float4*)pr + c, v);
-        }
-    } else {
-        for (uint32_t c = threadIdx.x; c < n; c += kSoftmaxThreads) pr[c] = __fdiv_rn(sm[c], fsum);
-    }
+#pragma unroll
+    for (int i = 0; i < kSliceVec; ++i)
+        store4(pr, c0 + (uint32_t)(threadIdx.x + kSliceThreads * i) * 4, cols, vec, div4(v[i], fsum));
     cluster.sync();  // peers may still read this CTA's slots
 }
 
-// Rows too long for a cluster's shared memory: three passes from HBM.
+// Rows longer than 16 slices: three passes from HBM.
+constexpr int kSoftmaxThreads = 512;
 __global__ void __launch_bounds__(kSoftmaxThreads) softmax_rows_global(float* __restrict__ r,
                                                                        const float* __restrict__ x, uint64_t rows,
                                                                        uint32_t cols) {
@@ -317,17 +385,11 @@ __global__ void __launch_bounds__(kSoftmaxThreads) softmax_rows_global(float* __
         for (uint32_t c = threadIdx.x; c < cols; c += kSoftmaxThreads) m = fmaxf(m, px[c]);
         m = block_combine(m, WMax(), sh_max, -(float)INFINITY);
         double s = 0.0;
-        for (uint32_t c = threadIdx.x; c < cols; c += kSoftmaxThreads) {
-            float t = fs(px[c], m);
-            s += (double)((c < vec_end) ? sse_expf(t) : (float)exp((double)t));
-        }
+        for (uint32_t c = threadIdx.x; c < cols; c += kSoftmaxThreads) s += (double)softmax_exp(fs(px[c], m), c, vec_end);
         s = block_combine(s, WSum(), sh_sum, 0.0);
         const float fsum = (float)s;
-        for (uint32_t c = threadIdx.x; c < cols; c += kSoftmaxThreads) {
-            float t = fs(px[c], m);
-            float e = (c < vec_end) ? sse_expf(t) : (float)exp((double)t);
-            pr[c] = __fdiv_rn(e, fsum);
-        }
+        for (uint32_t c = threadIdx.x; c < cols; c += kSoftmaxThreads)
+            pr[c] = __fdiv_rn(softmax_exp(fs(px[c], m), c, vec_end), fsum);
         __syncthreads();
     }
 }
@@ -383,34 +445,39 @@ extern "C" int mcu_launch_reduce_rows(int op, float* r, const float* x, int64_t 
 extern "C" int mcu_launch_softmax_rows(float* r, const float* x, int64_t rows, int64_t cols, cudaStream_t st) {
     if (rows <= 0 || cols <= 0) return (int)cudaSuccess;
     if (cols >= (1ll << 31) || rows >= (1ll << 31)) return (int)cudaErrorInvalidValue;
-    const size_t kSlice = 32 * 1024;        // preferred bytes of row per CTA
-    const size_t kSliceMax = 192 * 1024;    // hard cap per CTA
-    int csize = 1;
-    size_t bytes = (size_t)cols * 4;
-    while (csize < 8 && (bytes + csize - 1) / csize > kSlice) csize *= 2;
-    size_t chunk = ((size_t)cols + csize - 1) / csize;
-    chunk = (chunk + 3) & ~(size_t)3;
-    if (chunk * 4 > kSliceMax || (uint64_t)rows * csize >= (1ull << 31)) {
-        int g = sm_count() * 4;
-        softmax_rows_global<<<(unsigned)(rows < g ? rows : g), kSoftmaxThreads, 0, st>>>(r, x, (uint64_t)rows,
-                                                                                       (uint32_t)cols);
+    if (cols <= kWarpRowMax) {
+        uint64_t g = ((uint64_t)rows * 32 + 255) / 256;
+        const uint64_t cap = (uint64_t)sm_count() * 16;
+        const unsigned grid = (unsigned)(g < cap ? g : cap);
+        if (cols <= 512) softmax_rows_warp<4><<<grid, 256, 0, st>>>(r, x, (uint64_t)rows, (uint32_t)cols);
+        else if (cols <= 1024) softmax_rows_warp<8><<<grid, 256, 0, st>>>(r, x, (uint64_t)rows, (uint32_t)cols);
+        else softmax_rows_warp<16><<<grid, 256, 0, st>>>(r, x, (uint64_t)rows, (uint32_t)cols);
         return (int)cudaGetLastError();
     }
-    size_t smem = chunk * 4;
-    cudaError_t e = cudaFuncSetAttribute(softmax_rows_cluster, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)kSliceMax);
-    if (e != cudaSuccess) return (int)e;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)(rows * csize));
-    cfg.blockDim = dim3(kSoftmaxThreads);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = (unsigned)csize;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return (int)cudaLaunchKernelEx(&cfg, softmax_rows_cluster, r, x, (uint32_t)cols, (uint32_t)chunk);
+    const int64_t csize = (cols + kSlice - 1) / kSlice;
+    if (csize <= 16 && rows * csize < (1ll << 31)) {
+        if (csize > 8) {
+            cudaError_t e = cudaFuncSetAttribute(softmax_rows_slices, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+            if (e != cudaSuccess) return (int)e;
+        }
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)(rows * csize));
+        cfg.blockDim = dim3(kSliceThreads);
+        cfg.dynamicSmemBytes = 0;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = (unsigned)csize;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        cudaError_t e = cudaLaunchKernelEx(&cfg, softmax_rows_slices, r, x, (uint32_t)cols);
+        if (e == cudaSuccess) return (int)cudaSuccess;
+        cudaGetLastError();  // cluster shape not schedulable here: use the three-pass kernel
+    }
+    int g = sm_count() * 4;
+    softmax_rows_global<<<(unsigned)(rows < g ? rows : g), kSoftmaxThreads, 0, st>>>(r, x, (uint64_t)rows,
+                                                                                   (uint32_t)cols);
+    return (int)cudaGetLastError();
 }

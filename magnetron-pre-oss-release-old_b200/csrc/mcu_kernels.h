@@ -51,6 +51,23 @@ int mcu_launch_matmul_tc(float* r, const float* x, const float* y, int64_t M, in
                          void* scratch, int* status, cudaStream_t st);
 int mcu_matmul_tc_supported(void);
 
+/* Fused dense-layer epilogue for the tensor-core GEMM: out = act(X Y + bias) with
+ * bias at the result's row-major index (or NULL), act 0 = none, 1 = GELU; when
+ * out_hi/out_lo are set the tf32 hi/lo split of out is also written in the
+ * [M][kp_out] layout the next product reads (kp_out = N rounded up to 32, N % 32 == 0).
+ * a_hi/a_lo, when set, are X already split in that layout (no split pass). */
+typedef struct mcu_tc_epilogue {
+    const float* a_hi;
+    const float* a_lo;
+    const float* bias;
+    float* out_hi;
+    float* out_lo;
+    int64_t kp_out;
+    int act;
+} mcu_tc_epilogue;
+int mcu_launch_matmul_tc_ex(float* r, const float* x, const float* y, int64_t M, int64_t K, int64_t N,
+                            void* scratch, int* status, cudaStream_t st, const mcu_tc_epilogue* ep);
+
 #ifdef __cplusplus
 }
 #endif

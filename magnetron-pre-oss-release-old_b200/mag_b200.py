@@ -110,6 +110,7 @@ def load_library(path: str = LIB_PATH):
         "mag_cuda_last_error": ([vp], C.c_int),
         "mag_cuda_memory_in_use": ([vp], C.c_size_t),
         "mag_cuda_graph_exec": ([vp, vp], C.c_int),
+        "mag_cuda_graph_exec_fused": ([vp, vp], C.c_int),
         "mag_cuda_graph_release": ([vp, vp], C.c_int),
         "mag_cuda_exec_node": ([vp, vp], C.c_int),
         "mag_cuda_unary_f32": ([vp, C.c_int, vp, vp, i64, i64, i64, i64, C.c_float], C.c_int),
@@ -310,8 +311,9 @@ class Device:
     def exec(self, r: Tensor):
         self.dev.eager_exec_fwd(self.p, r.ptr)
 
-    def graph_exec(self, root: Tensor):
-        check(self.L.mag_cuda_graph_exec(self.p, root.ptr), "graph_exec")
+    def graph_exec(self, root: Tensor, fused: bool = False):
+        fn = self.L.mag_cuda_graph_exec_fused if fused else self.L.mag_cuda_graph_exec
+        check(fn(self.p, root.ptr), "graph_exec")
 
     def graph_release(self, root: Tensor):
         self.L.mag_cuda_graph_release(self.p, root.ptr)

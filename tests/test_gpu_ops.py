@@ -322,3 +322,56 @@ def test_matmul_tensor_core_large_k_sampled():
     rows = o.matmul_rows(x, y, 17, 3, k, n)
     ref_err = np.abs(rows - got.reshape(m, n)[17:20].reshape(-1))
     assert float(ref_err.max()) <= 2e-4 * float(np.abs(rows).max())
+
+
+def _build_mlp(dev, rows, dims, inplace_gelu=True):
+    X = dev.tensor((rows, dims[0]))
+    Ws, Bs = [], []
+    dev.eager = False
+    try:
+        h = X
+        for i in range(len(dims) - 1):
+            W = dev.tensor((dims[i], dims[i + 1]))
+            B = dev.tensor((rows, dims[i + 1]))
+            Ws.append(W)
+            Bs.append(B)
+            h = dev.op("MATMUL", h, W)
+            h = dev.op("ADD", h, B)
+            if i < len(dims) - 2:
+                h = dev.op("GELU", h, inplace=inplace_gelu)
+    finally:
+        dev.eager = True
+    return X, Ws, Bs, h
+
+
+@pytest.mark.parametrize("inplace", [True, False])
+def test_fused_graph_matches_unfused_bitwise(inplace):
+    """Dense layers fused into the GEMM epilogue give the same bits as the op-by-op graph."""
+    dev = device()
+    o = oracle()
+    rows, dims = 256, [512, 384, 256, 96]
+    X, Ws, Bs, root = _build_mlp(dev, rows, dims, inplace)
+    s = o.stream(9100)
+    X.write(s.uniform(rows * dims[0], -1, 1))
+    for W, B, (a, b) in zip(Ws, Bs, zip(dims[:-1], dims[1:])):
+        W.write(s.normal(a * b, 0.0, (2.0 / a) ** 0.5))
+        B.write(s.uniform(rows * b, -0.1, 0.1))
+    MB.check(dev.L.mag_cuda_set_matmul_mode(dev.p, 2), "tc")
+    try:
+        dev.graph_exec(root)
+        plain = root.read()
+        dev.graph_exec(root, fused=True)
+        fused = root.read()
+        x2 = s.uniform(rows * dims[0], -1, 1)  # replay with new input data
+        X.write(x2)
+        dev.graph_exec(root, fused=True)
+        fused2 = root.read()
+        dev.graph_exec(root)
+        plain2 = root.read()
+    finally:
+        dev.L.mag_cuda_set_matmul_mode(dev.p, 0)
+        dev.graph_release(root)
+    assert dev.L.mag_cuda_synchronize(dev.p) == 0
+    assert bits_equal(fused, plain).all()
+    assert bits_equal(fused2, plain2).all()
+    assert not bits_equal(fused, fused2).all()
