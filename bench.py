@@ -289,7 +289,8 @@ def run_ours(args):
     if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
-    rows = GLOBAL_BATCH // world
+    import dp
+    _, rows = dp.shard_rows(GLOBAL_BATCH, world, rank)
     dev = MB.Device()
     stream = torch.cuda.ExternalStream(dev.stream, device=torch.device("cuda", local))
 
@@ -316,7 +317,7 @@ def run_ours(args):
     z = dev.op("ADD", z, Bo)
     dev.eager = True
     P = dev.tensor((rows * D_OUT,))
-    gathered = torch.empty(world * rows * D_OUT, dtype=torch.float32, device=f"cuda:{local}") if world > 1 else None
+    gathered = {}
 
     # ---- inputs in pinned host memory
     xh = torch.randn(rows * D_IN, generator=torch.Generator().manual_seed(99 + rank)).pin_memory()
@@ -330,7 +331,7 @@ def run_ours(args):
         if world > 1:
             with torch.cuda.stream(stream):
                 src = torch.as_tensor(_CudaArray(P.data_ptr, rows * D_OUT, dev.stream), device=f"cuda:{local}")
-                dist.all_gather_into_tensor(gathered, src)
+                gathered["out"] = dp.gather_rows(src, GLOBAL_BATCH, D_OUT, world, rank)
 
     def e2e_step():
         X.write(xh.numpy())  # pinned -> straight DMA
@@ -338,7 +339,7 @@ def run_ours(args):
         if rank == 0:
             with torch.cuda.stream(stream):
                 if world > 1:
-                    out_h.copy_(gathered, non_blocking=True)
+                    out_h.copy_(gathered["out"], non_blocking=True)
                 else:
                     out_h.copy_(torch.as_tensor(_CudaArray(P.data_ptr, rows * D_OUT, dev.stream),
                                                 device=f"cuda:{local}"), non_blocking=True)
