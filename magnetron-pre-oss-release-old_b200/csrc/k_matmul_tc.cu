@@ -33,7 +33,7 @@ namespace {
 
 constexpr int BM = 128;          // UMMA M (one CTA, TMEM lanes 0..127)
 constexpr int BK = 32;           // f32 per 128-byte swizzle row
-constexpr int kEpiWarps = 4;
+constexpr int kEpiWarps = 8;   // two per TMEM lane quadrant, each owning half of the tile's columns
 constexpr int kThreads = 32 * (2 + kEpiWarps);
 constexpr uint32_t kWaitLimit = 1u << 22;
 
@@ -197,10 +197,11 @@ __device__ __forceinline__ float gelu_lane(float x) {
 }
 
 template <int BN, int STAGES, bool FUSED>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __maxnreg__(168)
     gemm_3xtf32(const __grid_constant__ CUtensorMap map_xhi, const __grid_constant__ CUtensorMap map_xlo,
                 const __grid_constant__ CUtensorMap map_yhi, const __grid_constant__ CUtensorMap map_ylo,
-                float* __restrict__ r, int M, int N, int Kp, int64_t ldr, int* status, const Epi epi) {
+                float* __restrict__ r, int M, int N, int Kp, int64_t ldr, int* status, const Epi epi,
+                int seg_kb) {
     using C = Cfg<BN, STAGES>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -267,105 +268,123 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     } else if (warp == 1) {
-        if (lane == 0) {  // ---- MMA issuer
+        if (lane == 0) {  // ---- MMA issuer: one TMEM accumulator per K segment, two in flight
             constexpr uint32_t idesc = idesc_tf32(BN);
-            uint32_t it = 0, tc = 0;
-            for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++tc) {
-                const uint32_t a = tc & 1, around = tc >> 1;
-                if (!mbar_wait(&acc_empty[a], (around & 1) ^ 1, ab, 2)) goto done;
-                tc_fence_after();
-                const uint32_t d = tmem_base + a * BN;
-                for (int kb = 0; kb < nk; ++kb, ++it) {
-                    const uint32_t s = it % STAGES, round = it / STAGES;
-                    if (!mbar_wait(&full[s], round & 1, ab, 3)) goto done;
+            uint32_t it = 0, gseg = 0;
+            for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+                for (int kb0 = 0; kb0 < nk; kb0 += seg_kb, ++gseg) {
+                    const uint32_t b = gseg & 1, bround = gseg >> 1;
+                    if (!mbar_wait(&acc_empty[b], (bround & 1) ^ 1, ab, 2)) goto done;
                     tc_fence_after();
-                    const uint32_t base = smem_u32(ring + s * C::STAGE_BYTES);
+                    const uint32_t d = tmem_base + b * BN;
+                    const int kb1 = min(kb0 + seg_kb, nk);
+                    for (int kb = kb0; kb < kb1; ++kb, ++it) {
+                        const uint32_t s = it % STAGES, round = it / STAGES;
+                        if (!mbar_wait(&full[s], round & 1, ab, 3)) goto done;
+                        tc_fence_after();
+                        const uint32_t base = smem_u32(ring + s * C::STAGE_BYTES);
 #pragma unroll
-                    for (int kk = 0; kk < BK / 8; ++kk) {
-                        const uint64_t xhi = sw128_desc(base + kk * 32);
-                        const uint64_t xlo = sw128_desc(base + C::A_BYTES + kk * 32);
-                        const uint64_t yhi = sw128_desc(base + 2 * C::A_BYTES + kk * 32);
-                        const uint64_t ylo = sw128_desc(base + 2 * C::A_BYTES + C::B_BYTES + kk * 32);
-                        umma_tf32(d, xlo, yhi, idesc, (kb | kk) != 0);
-                        umma_tf32(d, xhi, ylo, idesc, 1);
-                        umma_tf32(d, xhi, yhi, idesc, 1);
+                        for (int kk = 0; kk < BK / 8; ++kk) {
+                            const uint64_t xhi = sw128_desc(base + kk * 32);
+                            const uint64_t xlo = sw128_desc(base + C::A_BYTES + kk * 32);
+                            const uint64_t yhi = sw128_desc(base + 2 * C::A_BYTES + kk * 32);
+                            const uint64_t ylo = sw128_desc(base + 2 * C::A_BYTES + C::B_BYTES + kk * 32);
+                            umma_tf32(d, xlo, yhi, idesc, (kb != kb0 || kk != 0) ? 1u : 0u);
+                            umma_tf32(d, xhi, ylo, idesc, 1);
+                            umma_tf32(d, xhi, yhi, idesc, 1);
+                        }
+                        umma_commit(&empty[s]);
                     }
-                    umma_commit(&empty[s]);
+                    umma_commit(&acc_full[b]);
                 }
-                umma_commit(&acc_full[a]);
             }
         }
-    } else {  // ---- epilogue warps: TMEM lanes 32*(warp%4) .. +31
+    } else {  // ---- epilogue warps: TMEM lanes 32*(warp%4) .. +31, columns [h*BN/2, (h+1)*BN/2)
+        constexpr int HC = BN / 2;   // columns per thread
         const int q = warp & 3;
-        uint32_t tc = 0;
-        for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++tc) {
+        const int h = (warp - 2) >> 2;
+        uint32_t gseg = 0;
+        for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
             int mb, nb;
             tile_coords(t, num_m, num_n, mb, nb);
-            const uint32_t a = tc & 1, around = tc >> 1;
-            if (!mbar_wait(&acc_full[a], around & 1, ab, 4)) break;
-            tc_fence_after();
+            // segment sums are added in registers with round-to-nearest
+            float sum[HC];
+            for (int kb0 = 0; kb0 < nk; kb0 += seg_kb, ++gseg) {
+                const uint32_t b = gseg & 1, bround = gseg >> 1;
+                if (!mbar_wait(&acc_full[b], bround & 1, ab, 4)) goto done;
+                tc_fence_after();
+#pragma unroll
+                for (int c = 0; c < HC / 32; ++c) {
+                    uint32_t v[32];
+                    tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + b * BN + h * HC + c * 32, v);
+                    if (kb0 == 0) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) sum[c * 32 + j] = __uint_as_float(v[j]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) sum[c * 32 + j] = __fadd_rn(sum[c * 32 + j], __uint_as_float(v[j]));
+                    }
+                }
+                tc_fence_before();
+                mbar_arrive(&acc_empty[b]);
+            }
             const int row = mb * BM + q * 32 + lane;
-            const int col0 = nb * BN;
-            float* out = r + (int64_t)row * ldr + col0;
-            const bool row_ok = row < M;
+            if (row >= M) continue;
+            const int colh = nb * BN + h * HC;
+            float* out = r + (int64_t)row * ldr + colh;
             const bool vec = ((ldr & 3) == 0) && ((((uintptr_t)r) & 15) == 0);
-#pragma unroll 1
-            for (int c = 0; c < BN / 32; ++c) {
-                uint32_t v[32];
-                tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + a * BN + c * 32, v);
-                const int cb = col0 + c * 32;
-                if (!row_ok) continue;
+#pragma unroll
+            for (int c = 0; c < HC / 32; ++c) {
+                float* v = sum + c * 32;
+                const int cb = colh + c * 32;
+                const bool full = cb + 32 <= N;
                 if constexpr (FUSED) {
-                    const bool full = cb + 32 <= N;
                     if (epi.bias) {
                         const float* pb = epi.bias + (int64_t)row * N + cb;
                         if (full && vec) {
 #pragma unroll
                             for (int j = 0; j < 32; j += 4) {
                                 const float4 b4 = __ldcs((const float4*)(pb + j));
-                                v[j] = __float_as_uint(__fadd_rn(__uint_as_float(v[j]), b4.x));
-                                v[j + 1] = __float_as_uint(__fadd_rn(__uint_as_float(v[j + 1]), b4.y));
-                                v[j + 2] = __float_as_uint(__fadd_rn(__uint_as_float(v[j + 2]), b4.z));
-                                v[j + 3] = __float_as_uint(__fadd_rn(__uint_as_float(v[j + 3]), b4.w));
+                                v[j] = __fadd_rn(v[j], b4.x);
+                                v[j + 1] = __fadd_rn(v[j + 1], b4.y);
+                                v[j + 2] = __fadd_rn(v[j + 2], b4.z);
+                                v[j + 3] = __fadd_rn(v[j + 3], b4.w);
                             }
                         } else {
 #pragma unroll
                             for (int j = 0; j < 32; ++j)
-                                if (cb + j < N) v[j] = __float_as_uint(__fadd_rn(__uint_as_float(v[j]), pb[j]));
+                                if (cb + j < N) v[j] = __fadd_rn(v[j], pb[j]);
                         }
                     }
                     if (epi.act == 1) {
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(gelu_lane(__uint_as_float(v[j])));
+                        for (int j = 0; j < 32; ++j) v[j] = gelu_lane(v[j]);
                     }
                     if (epi.out_hi && full) {
                         float* ph = epi.out_hi + (int64_t)row * epi.kp_out + cb;
                         float* pl = epi.out_lo + (int64_t)row * epi.kp_out + cb;
 #pragma unroll
                         for (int j = 0; j < 32; j += 4) {
-                            float4 h, l;
-                            h.x = rna_tf32_dev(__uint_as_float(v[j]));     l.x = rna_tf32_dev(__uint_as_float(v[j]) - h.x);
-                            h.y = rna_tf32_dev(__uint_as_float(v[j + 1])); l.y = rna_tf32_dev(__uint_as_float(v[j + 1]) - h.y);
-                            h.z = rna_tf32_dev(__uint_as_float(v[j + 2])); l.z = rna_tf32_dev(__uint_as_float(v[j + 2]) - h.z);
-                            h.w = rna_tf32_dev(__uint_as_float(v[j + 3])); l.w = rna_tf32_dev(__uint_as_float(v[j + 3]) - h.w);
-                            *(float4*)(ph + j) = h;
-                            *(float4*)(pl + j) = l;
+                            float4 hh, ll;
+                            hh.x = rna_tf32_dev(v[j]);     ll.x = rna_tf32_dev(v[j] - hh.x);
+                            hh.y = rna_tf32_dev(v[j + 1]); ll.y = rna_tf32_dev(v[j + 1] - hh.y);
+                            hh.z = rna_tf32_dev(v[j + 2]); ll.z = rna_tf32_dev(v[j + 2] - hh.z);
+                            hh.w = rna_tf32_dev(v[j + 3]); ll.w = rna_tf32_dev(v[j + 3] - hh.w);
+                            *(float4*)(ph + j) = hh;
+                            *(float4*)(pl + j) = ll;
                         }
                     }
                 }
-                if (vec && cb + 32 <= N) {
+                if (vec && full) {
 #pragma unroll
                     for (int j = 0; j < 32; j += 4)
-                        *(float4*)(out + c * 32 + j) = make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]),
-                                                                   __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
+                        *(float4*)(out + c * 32 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
                 } else {
 #pragma unroll
                     for (int j = 0; j < 32; ++j)
-                        if (cb + j < N) out[c * 32 + j] = __uint_as_float(v[j]);
+                        if (cb + j < N) out[c * 32 + j] = v[j];
                 }
             }
-            tc_fence_before();
-            mbar_arrive(&acc_empty[a]);
         }
     }
 done:
@@ -487,6 +506,19 @@ Layout layout(int64_t M, int64_t K, int64_t N) {
 constexpr int kBN = 256;
 constexpr int kStages = 2;
 
+// K blocks (of 32) per TMEM accumulation segment.  Tensor-core f32 accumulation
+// truncates; restarting the accumulator every segment and adding segments with
+// round-to-nearest bounds that error by the segment length instead of K.
+int segment_kb() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("MAG_CUDA_TC_SEGMENT");
+        v = (e && *e) ? atoi(e) : 4;
+        if (v <= 0) v = 1 << 30;  // 0: one segment spanning K
+    }
+    return v;
+}
+
 }  // namespace
 
 extern "C" int mcu_matmul_tc_supported(void) {
@@ -539,12 +571,14 @@ extern "C" int mcu_launch_matmul_tc_ex(float* r, const float* x, const float* y,
         auto kern = gemm_3xtf32<kBN, kStages, true>;
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
         if (e != cudaSuccess) return (int)e;
-        kern<<<grid, kThreads, C::SMEM, st>>>(mxh, mxl, myh, myl, r, (int)M, (int)N, (int)l.kp, (int64_t)N, status, epi);
+        kern<<<grid, kThreads, C::SMEM, st>>>(mxh, mxl, myh, myl, r, (int)M, (int)N, (int)l.kp, (int64_t)N, status, epi,
+                                              segment_kb());
     } else {
         auto kern = gemm_3xtf32<kBN, kStages, false>;
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
         if (e != cudaSuccess) return (int)e;
-        kern<<<grid, kThreads, C::SMEM, st>>>(mxh, mxl, myh, myl, r, (int)M, (int)N, (int)l.kp, (int64_t)N, status, epi);
+        kern<<<grid, kThreads, C::SMEM, st>>>(mxh, mxl, myh, myl, r, (int)M, (int)N, (int)l.kp, (int64_t)N, status, epi,
+                                              segment_kb());
     }
     return (int)cudaGetLastError();
 }
