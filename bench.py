@@ -478,7 +478,24 @@ def run_case(args):
     import mag_b200 as MB
     dev = MB.Device()
     n = args.size
-    if args.case == "gemm":
+    if args.case == "layer":
+        # two dense layers of the MLP (rows = --size, 4096 features), fused graph:
+        # layer 1 = GEMM + bias + GELU + operand split, layer 2 reads the split
+        rows = n
+        g = torch.Generator().manual_seed(3)
+        X = dev.tensor((rows, D_IN))
+        W1, W2 = dev.tensor((D_IN, D_HID)), dev.tensor((D_HID, D_HID))
+        B1, B2 = dev.tensor((rows, D_HID)), dev.tensor((rows, D_HID))
+        X.write(torch.randn(rows * D_IN, generator=g).numpy())
+        for W in (W1, W2):
+            W.write((torch.randn(D_IN * D_HID, generator=g) * (2.0 / D_IN) ** 0.5).numpy())
+        dev.eager = False
+        h = dev.op("GELU", dev.op("ADD", dev.op("MATMUL", X, W1), B1), inplace=True)
+        z = dev.op("ADD", dev.op("MATMUL", h, W2), B2)
+        dev.eager = True
+        fn = lambda: dev.L.mag_cuda_graph_exec_fused(dev.p, z.ptr)
+        work, unit = 2 * 2.0 * rows * D_IN * D_HID / 1e12, "TFLOP/s"
+    elif args.case == "gemm":
         MB.check(dev.L.mag_cuda_set_matmul_mode(dev.p, 2), "tc")
         x, y, r = dev.tensor((n * n,)), dev.tensor((n * n,)), dev.tensor((n * n,))
         v = torch.randn(n * n, generator=torch.Generator().manual_seed(3)).numpy()
@@ -702,7 +719,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--case", default=None, choices=["gemm", "add", "sigmoid", "sum", "softmax"],
+    ap.add_argument("--case", default=None, choices=["gemm", "layer", "add", "sigmoid", "sum", "softmax"],
                     help="run one kernel family for a profiler instead of the benchmark")
     ap.add_argument("--size", type=int, default=None)
     ap.add_argument("--sweep-full", action="store_true", help="measure every other BASELINE configuration")
@@ -712,7 +729,7 @@ def main():
         run_sweep_full(args)
         return
     if args.case:
-        args.size = args.size or (8192 if args.case == "gemm" else 1 << 28)
+        args.size = args.size or (8192 if args.case in ("gemm", "layer") else 1 << 28)
         run_case(args)
         return
     if args.warmup < 3:
