@@ -14,8 +14,8 @@
 //   split_rows     X -> Xhi, Xlo     [M][Kp]    (Kp = K rounded up to 32, zero padded)
 //   split_cols_t   Y -> Yhi^T, Ylo^T [N][Kp]    (transposed so both operands are K-major)
 //   gemm_3xtf32    persistent, warp-specialised:
-//     warp 0      TMA producer: 128B-swizzled 128x32 (X) and BNx32 (Y) tiles, hi and lo,
-//                 into a STAGES-deep shared-memory ring (mbarrier complete_tx)
+//     warp 0      TMA producer: 64B-swizzled 128x16 (X) and BNx16 (Y) tiles, hi and lo,
+//                 into a 4-deep shared-memory ring (mbarrier complete_tx)
 //     warp 1      TMEM allocator; lane 0 issues tcgen05.mma kind::tf32 (M=128, N=BN, K=8),
 //                 three per k-step, and tcgen05.commit to free ring slots / publish tiles
 //     warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns -> registers -> global,
@@ -32,7 +32,8 @@
 namespace {
 
 constexpr int BM = 128;          // UMMA M (one CTA, TMEM lanes 0..127)
-constexpr int BK = 32;           // f32 per 128-byte swizzle row
+constexpr int BK = 16;           // f32 per 64-byte swizzle row (one ring stage holds K = 16)
+constexpr int KPAD = 32;         // K padding of the split operands
 constexpr int kEpiWarps = 8;   // two per TMEM lane quadrant, each owning half of the tile's columns
 constexpr int kThreads = 32 * (2 + kEpiWarps);
 constexpr uint32_t kWaitLimit = 1u << 22;
@@ -118,14 +119,16 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
                  : "memory");
 }
 
-// Shared-memory matrix descriptor: K-major, 128B swizzle, 8-row atoms 1024 B apart.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+// Shared-memory matrix descriptor: K-major rows of BK*4 bytes, swizzled (64B
+// or 128B), 8-row atoms 8*BK*4 bytes apart.
+__device__ __forceinline__ uint64_t sw_desc(uint32_t saddr) {
+    constexpr uint32_t row_bytes = BK * 4;
     uint64_t d = 0;
     d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
-    d |= (uint64_t)1 << 16;             // leading byte offset (unused for swizzled K-major)
-    d |= (uint64_t)(1024 >> 4) << 32;   // stride byte offset between 8-row atoms
-    d |= (uint64_t)1 << 46;             // descriptor version for tcgen05
-    d |= (uint64_t)2 << 61;             // SWIZZLE_128B
+    d |= (uint64_t)1 << 16;                         // leading byte offset (unused for swizzled K-major)
+    d |= (uint64_t)((8 * row_bytes) >> 4) << 32;    // stride byte offset between 8-row atoms
+    d |= (uint64_t)1 << 46;                         // descriptor version for tcgen05
+    d |= (uint64_t)(row_bytes == 128 ? 2 : 4) << 61; // SWIZZLE_128B or SWIZZLE_64B
     return d;
 }
 
@@ -285,10 +288,10 @@ __global__ void __maxnreg__(168)
                         const uint32_t base = smem_u32(ring + s * C::STAGE_BYTES);
 #pragma unroll
                         for (int kk = 0; kk < BK / 8; ++kk) {
-                            const uint64_t xhi = sw128_desc(base + kk * 32);
-                            const uint64_t xlo = sw128_desc(base + C::A_BYTES + kk * 32);
-                            const uint64_t yhi = sw128_desc(base + 2 * C::A_BYTES + kk * 32);
-                            const uint64_t ylo = sw128_desc(base + 2 * C::A_BYTES + C::B_BYTES + kk * 32);
+                            const uint64_t xhi = sw_desc(base + kk * 32);
+                            const uint64_t xlo = sw_desc(base + C::A_BYTES + kk * 32);
+                            const uint64_t yhi = sw_desc(base + 2 * C::A_BYTES + kk * 32);
+                            const uint64_t ylo = sw_desc(base + 2 * C::A_BYTES + C::B_BYTES + kk * 32);
                             umma_tf32(d, xlo, yhi, idesc, (kb != kb0 || kk != 0) ? 1u : 0u);
                             umma_tf32(d, xhi, ylo, idesc, 1);
                             umma_tf32(d, xhi, yhi, idesc, 1);
@@ -479,8 +482,8 @@ bool make_map(CUtensorMap* m, const float* base, int64_t rows, int64_t kp, int b
     cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void*)base, dims, strides, box, estr,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, BK == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
 
@@ -493,7 +496,7 @@ struct Layout {
 
 Layout layout(int64_t M, int64_t K, int64_t N) {
     Layout l;
-    l.kp = round_up(K < 1 ? 1 : K, BK);
+    l.kp = round_up(K < 1 ? 1 : K, KPAD);
     size_t xs = (size_t)round_up(M * l.kp * 4, 1024), ys = (size_t)round_up(N * l.kp * 4, 1024);
     l.xhi = 0;
     l.xlo = xs;
@@ -504,17 +507,18 @@ Layout layout(int64_t M, int64_t K, int64_t N) {
 }
 
 constexpr int kBN = 256;
-constexpr int kStages = 2;
+constexpr int kStages = 4;
 
-// K blocks (of 32) per TMEM accumulation segment.  Tensor-core f32 accumulation
-// truncates; restarting the accumulator every segment and adding segments with
-// round-to-nearest bounds that error by the segment length instead of K.
+// K per TMEM accumulation segment (MAG_CUDA_TC_SEGMENT, default 256).  Tensor-core
+// f32 accumulation truncates; restarting the accumulator every segment and
+// adding segments with round-to-nearest bounds that error by the segment length
+// instead of K.  0 = one segment spanning K.
 int segment_kb() {
     static int v = -1;
     if (v < 0) {
         const char* e = getenv("MAG_CUDA_TC_SEGMENT");
-        v = (e && *e) ? atoi(e) : 4;
-        if (v <= 0) v = 1 << 30;  // 0: one segment spanning K
+        int k = (e && *e) ? atoi(e) : 256;
+        v = k <= 0 ? (1 << 30) : (k + BK - 1) / BK;
     }
     return v;
 }
@@ -562,7 +566,7 @@ extern "C" int mcu_launch_matmul_tc_ex(float* r, const float* x, const float* y,
     Epi epi{};
     const bool fused = ep && (ep->bias || ep->act || ep->out_hi);
     if (fused) {
-        if (ep->out_hi && (N % 32 != 0 || ep->kp_out != round_up(N, BK))) return (int)cudaErrorInvalidValue;
+        if (ep->out_hi && (N % 32 != 0 || ep->kp_out != round_up(N, KPAD))) return (int)cudaErrorInvalidValue;
         epi.bias = ep->bias;
         epi.out_hi = ep->out_hi;
         epi.out_lo = ep->out_lo;
