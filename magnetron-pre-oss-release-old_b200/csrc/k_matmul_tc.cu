@@ -310,6 +310,16 @@ __global__ void __maxnreg__(168)
         for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
             int mb, nb;
             tile_coords(t, num_m, num_n, mb, nb);
+            if constexpr (FUSED) {
+                // bring this thread's bias row slice toward L2 now; it is read after the last segment
+                const int prow = mb * BM + q * 32 + lane;
+                if (epi.bias && prow < M) {
+                    const float* pb = epi.bias + (int64_t)prow * N + nb * BN + h * HC;
+#pragma unroll
+                    for (int j = 0; j < HC; j += 32)
+                        if (nb * BN + h * HC + j < N) asm volatile("prefetch.global.L2 [%0];" ::"l"(pb + j));
+                }
+            }
             // segment sums are added in registers with round-to-nearest
             float sum[HC];
             for (int kb0 = 0; kb0 < nk; kb0 += seg_kb, ++gseg) {
