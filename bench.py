@@ -53,56 +53,57 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
-
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock and clock-event (throttle) reasons of one GPU, read through NVML
+    every 5 ms while the timed region runs (read-only queries)."""
 
     def __init__(self, index: int):
         self.index = index
-        self.proc = None
-        self.lines = []
+        self.samples = []
+        self.reasons = set()
+        self.max_mhz = None
+        self.stop_flag = threading.Event()
         self.t = None
+        self.err = None
 
     def start(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
-            self.t.start()
-        except Exception:
-            self.proc = None
+            import pynvml as N
+            N.nvmlInit()
+            self.N = N
+            self.h = N.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = float(N.nvmlDeviceGetMaxClockInfo(self.h, N.NVML_CLOCK_SM))
+            self.names = {N.nvmlClocksEventReasonHwSlowdown: "hw_slowdown",
+                          N.nvmlClocksEventReasonHwThermalSlowdown: "hw_thermal_slowdown",
+                          N.nvmlClocksEventReasonSwThermalSlowdown: "sw_thermal_slowdown",
+                          N.nvmlClocksEventReasonSwPowerCap: "sw_power_cap"}
+        except Exception as e:  # no NVML: report it instead of guessing
+            self.err = str(e)
+            return
+        self.t = threading.Thread(target=self._run, daemon=True)
+        self.t.start()
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+    def _run(self):
+        N = self.N
+        while not self.stop_flag.is_set():
+            try:
+                self.samples.append(float(N.nvmlDeviceGetClockInfo(self.h, N.NVML_CLOCK_SM)))
+                bits = N.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for b, nm in self.names.items():
+                    if bits & b:
+                        self.reasons.add(nm)
+            except Exception as e:
+                self.err = str(e)
+                return
+            time.sleep(0.005)
 
     def stop(self):
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx.append(float(parts[2]))
-            except ValueError:
-                continue
-            for nm, v in zip(names, parts[5:9]):
-                if v.lower() == "active":
-                    reasons.add(nm)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        self.stop_flag.set()
+        if self.t is not None:
+            self.t.join(timeout=2)
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [f"no samples: {self.err}"]}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
 
 
 # ----------------------------------------------------------- CPU baselines
@@ -366,17 +367,18 @@ def run_ours(args):
     dev.profile_collect()
     dev.profile_start()  # reset the per-op totals; timing below only
     clocks = ClockSampler(local)
-    clocks.start()
     barrier()
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
     launches_before = dev.launches()
+    clocks.start()
     ev0.record(stream)
     for _ in range(args.steps):
         step()
         dev.profile_collect()  # reads this replay's op events (syncs the device stream)
     ev1.record(stream)
     barrier()
+    clk = clocks.stop()
     launches_timed = dev.launches() - launches_before
     ms = ev0.elapsed_time(ev1)
     ms = max_over_ranks(ms)
@@ -393,7 +395,6 @@ def run_ours(args):
     ev1.record(stream)
     barrier()
     e2e_ms = max_over_ranks(max(ev0.elapsed_time(ev1), (time.perf_counter() - t0) * 1e3))
-    clk = clocks.stop()
     dev.profile_stop(os.devnull)
 
     value = GLOBAL_BATCH * args.steps / (ms / 1e3)
