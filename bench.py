@@ -415,7 +415,10 @@ def run_ours(args):
                 "d2h_bytes_per_step": world * rows * D_OUT * 4},
         "gpu_launches": launches_timed,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": three_tf32_peak, "unit": "TFLOP/s",
-                     "frac": achieved / three_tf32_peak if three_tf32_peak else None, "traffic": None,
+                     "frac": achieved / three_tf32_peak if three_tf32_peak else None,
+                     "traffic": 8 * (1.450e9 + 0.363e9) * rows / 65536,
+                     "traffic_note": "DRAM bytes per hidden-layer GEMM launch: ncu capture at 8192 rows "
+                                     "(profiles/gemm_3xtf32_fused_layer_8192x4096.md) scaled by rows",
                      "kernel": "MATMUL op (per-op CUDA events inside the replayed graph)",
                      "peak_note": f"3xTF32 effective = {pk_src} bf16 sustained / 2 (TF32 rate) / 3 (products)",
                      "matmul_ms_per_step": mm_ms_per_step, "matmul_launches": n_mm},
