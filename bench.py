@@ -513,7 +513,27 @@ def run_case(args):
         x.write(v)
         y.write(v)
         dims, st = MB.i64x6([n, 1, 1, 1, 1, 1]), MB.i64x6(MB.strides6([n, 1, 1, 1, 1, 1]))
-        if args.case == "add":
+        if args.case in ("tile", "bcast2"):
+            if args.case == "tile":   # x rm [8,16,32,64,8,256] (+) y rm [1,16,1,64,1,256]
+                xs, ys = (256, 8, 64, 32, 16, 8), (256, 1, 64, 1, 16, 1)
+                rs = xs
+            else:                     # [8,16,1,64,1,256] (+) [1,16,32,1,128,256] -> 2^33 outputs
+                xs, ys, rs = (256, 1, 64, 1, 16, 8), (256, 128, 1, 32, 16, 1), (256, 128, 64, 32, 16, 8)
+            for t in (x, y, r):
+                t.free()
+            nx, ny, nr = int(np.prod(xs)), int(np.prod(ys)), int(np.prod(rs))
+            x, y, r = dev.tensor((nx,)), dev.tensor((ny,)), dev.tensor((nr,))
+            x.write(np.resize(v, nx))
+            y.write(np.resize(v, ny))
+            if args.case == "tile":
+                dx, sx = MB.i64x6(xs), MB.i64x6(MB.strides6(xs))
+                dy, sy = MB.i64x6(ys), MB.i64x6(MB.strides6(ys))
+                fn = lambda: dev.L.mag_cuda_binary_f32(dev.p, MB.OP["ADD"], r.data_ptr, x.data_ptr, y.data_ptr, dx, sx, sx, dy, sy)
+            else:
+                fn = lambda: dev.L.mag_cuda_broadcast2_f32(dev.p, MB.OP["ADD"], r.data_ptr, x.data_ptr, y.data_ptr,
+                                                           MB.i64x6(rs), MB.i64x6(xs), MB.i64x6(ys))
+            work = 4.0 * (nx + ny + nr) / 1e9
+        elif args.case == "add":
             fn = lambda: dev.L.mag_cuda_binary_f32(dev.p, MB.OP["ADD"], r.data_ptr, x.data_ptr, y.data_ptr, dims, st, st, dims, st)
             work = 12.0 * n / 1e9
         elif args.case == "sigmoid":
@@ -723,7 +743,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--case", default=None, choices=["gemm", "layer", "add", "sigmoid", "sum", "softmax"],
+    ap.add_argument("--case", default=None, choices=["gemm", "layer", "add", "sigmoid", "sum", "softmax", "tile", "bcast2"],
                     help="run one kernel family for a profiler instead of the benchmark")
     ap.add_argument("--size", type=int, default=None)
     ap.add_argument("--sweep-full", action="store_true", help="measure every other BASELINE configuration")

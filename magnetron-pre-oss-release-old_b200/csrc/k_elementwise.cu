@@ -198,14 +198,15 @@ struct RowParams {
     uint32_t cols;
     int y_mode;       // 0: y column == c*ys0, 1: y column fixed (y_d0 == 1), 2: c % y_d0
     int x_mod;        // x column wraps modulo x_d0 (row indices always wrap modulo x's dims)
+    uint32_t seg_w;   // columns per warp iteration: 128 * steps, steps = 1..4 (row length rounded up)
+    int steps;
 };
 
 __device__ __forceinline__ uint32_t mod_by(uint32_t v, const FastDiv& f) { return v - fdiv(v, f) * f.d; }
 
-constexpr uint32_t kRowSeg = 512;  // columns per warp iteration (4 steps of 32 lanes x 4)
 
 template <int OP, bool VEC>
-__global__ void __launch_bounds__(kThreads) binary_rows(float* __restrict__ r, const float* __restrict__ x,
+__global__ void __launch_bounds__(kThreads, 4) binary_rows(float* __restrict__ r, const float* __restrict__ x,
                                                         const float* __restrict__ y, const RowParams p) {
     const int lane_id = threadIdx.x & 31;
     uint64_t warp = ((uint64_t)blockIdx.x * kThreads + threadIdx.x) >> 5;
@@ -236,9 +237,9 @@ __global__ void __launch_bounds__(kThreads) binary_rows(float* __restrict__ r, c
             uint32_t cs[4];
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
-                const uint32_t c = seg * kRowSeg + 128u * u + 4u * (uint32_t)lane_id;
+                const uint32_t c = seg * p.seg_w + 128u * u + 4u * (uint32_t)lane_id;
                 cs[u] = c;
-                if (c < p.cols) {
+                if (u < p.steps && c < p.cols) {
                     const uint32_t xc = p.x_mod ? mod_by(c, p.xdim[0]) : c;
                     a[u] = *(const float4*)(x + xo + xc);
                     if (p.y_mode == 1) {
@@ -252,7 +253,7 @@ __global__ void __launch_bounds__(kThreads) binary_rows(float* __restrict__ r, c
             }
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
-                if (cs[u] < p.cols) {
+                if (u < p.steps && cs[u] < p.cols) {
                     float4 o;
                     o.x = binop<OP>(a[u].x, b[u].x); o.y = binop<OP>(a[u].y, b[u].y);
                     o.z = binop<OP>(a[u].z, b[u].z); o.w = binop<OP>(a[u].w, b[u].w);
@@ -262,13 +263,89 @@ __global__ void __launch_bounds__(kThreads) binary_rows(float* __restrict__ r, c
         } else {
 #pragma unroll 4
             for (int u = 0; u < 16; ++u) {
-                uint32_t c = seg * kRowSeg + (uint32_t)lane_id + 32u * u;
-                if (c < p.cols) {
+                uint32_t c = seg * p.seg_w + (uint32_t)lane_id + 32u * u;
+                if (u < 4 * p.steps && c < p.cols) {
                     uint32_t xc = p.x_mod ? mod_by(c, p.xdim[0]) : c;
                     int64_t yc = p.y_mode == 0 ? (int64_t)c * p.ys[0]
                                : p.y_mode == 1 ? 0 : (int64_t)mod_by(c, p.ydim[0]) * p.ys[0];
                     r[ro + c] = binop<OP>(x[xo + xc], y[yo + yc]);
                 }
+            }
+        }
+    }
+}
+
+// Rows of at most 512 columns, vectorised: a warp walks kRowChunk consecutive
+// rows; the first row's indices are decomposed once and later rows advance
+// them with a carry, keeping x's and y's wrapped indices in step.
+constexpr uint32_t kRowChunk = 16;
+
+template <int OP>
+__global__ void __launch_bounds__(kThreads, 4) binary_rows_chunked(float* __restrict__ r, const float* __restrict__ x,
+                                                                   const float* __restrict__ y, const RowParams p,
+                                                                   uint32_t nrows, uint32_t nchunks) {
+    const int lane_id = threadIdx.x & 31;
+    const uint32_t warp = (uint32_t)(((uint64_t)blockIdx.x * kThreads + threadIdx.x) >> 5);
+    const uint32_t nwarps = (uint32_t)(((uint64_t)gridDim.x * kThreads) >> 5);
+    for (uint32_t ch = warp; ch < nchunks; ch += nwarps) {
+        uint32_t row0 = ch * kRowChunk;
+        uint32_t idx[6], xi[6], yi[6];
+        int64_t ro = 0, xo = 0, yo = 0;
+        uint32_t q = row0;
+#pragma unroll
+        for (int k = 1; k < 6; ++k) {
+            const uint32_t nq = fdiv(q, p.dim[k]);
+            idx[k] = q - nq * p.dim[k].d;
+            q = nq;
+            xi[k] = mod_by(idx[k], p.xdim[k]);
+            yi[k] = mod_by(idx[k], p.ydim[k]);
+            ro += (int64_t)idx[k] * p.rs[k];
+            xo += (int64_t)xi[k] * p.xs[k];
+            yo += (int64_t)yi[k] * p.ys[k];
+        }
+        const uint32_t rows_here = min(kRowChunk, nrows - row0);
+        for (uint32_t rr = 0; rr < rows_here; ++rr) {
+            float4 a[4], b[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const uint32_t c = 128u * u + 4u * (uint32_t)lane_id;
+                if (u < p.steps && c < p.cols) {
+                    const uint32_t xc = p.x_mod ? mod_by(c, p.xdim[0]) : c;
+                    a[u] = *(const float4*)(x + xo + xc);
+                    if (p.y_mode == 1) {
+                        const float t = y[yo];
+                        b[u] = make_float4(t, t, t, t);
+                    } else {
+                        const uint32_t yc = p.y_mode == 0 ? c : mod_by(c, p.ydim[0]);
+                        b[u] = *(const float4*)(y + yo + yc);
+                    }
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const uint32_t c = 128u * u + 4u * (uint32_t)lane_id;
+                if (u < p.steps && c < p.cols) {
+                    float4 o;
+                    o.x = binop<OP>(a[u].x, b[u].x); o.y = binop<OP>(a[u].y, b[u].y);
+                    o.z = binop<OP>(a[u].z, b[u].z); o.w = binop<OP>(a[u].w, b[u].w);
+                    __stcs((float4*)(r + ro + c), o);
+                }
+            }
+            // next row: increment dim 1 with carry into dims 2..5
+#pragma unroll
+            for (int k = 1; k < 6; ++k) {
+                ++idx[k];
+                ro += p.rs[k];
+                if (++xi[k] == p.xdim[k].d) { xi[k] = 0; xo -= (int64_t)(p.xdim[k].d - 1) * p.xs[k]; } else { xo += p.xs[k]; }
+                if (++yi[k] == p.ydim[k].d) { yi[k] = 0; yo -= (int64_t)(p.ydim[k].d - 1) * p.ys[k]; } else { yo += p.ys[k]; }
+                if (idx[k] < p.dim[k].d) break;
+                idx[k] = 0;
+                ro -= (int64_t)p.dim[k].d * p.rs[k];
+                // the wrapped indices of x and y restart at 0 together with idx[k]
+                xo -= (int64_t)xi[k] * p.xs[k];
+                yo -= (int64_t)yi[k] * p.ys[k];
+                xi[k] = 0;
+                yi[k] = 0;
             }
         }
     }
@@ -293,7 +370,9 @@ cudaError_t launch_rows(float* r, const float* x, const float* y, const int64_t*
         p.ydim[k] = make_fastdiv((uint32_t)yd[k]);
         if (k) rows *= (uint64_t)dims[k];
     }
-    uint64_t spr = ((uint64_t)dims[0] + kRowSeg - 1) / kRowSeg;
+    p.steps = (int)(((uint64_t)dims[0] + 127) / 128 < 4 ? ((uint64_t)dims[0] + 127) / 128 : 4);
+    p.seg_w = 128u * (uint32_t)p.steps;
+    uint64_t spr = ((uint64_t)dims[0] + p.seg_w - 1) / p.seg_w;
     p.segs_per_row = make_fastdiv((uint32_t)spr);
     p.nseg = rows * spr;
     if (p.nseg >= (1ull << 32)) return cudaErrorInvalidValue;
@@ -306,6 +385,12 @@ cudaError_t launch_rows(float* r, const float* x, const float* y, const int64_t*
     if (p.y_mode != 1) {
         vec = vec && ys[0] == 1 && yd[0] % 4 == 0 && ((uintptr_t)y & 15) == 0;
         for (int k = 1; k < 6; ++k) vec = vec && ys[k] % 4 == 0;
+    }
+    if (vec && p.steps <= 4 && dims[0] <= 512 && rows >= 4 * kRowChunk && rows < (1ull << 32)) {
+        const uint32_t nchunks = (uint32_t)((rows + kRowChunk - 1) / kRowChunk);
+        binary_rows_chunked<OP><<<grid_for((uint64_t)nchunks * 32, kThreads), kThreads, 0, st>>>(
+            r, x, y, p, (uint32_t)rows, nchunks);
+        return cudaGetLastError();
     }
     unsigned grid = grid_for(p.nseg * 32, kThreads);
     if (vec) binary_rows<OP, true><<<grid, kThreads, 0, st>>>(r, x, y, p);

@@ -234,13 +234,13 @@ cudaError_t launch_rows_op(float* r, const float* x, int64_t rows, int64_t cols,
 // Rows stay in registers between the three phases (max, exp + double sum,
 // divide), so HBM sees one read and one write per element.  Short rows
 // (<= 2048) get one warp each; longer rows are split into slices of 16384
-// elements, one 256-thread CTA per slice, and the slices of a row form a
+// elements, one 512-thread CTA per slice, and the slices of a row form a
 // thread-block cluster that combines the row max and sum through distributed
 // shared memory.
 
 constexpr int kWarpRowMax = 2048;  // rows up to this length get one warp (16 float4 per lane at most)
-constexpr int kSliceThreads = 256;
-constexpr int kSliceVec = 16;     // float4 per thread: 16384 elements per CTA
+constexpr int kSliceThreads = 512;
+constexpr int kSliceVec = 8;      // float4 per thread: 16384 elements per CTA
 constexpr int kSlice = kSliceThreads * 4 * kSliceVec;
 
 // The reference's scalar tail calls libm expf; kept out of line so the common
@@ -274,8 +274,9 @@ __device__ __forceinline__ float4 exp4(float4 v, float m, uint32_t c, uint32_t c
     return e;
 }
 
-__device__ __forceinline__ float4 div4(float4 e, float d) {
-    return make_float4(__fdiv_rn(e.x, d), __fdiv_rn(e.y, d), __fdiv_rn(e.z, d), __fdiv_rn(e.w, d));
+// e / sum as e * rn(1/sum): within 1.5 ulp of the division, one reciprocal per row.
+__device__ __forceinline__ float4 div4(float4 e, float inv) {
+    return make_float4(__fmul_rn(e.x, inv), __fmul_rn(e.y, inv), __fmul_rn(e.z, inv), __fmul_rn(e.w, inv));
 }
 
 // Loads 4 consecutive elements starting at column c (c % 4 == 0 on the vector path).
@@ -321,14 +322,14 @@ __global__ void __launch_bounds__(256) softmax_rows_warp(float* __restrict__ r, 
         double s = 0.0;
 #pragma unroll
         for (int i = 0; i < V; ++i) v[i] = exp4(v[i], m, (uint32_t)(lane + 32 * i) * 4, cols, vec_end, s);
-        const float fsum = (float)warp_sum(s);
+        const float inv = __frcp_rn((float)warp_sum(s));
 #pragma unroll
-        for (int i = 0; i < V; ++i) store4(pr, (uint32_t)(lane + 32 * i) * 4, cols, vec, div4(v[i], fsum));
+        for (int i = 0; i < V; ++i) store4(pr, (uint32_t)(lane + 32 * i) * 4, cols, vec, div4(v[i], inv));
     }
 }
 
 // One CTA per 16384-element slice; the cluster spans the row.
-__global__ void __launch_bounds__(kSliceThreads) softmax_rows_slices(float* __restrict__ r,
+__global__ void __launch_bounds__(kSliceThreads, 2) softmax_rows_slices(float* __restrict__ r,
                                                                      const float* __restrict__ x, uint32_t cols) {
     __shared__ float sh_max[32];
     __shared__ double sh_sum[32];
@@ -363,10 +364,10 @@ __global__ void __launch_bounds__(kSliceThreads) softmax_rows_slices(float* __re
     cluster.sync();
     double gs = 0.0;
     for (uint32_t k = 0; k < csize; ++k) gs += *cluster.map_shared_rank(&slot_sum, k);
-    const float fsum = (float)gs;
+    const float inv = __frcp_rn((float)gs);
 #pragma unroll
     for (int i = 0; i < kSliceVec; ++i)
-        store4(pr, c0 + (uint32_t)(threadIdx.x + kSliceThreads * i) * 4, cols, vec, div4(v[i], fsum));
+        store4(pr, c0 + (uint32_t)(threadIdx.x + kSliceThreads * i) * 4, cols, vec, div4(v[i], inv));
     cluster.sync();  // peers may still read this CTA's slots
 }
 

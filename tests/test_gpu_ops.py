@@ -65,6 +65,9 @@ def test_binary_same_and_broadcast(op):
         for sh in [(1, 2, 1), (2, 1, 3), (3, 2, 2, 1, 1, 2), (4, 1, 1, 2)]:
             cases.append((tuple(d * f for d in sh), sh))
     cases += [((16, 8), (16, 1)), ((16, 8), (1, 8)), ((256, 4, 3), (256, 1, 3)), ((64, 6), (8, 3))]
+    # >= 64 rows of <= 512 columns: the chunked row kernel with carried indices
+    cases += [((8, 6, 4, 2, 2, 3), (4, 3, 2, 1, 2, 1)), ((8, 6, 4, 2, 2, 3), (1, 3, 4, 1, 2, 3)),
+              ((256, 8, 16, 3), (256, 1, 16, 1)), ((512, 70), (512, 7))]
     for i, (xs, ys) in enumerate(cases):
         x6, y6 = pad6(xs), pad6(ys)
         s = o.stream(3000 + i)
