@@ -542,6 +542,12 @@ def run_case(args):
         elif args.case == "sum":
             fn = lambda: dev.L.mag_cuda_reduce_f32(dev.p, MB.OP["SUM"], r.data_ptr, x.data_ptr, dims, st)
             work = 4.0 * n / 1e9
+        elif args.case == "softmax1k":
+            fn = lambda: dev.L.mag_cuda_softmax_rows_f32(dev.p, r.data_ptr, x.data_ptr, n // 1024, 1024)
+            work = 8.0 * n / 1e9
+        elif args.case == "skinny":  # M = 1, K = N = 4096
+            fn = lambda: dev.L.mag_cuda_matmul_f32(dev.p, r.data_ptr, x.data_ptr, y.data_ptr, 1, 4096, 4096)
+            work = 4.0 * (4096 + 4096 * 4096 + 4096) / 1e9
         else:
             fn = lambda: dev.L.mag_cuda_softmax_rows_f32(dev.p, r.data_ptr, x.data_ptr, n // 32768, 32768)
             work = 8.0 * n / 1e9
@@ -685,8 +691,8 @@ def run_sweep_full(args):
     bt, mm = 64, 512
     a, c_ = filled(bt * mm * mm, lambda c: c * (mm ** -0.25)), dev.tensor((bt * mm * mm,))
     ms = timeit(lambda: dev.L.mag_cuda_matmul_batched_f32(dev.p, c_.data_ptr, a.data_ptr, a.data_ptr, bt, mm, mm, mm), 5)
-    rec("matmul", "batched 64 x [512x512 . 512x512] (bit-exact CUDA-core path)", ms, 2.0 * bt * mm ** 3 / 1e12,
-        "TFLOP/s", None)
+    rec("matmul", "batched 64 x [512x512 . 512x512] (3xTF32 tcgen05, batch-indexed tiles)", ms,
+        2.0 * bt * mm ** 3 / 1e12, "TFLOP/s", tf)
     a.free()
     c_.free()
     # ---- reference CPU, single thread, on this host
@@ -743,7 +749,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--case", default=None, choices=["gemm", "layer", "add", "sigmoid", "sum", "softmax", "tile", "bcast2"],
+    ap.add_argument("--case", default=None, choices=["gemm", "layer", "add", "sigmoid", "sum", "softmax", "softmax1k", "skinny", "tile", "bcast2"],
                     help="run one kernel family for a profiler instead of the benchmark")
     ap.add_argument("--size", type=int, default=None)
     ap.add_argument("--sweep-full", action="store_true", help="measure every other BASELINE configuration")

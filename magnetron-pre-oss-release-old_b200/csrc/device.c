@@ -801,8 +801,16 @@ int mag_cuda_matmul_batched_f32(mag_compute_device_t* dvc, float* r, const float
     ext_in(d, x);
     ext_in(d, y);
     ext_out(d, r, (size_t)(batch * M * N * 4));
-    int rc = mcu_launch_matmul_exact(r, x, y, batch, M, K, N, N, 0, d->stream);
-    if (!rc) mcu_count_launches(1);
+    int rc;
+    if (d->matmul_mode != 1 && mcu_matmul_tc_supported() && M >= 128 && N >= 64 && K >= 32 &&
+        (double)batch * M * N * K >= 1.0e9) {
+        void* scratch = scratch_get(d, mcu_matmul_tc_batched_scratch_bytes(batch, M, K, N));
+        rc = mcu_launch_matmul_tc_batched(r, x, y, batch, M, K, N, scratch, d->d_status, d->stream);
+        if (!rc) mcu_count_launches(3);
+    } else {
+        rc = mcu_launch_matmul_exact(r, x, y, batch, M, K, N, N, 0, d->stream);
+        if (!rc) mcu_count_launches(1);
+    }
     return rc;
 }
 

@@ -204,7 +204,7 @@ __global__ void __maxnreg__(168)
     gemm_3xtf32(const __grid_constant__ CUtensorMap map_xhi, const __grid_constant__ CUtensorMap map_xlo,
                 const __grid_constant__ CUtensorMap map_yhi, const __grid_constant__ CUtensorMap map_ylo,
                 float* __restrict__ r, int M, int N, int Kp, int64_t ldr, int* status, const Epi epi,
-                int seg_kb) {
+                int seg_kb, int batch) {
     using C = Cfg<BN, STAGES>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -221,7 +221,8 @@ __global__ void __maxnreg__(168)
     const int lane = threadIdx.x & 31;
     const int num_m = (M + BM - 1) / BM;
     const int num_n = (N + BN - 1) / BN;
-    const int tiles = num_m * num_n;
+    const int tiles_per_batch = num_m * num_n;
+    const int tiles = tiles_per_batch * batch;  // batch b's operands start at rows b*M (X) and b*N (Y)
     const int nk = Kp / BK;
     Abort ab{abort_flag, status};
 
@@ -257,16 +258,18 @@ __global__ void __maxnreg__(168)
             uint32_t it = 0;
             for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
                 int mb, nb;
-                tile_coords(t, num_m, num_n, mb, nb);
+                const int bt = t / tiles_per_batch;
+                tile_coords(t - bt * tiles_per_batch, num_m, num_n, mb, nb);
+                const int xrow = bt * M + mb * BM, yrow = bt * N + nb * BN;
                 for (int kb = 0; kb < nk; ++kb, ++it) {
                     const uint32_t s = it % STAGES, round = it / STAGES;
                     if (!mbar_wait(&empty[s], (round & 1) ^ 1, ab, 1)) goto done;
                     uint8_t* st = ring + s * C::STAGE_BYTES;
                     mbar_expect_tx(&full[s], C::STAGE_BYTES);
-                    tma_load_2d(&map_xhi, &full[s], st, kb * BK, mb * BM);
-                    tma_load_2d(&map_xlo, &full[s], st + C::A_BYTES, kb * BK, mb * BM);
-                    tma_load_2d(&map_yhi, &full[s], st + 2 * C::A_BYTES, kb * BK, nb * BN);
-                    tma_load_2d(&map_ylo, &full[s], st + 2 * C::A_BYTES + C::B_BYTES, kb * BK, nb * BN);
+                    tma_load_2d(&map_xhi, &full[s], st, kb * BK, xrow);
+                    tma_load_2d(&map_xlo, &full[s], st + C::A_BYTES, kb * BK, xrow);
+                    tma_load_2d(&map_yhi, &full[s], st + 2 * C::A_BYTES, kb * BK, yrow);
+                    tma_load_2d(&map_ylo, &full[s], st + 2 * C::A_BYTES + C::B_BYTES, kb * BK, yrow);
                 }
             }
         }
@@ -309,7 +312,8 @@ __global__ void __maxnreg__(168)
         uint32_t gseg = 0;
         for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
             int mb, nb;
-            tile_coords(t, num_m, num_n, mb, nb);
+            const int bt = t / tiles_per_batch;
+            tile_coords(t - bt * tiles_per_batch, num_m, num_n, mb, nb);
             if constexpr (FUSED) {
                 // bring this thread's bias row slice toward L2 now; it is read after the last segment
                 const int prow = mb * BM + q * 32 + lane;
@@ -344,7 +348,7 @@ __global__ void __maxnreg__(168)
             const int row = mb * BM + q * 32 + lane;
             if (row >= M) continue;
             const int colh = nb * BN + h * HC;
-            float* out = r + (int64_t)row * ldr + colh;
+            float* out = r + (int64_t)bt * M * ldr + (int64_t)row * ldr + colh;
             const bool vec = ((ldr & 3) == 0) && ((((uintptr_t)r) & 15) == 0);
 #pragma unroll
             for (int c = 0; c < HC / 32; ++c) {
@@ -452,6 +456,9 @@ __global__ void __launch_bounds__(256) split_rows(const float* __restrict__ x, f
 __global__ void __launch_bounds__(256) split_cols_t(const float* __restrict__ y, float* __restrict__ hi,
                                                     float* __restrict__ lo, int64_t K, int64_t N, int64_t Kp) {
     __shared__ float tile[32][33];
+    y += (int64_t)blockIdx.z * K * N;   // batch b: Y[b] is K x N, its split rows start at b*N
+    hi += (int64_t)blockIdx.z * N * Kp;
+    lo += (int64_t)blockIdx.z * N * Kp;
     const int64_t k0 = (int64_t)blockIdx.y * 32, n0 = (int64_t)blockIdx.x * 32;
     const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
     for (int j = ty; j < 32; j += 8) {
@@ -542,11 +549,29 @@ extern "C" int mcu_matmul_tc_supported(void) {
 
 extern "C" size_t mcu_matmul_tc_scratch_bytes(int64_t M, int64_t K, int64_t N) { return layout(M, K, N).total; }
 
+static int launch_tc(float* r, const float* x, const float* y, int64_t B, int64_t M, int64_t K, int64_t N,
+                     void* scratch, int* status, cudaStream_t st, const mcu_tc_epilogue* ep);
+
 extern "C" int mcu_launch_matmul_tc_ex(float* r, const float* x, const float* y, int64_t M, int64_t K, int64_t N,
                                        void* scratch, int* status, cudaStream_t st, const mcu_tc_epilogue* ep) {
-    if (M <= 0 || N <= 0) return (int)cudaSuccess;
-    if (M >= (1ll << 31) || N >= (1ll << 31) || K >= (1ll << 21) || !scratch) return (int)cudaErrorInvalidValue;
-    const Layout l = layout(M, K, N);
+    return launch_tc(r, x, y, 1, M, K, N, scratch, status, st, ep);
+}
+
+extern "C" size_t mcu_matmul_tc_batched_scratch_bytes(int64_t B, int64_t M, int64_t K, int64_t N) {
+    return layout(B * M, K, B * N).total;
+}
+
+extern "C" int mcu_launch_matmul_tc_batched(float* r, const float* x, const float* y, int64_t B, int64_t M, int64_t K,
+                                            int64_t N, void* scratch, int* status, cudaStream_t st) {
+    return launch_tc(r, x, y, B, M, K, N, scratch, status, st, nullptr);
+}
+
+static int launch_tc(float* r, const float* x, const float* y, int64_t B, int64_t M, int64_t K, int64_t N,
+                     void* scratch, int* status, cudaStream_t st, const mcu_tc_epilogue* ep) {
+    if (B <= 0 || M <= 0 || N <= 0) return (int)cudaSuccess;
+    if (B * M >= (1ll << 31) || B * N >= (1ll << 31) || K >= (1ll << 21) || !scratch) return (int)cudaErrorInvalidValue;
+    if (B > 1 && ep) return (int)cudaErrorInvalidValue;
+    const Layout l = layout(B * M, K, B * N);
     char* base = (char*)scratch;
     float* xhi = (float*)(base + l.xhi);
     float* xlo = (float*)(base + l.xlo);
@@ -557,21 +582,21 @@ extern "C" int mcu_launch_matmul_tc_ex(float* r, const float* x, const float* y,
         xhi = (float*)ep->a_hi;
         xlo = (float*)ep->a_lo;
     } else {
-        int64_t n = M * (l.kp / 4);
+        int64_t n = B * M * (l.kp / 4);  // X of all batches is one (B*M) x K row-major matrix
         int64_t g = (n + 255) / 256;
         if (g > 8 * sm_count()) g = 8 * sm_count();
-        split_rows<<<(unsigned)g, 256, 0, st>>>(x, xhi, xlo, M, K, l.kp);
+        split_rows<<<(unsigned)g, 256, 0, st>>>(x, xhi, xlo, B * M, K, l.kp);
     }
     {
-        dim3 grid((unsigned)((N + 31) / 32), (unsigned)(l.kp / 32));
+        dim3 grid((unsigned)((N + 31) / 32), (unsigned)(l.kp / 32), (unsigned)B);
         split_cols_t<<<grid, 256, 0, st>>>(y, yhi, ylo, K, N, l.kp);
     }
     CUtensorMap mxh, mxl, myh, myl;
-    if (!make_map(&mxh, xhi, M, l.kp, BM) || !make_map(&mxl, xlo, M, l.kp, BM) ||
-        !make_map(&myh, yhi, N, l.kp, kBN) || !make_map(&myl, ylo, N, l.kp, kBN))
+    if (!make_map(&mxh, xhi, B * M, l.kp, BM) || !make_map(&mxl, xlo, B * M, l.kp, BM) ||
+        !make_map(&myh, yhi, B * N, l.kp, kBN) || !make_map(&myl, ylo, B * N, l.kp, kBN))
         return (int)cudaErrorInvalidValue;
     using C = Cfg<kBN, kStages>;
-    const int64_t tiles = ((M + BM - 1) / BM) * ((N + kBN - 1) / kBN);
+    const int64_t tiles = B * ((M + BM - 1) / BM) * ((N + kBN - 1) / kBN);
     const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
     Epi epi{};
     const bool fused = ep && (ep->bias || ep->act || ep->out_hi);
@@ -586,13 +611,13 @@ extern "C" int mcu_launch_matmul_tc_ex(float* r, const float* x, const float* y,
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
         if (e != cudaSuccess) return (int)e;
         kern<<<grid, kThreads, C::SMEM, st>>>(mxh, mxl, myh, myl, r, (int)M, (int)N, (int)l.kp, (int64_t)N, status, epi,
-                                              segment_kb());
+                                              segment_kb(), (int)B);
     } else {
         auto kern = gemm_3xtf32<kBN, kStages, false>;
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
         if (e != cudaSuccess) return (int)e;
         kern<<<grid, kThreads, C::SMEM, st>>>(mxh, mxl, myh, myl, r, (int)M, (int)N, (int)l.kp, (int64_t)N, status, epi,
-                                              segment_kb());
+                                              segment_kb(), (int)B);
     }
     return (int)cudaGetLastError();
 }

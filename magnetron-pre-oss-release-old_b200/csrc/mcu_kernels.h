@@ -65,6 +65,9 @@ typedef struct mcu_tc_epilogue {
     int64_t kp_out;
     int act;
 } mcu_tc_epilogue;
+size_t mcu_matmul_tc_batched_scratch_bytes(int64_t B, int64_t M, int64_t K, int64_t N);
+int mcu_launch_matmul_tc_batched(float* r, const float* x, const float* y, int64_t B, int64_t M, int64_t K,
+                                 int64_t N, void* scratch, int* status, cudaStream_t st);
 int mcu_launch_matmul_tc_ex(float* r, const float* x, const float* y, int64_t M, int64_t K, int64_t N,
                             void* scratch, int* status, cudaStream_t st, const mcu_tc_epilogue* ep);
 

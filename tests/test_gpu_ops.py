@@ -378,3 +378,22 @@ def test_fused_graph_matches_unfused_bitwise(inplace):
     assert bits_equal(fused, plain).all()
     assert bits_equal(fused2, plain2).all()
     assert not bits_equal(fused, fused2).all()
+
+
+def test_matmul_batched_tensor_core():
+    """Batched product large enough for the tensor-core path (tiles indexed by batch)."""
+    dev = device()
+    o = oracle()
+    b, m, k, n = 16, 520, 512, 264  # M, N not multiples of the 128 x 256 tile: tiles straddle batches
+    s = o.stream(7200)
+    x = s.uniform(b * m * k, -1, 1)
+    y = s.uniform(b * k * n, -1, 1)
+    tx, ty, tr = dev.tensor((b * m * k,)), dev.tensor((b * k * n,)), dev.tensor((b * m * n,))
+    tx.write(x)
+    ty.write(y)
+    MB.check(dev.L.mag_cuda_matmul_batched_f32(dev.p, tr.data_ptr, tx.data_ptr, ty.data_ptr, b, m, k, n), "bmm")
+    assert dev.L.mag_cuda_synchronize(dev.p) == 0
+    got = _raw(dev, tr.data_ptr, b * m * n)
+    for i in range(b):
+        assert _normwise_ok(got[i * m * n:(i + 1) * m * n], x[i * m * k:(i + 1) * m * k],
+                            y[i * k * n:(i + 1) * k * n], m, k, n), i
