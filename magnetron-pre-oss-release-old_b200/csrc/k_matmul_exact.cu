@@ -106,11 +106,11 @@ cudaError_t launch_exact(float* r, const float* x, const float* y, int64_t batch
 
 constexpr int kSkinnyRows = 16;           // rows per CTA (M up to 64 uses up to 4 row blocks)
 constexpr int kSkinnyCols = kThreads * 4; // each thread owns 4 columns
-constexpr int kSkinnyKc = 64;             // k rows per slice (multiple of 8)
+constexpr int kSkinnyKc = 64;             // k rows per slice (multiple of 16)
 
 // Partial product of X[m0:m0+MR, slice] and Y[slice, cols]; Y rows are
-// fetched 8 at a time before any FMA so every thread keeps 8 128-bit loads
-// in flight.
+// fetched 16 (MR <= 4) or 8 at a time before any FMA, so every thread keeps
+// that many 128-bit loads in flight.
 template <int MR>
 __global__ void __launch_bounds__(kThreads) matmul_skinny_part(float* __restrict__ part, const float* __restrict__ x,
                                                                const float* __restrict__ y, int M, int64_t K,
@@ -140,13 +140,14 @@ __global__ void __launch_bounds__(kThreads) matmul_skinny_part(float* __restrict
             t.w = c + 3 < N ? py[3] : 0.0f;
             return t;
         };
+        constexpr int U = MR <= 4 ? 16 : 8;  // loads in flight per thread (registers permitting)
         int64_t k = k0;
-        for (; k + 8 <= k1; k += 8) {
-            float4 yv[8];
+        for (; k + U <= k1; k += U) {
+            float4 yv[U];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) yv[u] = load(k + u);
+            for (int u = 0; u < U; ++u) yv[u] = load(k + u);
 #pragma unroll
-            for (int u = 0; u < 8; ++u)
+            for (int u = 0; u < U; ++u)
 #pragma unroll
                 for (int m = 0; m < MR; ++m) {
                     const float xv = xs[m][k - k0 + u];
@@ -191,22 +192,22 @@ __global__ void __launch_bounds__(kThreads) matmul_skinny_sum(float* __restrict_
     }
 }
 
-// K slices so that about two CTAs per SM stream Y.
+// K slices so that about four CTAs per SM stream Y.
 int64_t skinny_slices(int64_t M, int64_t K, int64_t N) {
     const int64_t colblocks = (N + kSkinnyCols - 1) / kSkinnyCols;
     const int64_t rowblocks = (M + kSkinnyRows - 1) / kSkinnyRows;
-    int64_t want = (2 * (int64_t)sm_count() + colblocks * rowblocks - 1) / (colblocks * rowblocks);
+    int64_t want = (4 * (int64_t)sm_count() + colblocks * rowblocks - 1) / (colblocks * rowblocks);
     int64_t kc = (K + want - 1) / (want < 1 ? 1 : want);
-    kc = (kc + 7) / 8 * 8;
+    kc = (kc + 15) / 16 * 16;
     if (kc > kSkinnyKc) kc = kSkinnyKc;
-    if (kc < 8) kc = 8;
+    if (kc < 16) kc = 16;
     int64_t slices = (K + kc - 1) / kc;
     return slices < 1 ? 1 : slices;
 }
 
 int64_t skinny_kc(int64_t K, int64_t slices) {
     int64_t kc = (K + slices - 1) / slices;
-    return (kc + 7) / 8 * 8;
+    return (kc + 15) / 16 * 16;
 }
 
 }  // namespace

@@ -303,7 +303,7 @@ __device__ __forceinline__ void store4(float* pr, uint32_t c, uint32_t cols, boo
 
 // One warp per row; lane holds columns 4*(lane + 32*i) .. +3.
 template <int V>
-__global__ void __launch_bounds__(256) softmax_rows_warp(float* __restrict__ r, const float* __restrict__ x,
+__global__ void __launch_bounds__(256, V <= 4 ? 4 : (V <= 8 ? 3 : 1)) softmax_rows_warp(float* __restrict__ r, const float* __restrict__ x,
                                                          uint64_t rows, uint32_t cols) {
     const int lane = threadIdx.x & 31;
     const uint64_t nw = ((uint64_t)gridDim.x * blockDim.x) >> 5;
