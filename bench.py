@@ -23,6 +23,7 @@ no flush is needed between steps.
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import statistics
@@ -545,6 +546,14 @@ def run_case(args):
         elif args.case == "softmax1k":
             fn = lambda: dev.L.mag_cuda_softmax_rows_f32(dev.p, r.data_ptr, x.data_ptr, n // 1024, 1024)
             work = 8.0 * n / 1e9
+        elif args.case == "fill_const":
+            fn = lambda: dev.L.mag_cuda_fill_f32(dev.p, r.data_ptr, n, 1.5)
+            work = 4.0 * n / 1e9
+        elif args.case in ("fill_uniform", "fill_normal"):
+            g = MB.Pcg(0x5EED0002)
+            fill = getattr(dev.L, f"mag_cuda_{args.case}_pcg_f32")
+            fn = lambda: fill(dev.p, r.data_ptr, n, 0.0, 1.0, ctypes.byref(g.state), g.inc)
+            work = 4.0 * n / 1e9
         elif args.case == "skinny":  # M = 1, K = N = 4096
             fn = lambda: dev.L.mag_cuda_matmul_f32(dev.p, r.data_ptr, x.data_ptr, y.data_ptr, 1, 4096, 4096)
             work = 4.0 * (4096 + 4096 * 4096 + 4096) / 1e9
@@ -695,6 +704,17 @@ def run_sweep_full(args):
         2.0 * bt * mm ** 3 / 1e12, "TFLOP/s", tf)
     a.free()
     c_.free()
+    # ---- seeded fills on the device (the PCG stream of a reference context, jumped per thread)
+    n = 1 << 28
+    r = dev.tensor((n,))
+    g = MB.Pcg(0x5EED0002)
+    ms = timeit(lambda: dev.L.mag_cuda_fill_uniform_pcg_f32(dev.p, r.data_ptr, n, -1.0, 1.0, ctypes.byref(g.state),
+                                                           g.inc), 5)
+    rec("fill", "uniform PCG 2^28", ms, 4.0 * n / 1e9, "GB/s", hbm)
+    ms = timeit(lambda: dev.L.mag_cuda_fill_normal_pcg_f32(dev.p, r.data_ptr, n, 0.0, 1.0, ctypes.byref(g.state),
+                                                          g.inc), 5)
+    rec("fill", "normal PCG + Box-Muller 2^28", ms, 4.0 * n / 1e9, "GB/s", hbm)
+    r.free()
     # ---- reference CPU, single thread, on this host
     cpu = []
     if not args.no_cpu_baseline:
@@ -724,6 +744,12 @@ def run_sweep_full(args):
                 cpu.append({"case": f"{op} 2^24", "rate": 8.0 * n / dt / 1e9, "unit": "GB/s"})
             dt = cpu_time(lambda: R.op("SUM", tx))
             cpu.append({"case": "full SUM 2^24", "rate": 4.0 * n / dt / 1e9, "unit": "GB/s"})
+            for kind in ("uniform", "normal"):
+                fill = getattr(R.L, f"mag_tensor_fill_random_{kind}")
+                t0 = time.perf_counter()
+                fill(tx, 0.0, 1.0)
+                cpu.append({"case": f"fill {kind} 2^24", "rate": 4.0 * n / (time.perf_counter() - t0) / 1e9,
+                            "unit": "GB/s"})
             m = 1024
             ta, tb = R.tensor_nd((m, m)), R.tensor_nd((m, m))
             R.write(ta, v[:m * m])
@@ -749,7 +775,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--case", default=None, choices=["gemm", "layer", "add", "sigmoid", "sum", "softmax", "softmax1k", "skinny", "tile", "bcast2"],
+    ap.add_argument("--case", default=None, choices=["gemm", "layer", "add", "sigmoid", "sum", "softmax", "softmax1k", "skinny", "tile", "bcast2",
+                                                      "fill_uniform", "fill_normal", "fill_const"],
                     help="run one kernel family for a profiler instead of the benchmark")
     ap.add_argument("--size", type=int, default=None)
     ap.add_argument("--sweep-full", action="store_true", help="measure every other BASELINE configuration")

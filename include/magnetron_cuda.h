@@ -113,6 +113,25 @@ MAG_CUDA_EXPORT int mag_cuda_softmax_rows_f32(mag_compute_device_t* dvc, float* 
 MAG_CUDA_EXPORT int mag_cuda_matmul_batched_f32(mag_compute_device_t* dvc, float* r, const float* x,
                                                 const float* y, int64_t batch, int64_t M, int64_t K, int64_t N);
 
+/* ---- seeded fills on the device ----
+ * The core fills tensors on the host only (magnetron/magnetron.c:1826-1876 assert a
+ * CPU context).  These generate the same PCG stream on the device: *state and inc are
+ * the context's PCG state (magnetron/magnetron.c:779-790, seeded as at :805-808), the
+ * values equal what mag_prng_generate_n would write from *state, and on return *state
+ * has advanced by n steps, as the host generator would leave it.
+ * Uniform: min + (max - min) * u, bit-identical to the host stream
+ * (mag_tensor_fill_random_uniform, magnetron/magnetron.c:1844-1854).
+ * Normal: Box-Muller pairs over the uniform(0, 1) stream, n even
+ * (mag_tensor_fill_random_normal, magnetron/magnetron.c:1856-1876); log, sin and cos
+ * are rounded once from f64, so a value can differ from the host libm's by its
+ * rounding (a few ulp of the pair's magnitude). */
+MAG_CUDA_EXPORT int mag_cuda_fill_uniform_pcg_f32(mag_compute_device_t* dvc, float* r, int64_t n, float min,
+                                                  float max, uint64_t* state, uint64_t inc);
+MAG_CUDA_EXPORT int mag_cuda_fill_normal_pcg_f32(mag_compute_device_t* dvc, float* r, int64_t n, float mean,
+                                                 float stddev, uint64_t* state, uint64_t inc);
+/* r[0..n) = x (mag_tensor_fill, magnetron/magnetron.c:1826-1842, for any x). */
+MAG_CUDA_EXPORT int mag_cuda_fill_f32(mag_compute_device_t* dvc, float* r, int64_t n, float x);
+
 /* ---- allocation-free entry point (no counterpart in the reference) ----
  * R[M,N] = X[M,K] Y[K,N] for 1 <= M <= 16, the same split-K kernels as
  * mag_cuda_matmul_f32 uses for such shapes, but it never allocates: for callers

@@ -634,10 +634,21 @@ void mag_destroy_device_cuda(mag_compute_device_t* dvc) {
 
 /* Plain-pointer entry points keep the zero bookkeeping of tensor storage they
  * touch: inputs are cleared if still pending, outputs are marked written. */
-static void ext_in(mcu_device* d, const void* p) { materialize(d, (uintptr_t)p); }
+/* The block holding p: by base first, else (a pointer into a buffer) by range. */
+static mcu_block* tab_find_containing(mcu_device* d, uintptr_t p) {
+    mcu_block* b = tab_find(d, p);
+    if (b) return b;
+    for (size_t i = 0; i < d->tab_cap; ++i)
+        if (d->tab[i].state == 1 && d->tab[i].base <= p && p - d->tab[i].base < d->tab[i].size) return &d->tab[i];
+    return NULL;
+}
+static void ext_in(mcu_device* d, const void* p) {
+    mcu_block* b = tab_find_containing(d, (uintptr_t)p);
+    if (b) materialize(d, b->base);
+}
 static void ext_out(mcu_device* d, void* p, size_t bytes) {
-    mcu_block* b = tab_find(d, (uintptr_t)p);
-    if (b) result_written(d, (uintptr_t)p, bytes >= b->size);
+    mcu_block* b = tab_find_containing(d, (uintptr_t)p);
+    if (b) result_written(d, b->base, b->base == (uintptr_t)p && bytes >= b->size);
 }
 
 int mag_cuda_device_ordinal(mag_compute_device_t* dvc) { return dev_of(dvc)->ordinal; }
@@ -791,6 +802,40 @@ int mag_cuda_softmax_rows_f32(mag_compute_device_t* dvc, float* r, const float* 
     ext_out(d, r, (size_t)(rows * cols * 4));
     int rc = mcu_launch_softmax_rows(r, x, rows, cols, d->stream);
     if (!rc) mcu_count_launches(1);
+    return rc;
+}
+
+int mag_cuda_fill_uniform_pcg_f32(mag_compute_device_t* dvc, float* r, int64_t n, float min, float max,
+                                  uint64_t* state, uint64_t inc) {
+    if (n < 0 || !state) return MAG_CUDA_E_INVALID;
+    mcu_device* d = dev_of(dvc);
+    ext_out(d, r, (size_t)n * 4);
+    const float span = max - min; /* rounded to f32 as the host generator does */
+    int rc = mcu_launch_fill_pcg(r, n, 0, min, span, *state, inc, d->stream);
+    if (rc) return rc;
+    if (n) mcu_count_launches(1);
+    *state = mcu_pcg_advance(*state, inc, (uint64_t)n);
+    return 0;
+}
+
+int mag_cuda_fill_normal_pcg_f32(mag_compute_device_t* dvc, float* r, int64_t n, float mean, float stddev,
+                                 uint64_t* state, uint64_t inc) {
+    if (n < 0 || (n & 1) || !state) return MAG_CUDA_E_INVALID; /* pairs, as the core asserts */
+    mcu_device* d = dev_of(dvc);
+    ext_out(d, r, (size_t)n * 4);
+    int rc = mcu_launch_fill_pcg(r, n, 1, mean, stddev, *state, inc, d->stream);
+    if (rc) return rc;
+    if (n) mcu_count_launches(1);
+    *state = mcu_pcg_advance(*state, inc, (uint64_t)n);
+    return 0;
+}
+
+int mag_cuda_fill_f32(mag_compute_device_t* dvc, float* r, int64_t n, float x) {
+    if (n < 0) return MAG_CUDA_E_INVALID;
+    mcu_device* d = dev_of(dvc);
+    ext_out(d, r, (size_t)n * 4);
+    int rc = mcu_launch_fill_const(r, n, x, d->stream);
+    if (!rc && n) mcu_count_launches(1);
     return rc;
 }
 

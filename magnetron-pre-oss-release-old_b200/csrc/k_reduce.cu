@@ -233,15 +233,14 @@ cudaError_t launch_rows_op(float* r, const float* x, int64_t rows, int64_t cols,
 //
 // Rows stay in registers between the three phases (max, exp + double sum,
 // divide), so HBM sees one read and one write per element.  Short rows
-// (<= 2048) get one warp each; longer rows are split into slices of 16384
-// elements, one 512-thread CTA per slice, and the slices of a row form a
+// (<= 2048) get one warp each; longer rows are split into slices of 8192
+// elements (one 256-thread CTA each) when 16 of them cover the row, else of
+// 16384 elements (512 threads), and the slices of a row form a
 // thread-block cluster that combines the row max and sum through distributed
 // shared memory.
 
 constexpr int kWarpRowMax = 2048;  // rows up to this length get one warp (16 float4 per lane at most)
-constexpr int kSliceThreads = 512;
-constexpr int kSliceVec = 8;      // float4 per thread: 16384 elements per CTA
-constexpr int kSlice = kSliceThreads * 4 * kSliceVec;
+constexpr int kSliceVec = 8;      // float4 per thread: slices of 32 x threads elements
 
 // The reference's scalar tail calls libm expf; kept out of line so the common
 // vector-lane path is never if-converted into evaluating it.
@@ -328,9 +327,11 @@ __global__ void __launch_bounds__(256, V <= 4 ? 4 : (V <= 8 ? 3 : 1)) softmax_ro
     }
 }
 
-// One CTA per 16384-element slice; the cluster spans the row.
-__global__ void __launch_bounds__(kSliceThreads, 2) softmax_rows_slices(float* __restrict__ r,
-                                                                     const float* __restrict__ x, uint32_t cols) {
+// One CTA per slice of 32*T elements; the cluster spans the row.
+template <int kSliceThreads>
+__global__ void __launch_bounds__(kSliceThreads, 1024 / kSliceThreads) softmax_rows_slices(
+    float* __restrict__ r, const float* __restrict__ x, uint32_t cols) {
+    constexpr int kSlice = kSliceThreads * 4 * kSliceVec;
     __shared__ float sh_max[32];
     __shared__ double sh_sum[32];
     __shared__ float slot_max;
@@ -455,15 +456,19 @@ extern "C" int mcu_launch_softmax_rows(float* r, const float* x, int64_t rows, i
         else softmax_rows_warp<16><<<grid, 256, 0, st>>>(r, x, (uint64_t)rows, (uint32_t)cols);
         return (int)cudaGetLastError();
     }
-    const int64_t csize = (cols + kSlice - 1) / kSlice;
+    // slices of 8192 elements (256 threads) when the row fits 16 of them, else 16384 (512 threads)
+    const bool small = cols <= 16 * 8192;
+    const int64_t slice = small ? 8192 : 16384;
+    const int64_t csize = (cols + slice - 1) / slice;
+    auto kern = small ? softmax_rows_slices<256> : softmax_rows_slices<512>;
     if (csize <= 16 && rows * csize < (1ll << 31)) {
         if (csize > 8) {
-            cudaError_t e = cudaFuncSetAttribute(softmax_rows_slices, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+            cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
             if (e != cudaSuccess) return (int)e;
         }
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3((unsigned)(rows * csize));
-        cfg.blockDim = dim3(kSliceThreads);
+        cfg.blockDim = dim3(small ? 256 : 512);
         cfg.dynamicSmemBytes = 0;
         cfg.stream = st;
         cudaLaunchAttribute attr[1];
@@ -473,7 +478,7 @@ extern "C" int mcu_launch_softmax_rows(float* r, const float* x, int64_t rows, i
         attr[0].val.clusterDim.z = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        cudaError_t e = cudaLaunchKernelEx(&cfg, softmax_rows_slices, r, x, (uint32_t)cols);
+        cudaError_t e = cudaLaunchKernelEx(&cfg, kern, r, x, (uint32_t)cols);
         if (e == cudaSuccess) return (int)cudaSuccess;
         cudaGetLastError();  // cluster shape not schedulable here: use the three-pass kernel
     }

@@ -31,6 +31,13 @@ int mcu_launch_reduce(int op, float* r, const float* x, const int64_t* x_dims, c
 int mcu_launch_reduce_rows(int op, float* r, const float* x, int64_t rows, int64_t cols, cudaStream_t st);
 int mcu_launch_softmax_rows(float* r, const float* x, int64_t rows, int64_t cols, cudaStream_t st);
 
+/* k_fill.cu: PCG stream fills (normal != 0: Box-Muller pairs; p0, p1 = mean, stddev,
+ * else p0, p1 = min, max - min) and constant fills. */
+uint64_t mcu_pcg_advance(uint64_t state, uint64_t inc, uint64_t n);
+int mcu_launch_fill_pcg(float* r, int64_t n, int normal, float p0, float p1, uint64_t state, uint64_t inc,
+                        cudaStream_t st);
+int mcu_launch_fill_const(float* r, int64_t n, float x, cudaStream_t st);
+
 /* k_matmul_exact.cu: R[b][i*r_ld + j] = (accumulate ? R : 0) + sum_k X[b][i*K+k]*Y[b][k*N+j],
  * summed k = 0..K-1 in order with separately rounded multiply and add. */
 int mcu_launch_matmul_exact(float* r, const float* x, const float* y, int64_t batch, int64_t M, int64_t K,

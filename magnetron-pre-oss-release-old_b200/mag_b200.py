@@ -128,6 +128,11 @@ def load_library(path: str = LIB_PATH):
         "mag_cuda_kernel_launches": ([], C.c_uint64),
         "mag_cuda_matmul_skinny_f32_noalloc": ([vp, vp, vp, vp, i64, i64, i64], C.c_int),
         "mag_cuda_matmul_skinny_noalloc_limit": ([], C.c_size_t),
+        "mag_cuda_fill_uniform_pcg_f32": ([vp, vp, i64, C.c_float, C.c_float, C.POINTER(C.c_uint64), C.c_uint64],
+                                          C.c_int),
+        "mag_cuda_fill_normal_pcg_f32": ([vp, vp, i64, C.c_float, C.c_float, C.POINTER(C.c_uint64), C.c_uint64],
+                                         C.c_int),
+        "mag_cuda_fill_f32": ([vp, vp, i64, C.c_float], C.c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
@@ -135,6 +140,18 @@ def load_library(path: str = LIB_PATH):
         fn.restype = res
     _lib = L
     return L
+
+
+class Pcg:
+    """A context's PCG stream: mag_prng_init, PCG branch (magnetron/magnetron.c:797-808).
+    Fills draw from it in order and advance it, as the reference context's generator does."""
+
+    def __init__(self, seed: int):
+        seed &= (1 << 64) - 1
+        if not seed:  # the reference derives a default seed from the context's address
+            seed = 0x853C49E6748FEA9B ^ id(self)
+        self.state = C.c_uint64(seed ^ 0x853C49E6748FEA9B)
+        self.inc = 0xDA3E39CB94B95BDB
 
 
 def i64x6(v) -> C.Array:
@@ -310,6 +327,18 @@ class Device:
 
     def exec(self, r: Tensor):
         self.dev.eager_exec_fwd(self.p, r.ptr)
+
+    # ---- seeded fills (mag_tensor_fill*, magnetron/magnetron.c:1826-1876, on the device)
+    def fill(self, t: Tensor, x: float):
+        check(self.L.mag_cuda_fill_f32(self.p, t.data_ptr, t.numel, x), "fill")
+
+    def fill_random_uniform(self, t: Tensor, lo: float, hi: float, gen: "Pcg"):
+        check(self.L.mag_cuda_fill_uniform_pcg_f32(self.p, t.data_ptr, t.numel, lo, hi, C.byref(gen.state), gen.inc),
+              "fill_random_uniform")
+
+    def fill_random_normal(self, t: Tensor, mean: float, std: float, gen: "Pcg"):
+        check(self.L.mag_cuda_fill_normal_pcg_f32(self.p, t.data_ptr, t.numel, mean, std, C.byref(gen.state), gen.inc),
+              "fill_random_normal")
 
     def graph_exec(self, root: Tensor, fused: bool = False):
         fn = self.L.mag_cuda_graph_exec_fused if fused else self.L.mag_cuda_graph_exec

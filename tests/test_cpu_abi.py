@@ -56,3 +56,12 @@ def test_init_without_gpu_returns_null():
         pytest.skip("a GPU is present")
     L = MB.load_library()
     assert not L.mag_init_device_cuda(None)
+
+
+def test_pcg_seeding_matches_oracle():
+    """The host-side stream handle starts where the reference context's PCG does."""
+    from harness import oracle
+    o = oracle()
+    for seed in (1, 0x5EED0001, 2**63 + 5):
+        g, ref = MB.Pcg(seed), o.stream(seed)
+        assert (g.state.value, g.inc) == (ref.g.state, ref.g.inc)
