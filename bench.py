@@ -477,6 +477,70 @@ def sweep(dev, MB, torch, local):
     return out
 
 
+def run_storage(args):
+    """.magnetron save/load of one f32 tensor of --size elements between HBM and a file
+    (page-cache resident: the load follows the save), beside pinned-memory DMA peaks and
+    the reference's own CPU save/load of the same tensor on this host."""
+    import tempfile
+    import torch
+    import mag_b200 as MB
+    dev = MB.Device()
+    n = args.size or (1 << 28)
+    nbytes = 4 * n
+    tmp = tempfile.mkdtemp(prefix="magsto")
+    path = os.path.join(tmp, "t.magnetron")
+    x = dev.tensor((n,))
+    g = MB.Pcg(7)
+    dev.fill_random_uniform(x, -1.0, 1.0, g)
+    dev.sync()
+    reps = max(1, args.steps)
+
+    def rate(fn):
+        fn()
+        ts = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            fn()
+            ts.append(time.perf_counter() - t0)
+        return nbytes / statistics.median(ts) / 1e9
+
+    out = {"case": "storage", "size": n, "bytes": nbytes, "unit": "GB/s", "file_dir": tmp}
+    out["save"] = rate(lambda: dev.save(path, [x]))
+    y = dev.tensor((n,))
+    arr = (ctypes.c_void_p * 1)(y.ptr)
+    out["load"] = rate(lambda: MB.check(dev.L.mag_cuda_tensor_load(dev.p, path.encode(), arr, 1), "load"))
+    assert np.array_equal(y.read(1 << 20), x.read(1 << 20))
+    host = torch.empty(n, dtype=torch.float32).pin_memory()
+    gpu = torch.empty(n, dtype=torch.float32, device="cuda")
+    out["pinned_h2d"] = rate(lambda: (gpu.copy_(host, non_blocking=True), torch.cuda.synchronize()))
+    out["pinned_d2h"] = rate(lambda: (host.copy_(gpu, non_blocking=True), torch.cuda.synchronize()))
+    del host, gpu
+    if not args.no_cpu_baseline:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        from oracle import RefLib, REF_SO
+        if os.path.exists(REF_SO):
+            R = RefLib()
+            R.L.mag_tensor_save.argtypes = [ctypes.c_void_p, ctypes.c_char_p]
+            R.L.mag_tensor_load.argtypes = [ctypes.c_void_p, ctypes.c_char_p]
+            R.L.mag_tensor_load.restype = ctypes.c_void_p
+            t = R.tensor_nd((n,))
+            rpath = os.path.join(tmp, "ref.magnetron").encode()
+            out["reference_cpu_save"] = rate(lambda: R.L.mag_tensor_save(t, rpath))
+
+            def ref_load():
+                R.free(R.L.mag_tensor_load(R.ctx, rpath))
+            out["reference_cpu_load"] = rate(ref_load)
+            R.free(t)
+            R.close()
+    for k in list(out):
+        if isinstance(out[k], float):
+            out[k] = round(out[k], 2)
+    for f in os.listdir(tmp):
+        os.remove(os.path.join(tmp, f))
+    os.rmdir(tmp)
+    print(json.dumps(out), flush=True)
+
+
 def run_case(args):
     """One kernel family, a few launches, for profilers: `--case gemm|add|sigmoid|sum|softmax`."""
     import torch
@@ -776,7 +840,7 @@ def main():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--case", default=None, choices=["gemm", "layer", "add", "sigmoid", "sum", "softmax", "softmax1k", "skinny", "tile", "bcast2",
-                                                      "fill_uniform", "fill_normal", "fill_const"],
+                                                      "fill_uniform", "fill_normal", "fill_const", "storage"],
                     help="run one kernel family for a profiler instead of the benchmark")
     ap.add_argument("--size", type=int, default=None)
     ap.add_argument("--sweep-full", action="store_true", help="measure every other BASELINE configuration")
@@ -787,7 +851,7 @@ def main():
         return
     if args.case:
         args.size = args.size or (8192 if args.case in ("gemm", "layer") else 1 << 28)
-        run_case(args)
+        run_storage(args) if args.case == "storage" else run_case(args)
         return
     if args.warmup < 3:
         args.warmup = 3

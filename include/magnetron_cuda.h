@@ -42,6 +42,7 @@ extern "C" {
 #define MAG_CUDA_E_DEVICE_WAIT 10002 /* a kernel's bounded wait expired (device status word) */
 #define MAG_CUDA_E_UNSUPPORTED 10003 /* op not available (e.g. the reference panics with NYI) */
 #define MAG_CUDA_E_SCRATCH_LIMIT 10004 /* the call needs more than the fixed scratch array holds */
+#define MAG_CUDA_E_IO 10005            /* a file could not be opened, read or written */
 
 /* ---- drop-in device interface (magnetron/magnetron_cuda.cuh:14-15) ---- */
 
@@ -131,6 +132,41 @@ MAG_CUDA_EXPORT int mag_cuda_fill_normal_pcg_f32(mag_compute_device_t* dvc, floa
                                                  float stddev, uint64_t* state, uint64_t inc);
 /* r[0..n) = x (mag_tensor_fill, magnetron/magnetron.c:1826-1842, for any x). */
 MAG_CUDA_EXPORT int mag_cuda_fill_f32(mag_compute_device_t* dvc, float* r, int64_t n, float x);
+
+/* ---- .magnetron storage with device-resident data ----
+ * The storage v1 format of magnetron/magnetron.c:2688-3011, byte for byte.  The reference
+ * serialises only CPU tensors (:2878, :2912 assert a CPU context); these stream tensor data
+ * between the file and device memory in pinned chunks on several host threads.
+ * Paths must end in ".magnetron" (mag_sto_has_mag_ext, :2925-2929).  Where the reference
+ * panics (I/O failure, truncated data) these return MAG_CUDA_E_IO / MAG_CUDA_E_INVALID. */
+typedef struct mag_cuda_sto_entry {
+    char name[64];   /* MAG_MAX_TENSOR_NAME_LEN bytes, NUL forced at [63] as the reader does */
+    uint32_t flags;  /* tensor flags, 4 bits */
+    uint32_t dtype;  /* 0 = f32 */
+    int64_t rank;    /* 1..6 */
+    int64_t shape[6];
+    uint64_t offset; /* byte offset of the tensor's data in the file */
+    uint64_t bytes;  /* bytes of data */
+} mag_cuda_sto_entry;
+
+/* The reader's header checks (mag_sto_read_buffered, :2891-2916) over the first `avail`
+ * bytes of a file of `total` bytes; the first min(cap, count) entries are filled. */
+MAG_CUDA_EXPORT int mag_cuda_sto_parse(const void* buf, size_t avail, size_t total, mag_cuda_sto_entry* entries,
+                                       uint32_t cap, uint32_t* n_tensors, uint32_t* version);
+/* The file header and tensor headers the writer emits for these tensors
+ * (mag_sto_write_buffered, :2861-2876); *size receives the header bytes. */
+MAG_CUDA_EXPORT int mag_cuda_sto_write_header(const mag_tensor_t* const* tensors, uint32_t n, void* buf, size_t cap,
+                                              size_t* size);
+/* mag_tensor_save (:2931-2950) for n >= 1 tensors whose storage is on this device. */
+MAG_CUDA_EXPORT int mag_cuda_tensor_save(mag_compute_device_t* dvc, const char* path,
+                                         const mag_tensor_t* const* tensors, uint32_t n);
+/* The header phase of mag_tensor_load (:2952-2977): the file's tensor directory. */
+MAG_CUDA_EXPORT int mag_cuda_sto_read_directory(const char* path, mag_cuda_sto_entry* entries, uint32_t cap,
+                                                uint32_t* n_tensors, uint32_t* version);
+/* The data phase: the first n stored tensors into device tensors of the stored dtype, rank
+ * and shape, whose name and flags are then set from the file as the reader does (:2907-2908). */
+MAG_CUDA_EXPORT int mag_cuda_tensor_load(mag_compute_device_t* dvc, const char* path, mag_tensor_t* const* tensors,
+                                         uint32_t n);
 
 /* ---- allocation-free entry point (no counterpart in the reference) ----
  * R[M,N] = X[M,K] Y[K,N] for 1 <= M <= 16, the same split-K kernels as

@@ -23,6 +23,7 @@
  */
 #include "mag_cuda_abi.h"
 #include "magnetron_cuda.h"
+#include "mcu_device.h"
 #include "mcu_kernels.h"
 
 #include <cuda_runtime_api.h>
@@ -652,6 +653,11 @@ static void ext_out(mcu_device* d, void* p, size_t bytes) {
 }
 
 int mag_cuda_device_ordinal(mag_compute_device_t* dvc) { return dev_of(dvc)->ordinal; }
+
+int mcu_dev_ordinal(mag_compute_device_t* dvc) { return dev_of(dvc)->ordinal; }
+int mcu_dev_sync(mag_compute_device_t* dvc) { return mag_cuda_synchronize(dvc); }
+void mcu_dev_in(mag_compute_device_t* dvc, const void* p) { ext_in(dev_of(dvc), p); }
+void mcu_dev_out(mag_compute_device_t* dvc, void* p, size_t bytes) { ext_out(dev_of(dvc), p, bytes); }
 
 int mag_cuda_set_matmul_mode(mag_compute_device_t* dvc, int mode) {
     if (mode < 0 || mode > 2) return MAG_CUDA_E_INVALID;

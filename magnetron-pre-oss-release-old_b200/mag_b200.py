@@ -45,7 +45,7 @@ REDUCE = {"MEAN", "MIN", "MAX", "SUM"}
 INPLACE_OK = UNARY | SCALAR | BINARY | {"MATMUL"}
 TFLAG_OWNER, TFLAG_VIEW = 1, 2
 
-E_INVALID, E_DEVICE_WAIT, E_UNSUPPORTED, E_SCRATCH_LIMIT = 10001, 10002, 10003, 10004
+E_INVALID, E_DEVICE_WAIT, E_UNSUPPORTED, E_SCRATCH_LIMIT, E_IO = 10001, 10002, 10003, 10004, 10005
 
 
 # ---------------------------------------------------------------- ABI structs
@@ -133,6 +133,13 @@ def load_library(path: str = LIB_PATH):
         "mag_cuda_fill_normal_pcg_f32": ([vp, vp, i64, C.c_float, C.c_float, C.POINTER(C.c_uint64), C.c_uint64],
                                          C.c_int),
         "mag_cuda_fill_f32": ([vp, vp, i64, C.c_float], C.c_int),
+        "mag_cuda_sto_parse": ([vp, C.c_size_t, C.c_size_t, vp, C.c_uint32, C.POINTER(C.c_uint32),
+                                C.POINTER(C.c_uint32)], C.c_int),
+        "mag_cuda_sto_write_header": ([vp, C.c_uint32, vp, C.c_size_t, C.POINTER(C.c_size_t)], C.c_int),
+        "mag_cuda_tensor_save": ([vp, C.c_char_p, vp, C.c_uint32], C.c_int),
+        "mag_cuda_sto_read_directory": ([C.c_char_p, vp, C.c_uint32, C.POINTER(C.c_uint32), C.POINTER(C.c_uint32)],
+                                        C.c_int),
+        "mag_cuda_tensor_load": ([vp, C.c_char_p, vp, C.c_uint32], C.c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
@@ -140,6 +147,39 @@ def load_library(path: str = LIB_PATH):
         fn.restype = res
     _lib = L
     return L
+
+
+class StoEntry(C.Structure):
+    """mag_cuda_sto_entry: one tensor of a .magnetron file's directory."""
+    _fields_ = [("name", C.c_char * 64), ("flags", C.c_uint32), ("dtype", C.c_uint32), ("rank", C.c_int64),
+                ("shape", C.c_int64 * 6), ("offset", C.c_uint64), ("bytes", C.c_uint64)]
+
+    @property
+    def dims(self):
+        return tuple(int(self.shape[i]) for i in range(int(self.rank)))
+
+
+def sto_parse(buf: bytes, total: int | None = None):
+    """The reader's header checks over a .magnetron image (no GPU needed).
+    Returns (version, entries) or raises CudaError with the library's code."""
+    L = load_library()
+    total = len(buf) if total is None else total
+    n, ver = C.c_uint32(0), C.c_uint32(0)
+    cap = 64
+    ents = (StoEntry * cap)()
+    check(L.mag_cuda_sto_parse(buf, len(buf), total, ents, cap, C.byref(n), C.byref(ver)), "sto_parse")
+    return int(ver.value), list(ents[:min(cap, n.value)])
+
+
+def sto_header(tensors) -> bytes:
+    """Header bytes the writer emits for these tensors (no GPU needed)."""
+    L = load_library()
+    arr = (C.c_void_p * len(tensors))(*[t.ptr for t in tensors])
+    size = C.c_size_t(0)
+    check(L.mag_cuda_sto_write_header(arr, len(tensors), None, 0, C.byref(size)), "sto_write_header")
+    out = C.create_string_buffer(size.value)
+    check(L.mag_cuda_sto_write_header(arr, len(tensors), out, size.value, C.byref(size)), "sto_write_header")
+    return out.raw[:size.value]
 
 
 class Pcg:
@@ -221,6 +261,16 @@ class Tensor:
     @property
     def data_ptr(self) -> int:
         return int(self.t.storage.base)
+
+    @property
+    def name(self) -> str:
+        return self.t.name.decode()
+
+    @name.setter
+    def name(self, v: str):  # mag_tensor_set_name: strncpy into 64 bytes, NUL at [63] (magnetron/magnetron.c:1968-1971)
+        raw = v.encode()[:63]
+        C.memset(C.addressof(self.t) + TensorT.name.offset, 0, 64)
+        C.memmove(C.addressof(self.t) + TensorT.name.offset, raw, len(raw))
 
     @property
     def shape(self):
@@ -327,6 +377,26 @@ class Device:
 
     def exec(self, r: Tensor):
         self.dev.eager_exec_fwd(self.p, r.ptr)
+
+    # ---- .magnetron storage (mag_tensor_save / mag_tensor_load, magnetron/magnetron.c:2931-2977)
+    def save(self, path: str, tensors):
+        arr = (C.c_void_p * len(tensors))(*[t.ptr for t in tensors])
+        check(self.L.mag_cuda_tensor_save(self.p, path.encode(), arr, len(tensors)), "tensor_save")
+
+    def read_directory(self, path: str):
+        n, ver = C.c_uint32(0), C.c_uint32(0)
+        check(self.L.mag_cuda_sto_read_directory(path.encode(), None, 0, C.byref(n), C.byref(ver)), "read_directory")
+        ents = (StoEntry * max(1, n.value))()
+        check(self.L.mag_cuda_sto_read_directory(path.encode(), ents, n.value, C.byref(n), C.byref(ver)),
+              "read_directory")
+        return list(ents[:n.value])
+
+    def load(self, path: str):
+        """Every tensor of the file, as new device tensors named and flagged from the file."""
+        ts = [self.tensor(e.dims) for e in self.read_directory(path)]
+        arr = (C.c_void_p * len(ts))(*[t.ptr for t in ts])
+        check(self.L.mag_cuda_tensor_load(self.p, path.encode(), arr, len(ts)), "tensor_load")
+        return ts
 
     # ---- seeded fills (mag_tensor_fill*, magnetron/magnetron.c:1826-1876, on the device)
     def fill(self, t: Tensor, x: float):
