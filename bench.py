@@ -541,6 +541,79 @@ def run_storage(args):
     print(json.dumps(out), flush=True)
 
 
+def run_image(args):
+    """Image pixel work on a 3840 x 2160 RGB frame: decoded u8 pixels (host memory) to a planar
+    f32 tensor, with and without a resize to 1920 x 1080, and back to u8 (host memory), beside
+    the reference's own CPU code on the same pixels (through its image callbacks)."""
+    import mag_b200 as MB
+    dev = MB.Device()
+    w, h, c = 3840, 2160, 3
+    src = np.random.default_rng(5).integers(0, 256, w * h * c, dtype=np.uint8)
+    reps = max(1, args.steps)
+    out = {"case": "image", "frame": [w, h, c], "unit": "Mpixel/s"}
+
+    def rate(fn, pixels):
+        fn()
+        dev.sync()
+        ts = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            fn()
+            dev.sync()
+            ts.append(time.perf_counter() - t0)
+        return round(pixels / statistics.median(ts) / 1e6, 1)
+
+    full, half = dev.tensor((c, h, w)), dev.tensor((c, h // 2, w // 2))
+    u8 = np.empty(w * h * c, np.uint8)
+    out["load"] = rate(lambda: dev.L.mag_cuda_img_from_u8(dev.p, full.ptr, src.ctypes.data, w, h, c, 0, 0), w * h)
+    out["load_resize_1080p"] = rate(lambda: dev.L.mag_cuda_img_from_u8(dev.p, half.ptr, src.ctypes.data, w, h, c,
+                                                                       w // 2, h // 2), w * h)
+    out["save"] = rate(lambda: dev.L.mag_cuda_img_to_u8(dev.p, full.ptr, u8.ctypes.data), w * h)
+    if not args.no_cpu_baseline:
+        sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        from oracle import REF_SO
+        if os.path.exists(REF_SO):
+            import gen_images as GI
+            L = ctypes.CDLL(REF_SO)
+            vp = ctypes.c_void_p
+            L.mag_ctx_create.argtypes = [ctypes.POINTER(GI.CtxInfo)]
+            L.mag_ctx_create.restype = vp
+            L.mag_tensor_load_image.argtypes = [vp, ctypes.c_char_p, ctypes.c_int, ctypes.c_uint32, ctypes.c_uint32]
+            L.mag_tensor_load_image.restype = vp
+            L.mag_tensor_save_image.argtypes = [vp, ctypes.c_char_p]
+            L.mag_tensor_decref.argtypes = [vp]
+            L.mag_ctx_destroy.argtypes = [vp]
+
+            @GI.LOAD_FN
+            def load(path, whc, channels):
+                whc.contents[0], whc.contents[1], whc.contents[2] = w, h, c
+                return src.ctypes.data
+
+            @GI.FREE_FN
+            def free(p):
+                pass
+
+            @GI.SAVE_FN
+            def save(path, data, whc):
+                return True
+
+            info = GI.CtxInfo()
+            info.image_load_fn, info.image_load_free_fn, info.image_save_fn = load, free, save
+            ctx = L.mag_ctx_create(ctypes.byref(info))
+
+            def ref(rw, rh):
+                t = L.mag_tensor_load_image(ctx, b"frame", 0, rw, rh)
+                L.mag_tensor_decref(t)
+            out["reference_cpu_load"] = rate(lambda: ref(0, 0), w * h)
+            out["reference_cpu_load_resize_1080p"] = rate(lambda: ref(w // 2, h // 2), w * h)
+            t = L.mag_tensor_load_image(ctx, b"frame", 0, 0, 0)
+            out["reference_cpu_save"] = rate(lambda: L.mag_tensor_save_image(t, b"frame.png"), w * h)
+            L.mag_tensor_decref(t)
+            L.mag_ctx_destroy(ctx)
+    print(json.dumps(out), flush=True)
+
+
 def run_case(args):
     """One kernel family, a few launches, for profilers: `--case gemm|add|sigmoid|sum|softmax`."""
     import torch
@@ -840,7 +913,7 @@ def main():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--case", default=None, choices=["gemm", "layer", "add", "sigmoid", "sum", "softmax", "softmax1k", "skinny", "tile", "bcast2",
-                                                      "fill_uniform", "fill_normal", "fill_const", "storage"],
+                                                      "fill_uniform", "fill_normal", "fill_const", "storage", "image"],
                     help="run one kernel family for a profiler instead of the benchmark")
     ap.add_argument("--size", type=int, default=None)
     ap.add_argument("--sweep-full", action="store_true", help="measure every other BASELINE configuration")
@@ -851,7 +924,7 @@ def main():
         return
     if args.case:
         args.size = args.size or (8192 if args.case in ("gemm", "layer") else 1 << 28)
-        run_storage(args) if args.case == "storage" else run_case(args)
+        {"storage": run_storage, "image": run_image}.get(args.case, run_case)(args)
         return
     if args.warmup < 3:
         args.warmup = 3

@@ -168,6 +168,25 @@ MAG_CUDA_EXPORT int mag_cuda_sto_read_directory(const char* path, mag_cuda_sto_e
 MAG_CUDA_EXPORT int mag_cuda_tensor_load(mag_compute_device_t* dvc, const char* path, mag_tensor_t* const* tensors,
                                          uint32_t n);
 
+/* ---- image tensors on the device ----
+ * An image tensor is rank 3, shape (c, h, w), planar f32 (magnetron/magnetron.h:394-396).
+ * Results are bit-identical with the reference's CPU code for the same pixels. */
+/* The pixel work of mag_tensor_load_image (magnetron/magnetron.c:3013-3087): interleaved u8
+ * [h][w][c] (host or device memory, as the image decoder returns it) -> dst / 255, resized
+ * to rw x rh by the reference's two-pass bilinear scheme when both are nonzero.  dst has shape
+ * (c, rh, rw) or (c, h, w). */
+MAG_CUDA_EXPORT int mag_cuda_img_from_u8(mag_compute_device_t* dvc, mag_tensor_t* dst, const uint8_t* src, uint32_t w,
+                                         uint32_t h, uint32_t c, uint32_t rw, uint32_t rh);
+/* The pixel work of mag_tensor_save_image (:3089-3109): interleaved u8 [h][w][c] of
+ * (uint8_t)(x * 255) with x86 conversion semantics, into host or device memory; c in {1, 3, 4}. */
+MAG_CUDA_EXPORT int mag_cuda_img_to_u8(mag_compute_device_t* dvc, const mag_tensor_t* src, uint8_t* dst);
+/* mag_tensor_img_draw_box (:2159-2214) on a 3-channel image. */
+MAG_CUDA_EXPORT int mag_cuda_img_draw_box(mag_compute_device_t* dvc, mag_tensor_t* t, int32_t x1, int32_t y1,
+                                          int32_t x2, int32_t y2, int32_t wi, uint32_t rgb);
+/* mag_tensor_img_draw_text (:2243-2270) on a 3-channel image; size is ignored, as there. */
+MAG_CUDA_EXPORT int mag_cuda_img_draw_text(mag_compute_device_t* dvc, mag_tensor_t* t, int32_t x, int32_t y,
+                                           int32_t size, uint32_t rgb, const char* txt);
+
 /* ---- allocation-free entry point (no counterpart in the reference) ----
  * R[M,N] = X[M,K] Y[K,N] for 1 <= M <= 16, the same split-K kernels as
  * mag_cuda_matmul_f32 uses for such shapes, but it never allocates: for callers

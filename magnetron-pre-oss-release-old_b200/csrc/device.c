@@ -845,6 +845,151 @@ int mag_cuda_fill_f32(mag_compute_device_t* dvc, float* r, int64_t n, float x) {
     return rc;
 }
 
+/* ------------------------------------------------------------ images --- */
+
+/* (c, h, w) of a rank-3 image tensor (mag_tensor_image_* macros, magnetron/magnetron.h:394-396). */
+static int img_dims(const mag_tensor_t* t, int32_t* w, int32_t* h, int32_t* c) {
+    if (!t || t->rank != 3 || t->dtype != 0) return MAG_CUDA_E_INVALID;
+    if (t->shape[0] < 1 || t->shape[1] < 1 || t->shape[2] < 1 || t->shape[1] > INT32_MAX || t->shape[2] > INT32_MAX ||
+        t->shape[0] > 4)
+        return MAG_CUDA_E_INVALID;
+    *c = (int32_t)t->shape[0];
+    *h = (int32_t)t->shape[1];
+    *w = (int32_t)t->shape[2];
+    return 0;
+}
+
+static int is_device_ptr(const void* p) {
+    struct cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
+static float img_channel(uint32_t rgb, int shift) { return (float)((rgb >> shift) & 0xff) / 255.0f; }
+
+int mag_cuda_img_from_u8(mag_compute_device_t* dvc, mag_tensor_t* dst, const uint8_t* src, uint32_t w, uint32_t h,
+                         uint32_t c, uint32_t rw, uint32_t rh) {
+    int32_t tw, th, tc;
+    if (!src || !w || !h || !c || c > 4 || img_dims(dst, &tw, &th, &tc)) return MAG_CUDA_E_INVALID;
+    const int resize = rw && rh;
+    if ((uint32_t)tc != c || (uint32_t)tw != (resize ? rw : w) || (uint32_t)th != (resize ? rh : h))
+        return MAG_CUDA_E_INVALID;
+    mcu_device* d = dev_of(dvc);
+    const size_t bytes = (size_t)w * h * c;
+    const uint8_t* s = src;
+    const int host = !is_device_ptr(src);
+    if (host) { /* the decoded file is a quarter of the f32 image: move it as bytes, expand on the device */
+        uint8_t* tmp = (uint8_t*)scratch_get(d, bytes);
+        MCU_CHECK(cudaMemcpyAsync(tmp, src, bytes, cudaMemcpyHostToDevice, d->stream));
+        s = tmp;
+    }
+    ext_out(d, fptr(dst), (size_t)dst->numel * 4);
+    /* the reference's scale factors, rounded to f32 on the host as it rounds them
+     * (magnetron/magnetron.c:3028-3029) */
+    const float ws = resize ? (float)(w - 1) / (float)(rw - 1) : 0.0f;
+    const float hs = resize ? (float)(h - 1) / (float)(rh - 1) : 0.0f;
+    int rc = mcu_launch_img_from_u8(fptr(dst), s, w, h, c, resize ? rw : 0, resize ? rh : 0, ws, hs, d->stream);
+    if (rc) return rc;
+    mcu_count_launches(1);
+    if (host && host_is_pinned(src)) { /* the caller may reuse src on return */
+        cudaError_t e = cudaStreamSynchronize(d->stream);
+        if (e != cudaSuccess) return (int)e;
+    }
+    return 0;
+}
+
+int mag_cuda_img_to_u8(mag_compute_device_t* dvc, const mag_tensor_t* src, uint8_t* dst) {
+    int32_t w, h, c;
+    if (!dst || img_dims(src, &w, &h, &c) || !(c == 1 || c == 3 || c == 4)) return MAG_CUDA_E_INVALID;
+    mcu_device* d = dev_of(dvc);
+    ext_in(d, fptr(src));
+    const size_t bytes = (size_t)w * h * c;
+    const int dev_dst = is_device_ptr(dst);
+    uint8_t* out = dev_dst ? dst : (uint8_t*)scratch_get(d, bytes);
+    int rc = mcu_launch_img_to_u8(out, fptr(src), (uint32_t)w, (uint32_t)h, (uint32_t)c, d->stream);
+    if (rc) return rc;
+    mcu_count_launches(1);
+    if (!dev_dst) {
+        MCU_CHECK(cudaMemcpyAsync(dst, out, bytes, cudaMemcpyDeviceToHost, d->stream));
+        cudaError_t e = cudaStreamSynchronize(d->stream);
+        if (e != cudaSuccess) return (int)e;
+    }
+    return 0;
+}
+
+/* Ring i of a box draws something while its horizontal edge (xx1 <= xx2) or vertical edge
+ * (yy1 <= yy2) is non-empty; both bounds move monotonically with i. */
+static int box_ring_draws(int64_t i, int32_t w, int32_t h, int32_t x1, int32_t y1, int32_t x2, int32_t y2) {
+    int64_t xx1 = x1 + i, yy1 = y1 + i, xx2 = x2 - i, yy2 = y2 - i;
+    if (xx1 >= w) xx1 = w - 1;
+    if (xx2 >= w) xx2 = w - 1;
+    if (yy1 >= h) yy1 = h - 1;
+    if (yy2 >= h) yy2 = h - 1;
+    return xx1 <= xx2 || yy1 <= yy2;
+}
+
+int mag_cuda_img_draw_box(mag_compute_device_t* dvc, mag_tensor_t* t, int32_t x1, int32_t y1, int32_t x2, int32_t y2,
+                          int32_t wi, uint32_t rgb) {
+    int32_t w, h, c;
+    if (img_dims(t, &w, &h, &c) || c != 3) return MAG_CUDA_E_INVALID;
+    if (!(x2 > x1 && y2 > y1 && x1 > 0 && y1 > 0 && x2 > 0 && y2 > 0)) return MAG_CUDA_E_INVALID;
+    if (wi < 1) wi = 1;
+    int64_t lo = 0, hi = wi; /* first ring that draws nothing, by bisection */
+    while (lo < hi) {
+        const int64_t mid = lo + (hi - lo) / 2;
+        if (box_ring_draws(mid, w, h, x1, y1, x2, y2)) lo = mid + 1;
+        else hi = mid;
+    }
+    mcu_device* d = dev_of(dvc);
+    ext_out(d, fptr(t), 4); /* a partial write: pending zeros are cleared first */
+    int rc = mcu_launch_img_draw_box(fptr(t), w, h, x1, y1, x2, y2, (int32_t)lo, img_channel(rgb, 16),
+                                     img_channel(rgb, 8), img_channel(rgb, 0), d->stream);
+    if (!rc && lo) mcu_count_launches(1);
+    return rc;
+}
+
+int mag_cuda_img_draw_text(mag_compute_device_t* dvc, mag_tensor_t* t, int32_t x, int32_t y, int32_t size,
+                           uint32_t rgb, const char* txt) {
+    int32_t w, h, c;
+    if (img_dims(t, &w, &h, &c) || c != 3 || x < 0 || y < 0 || size < 8 || !txt || !*txt) return MAG_CUDA_E_INVALID;
+    const size_t len = strlen(txt);
+    int32_t* cells = (int32_t*)malloc(3 * len * sizeof(int32_t));
+    if (!cells) return MAG_CUDA_E_INVALID;
+    int32_t n = 0, lx = x, ly = y;
+    for (const unsigned char* p = (const unsigned char*)txt; *p; ++p) {
+        /* printable in the C locale; space has no pixels; '\n' returns to x one line down */
+        if (*p > 32 && *p < 127) {
+            cells[3 * n] = lx;
+            cells[3 * n + 1] = ly;
+            cells[3 * n + 2] = *p - 33;
+            ++n;
+        }
+        if (*p == '\n') {
+            lx = x;
+            ly += 14;
+        } else {
+            lx += 8;
+        }
+    }
+    mcu_device* d = dev_of(dvc);
+    int rc = 0;
+    if (n) {
+        int32_t* dev_cells = (int32_t*)scratch_get(d, (size_t)n * 3 * sizeof(int32_t));
+        /* a pageable source is staged before the call returns, so cells can be freed below */
+        MCU_CHECK(cudaMemcpyAsync(dev_cells, cells, (size_t)n * 3 * sizeof(int32_t), cudaMemcpyHostToDevice,
+                                  d->stream));
+        ext_out(d, fptr(t), 4);
+        rc = mcu_launch_img_draw_text(fptr(t), w, h, dev_cells, n, img_channel(rgb, 16), img_channel(rgb, 8),
+                                      img_channel(rgb, 0), d->stream);
+        if (!rc) mcu_count_launches(1);
+    }
+    free(cells);
+    return rc;
+}
+
 int mag_cuda_matmul_batched_f32(mag_compute_device_t* dvc, float* r, const float* x, const float* y, int64_t batch,
                                 int64_t M, int64_t K, int64_t N) {
     if (batch < 0 || M < 0 || K < 0 || N < 0) return MAG_CUDA_E_INVALID;

@@ -38,6 +38,17 @@ int mcu_launch_fill_pcg(float* r, int64_t n, int normal, float p0, float p1, uin
                         cudaStream_t st);
 int mcu_launch_fill_const(float* r, int64_t n, float x, cudaStream_t st);
 
+/* k_image.cu: planar f32 [c][h][w] <-> interleaved u8 [h][w][c] (resized to rw x rh when both
+ * are nonzero, with ws = (w-1)/(rw-1), hs = (h-1)/(rh-1) rounded to f32), box and text drawing
+ * on 3-channel images; glyphs holds (x, y, glyph index) triples. */
+int mcu_launch_img_from_u8(float* dst, const uint8_t* src, uint32_t w, uint32_t h, uint32_t c, uint32_t rw,
+                           uint32_t rh, float ws, float hs, cudaStream_t st);
+int mcu_launch_img_to_u8(uint8_t* dst, const float* src, uint32_t w, uint32_t h, uint32_t c, cudaStream_t st);
+int mcu_launch_img_draw_box(float* img, int32_t w, int32_t h, int32_t x1, int32_t y1, int32_t x2, int32_t y2,
+                            int32_t wi, float r, float g, float b, cudaStream_t st);
+int mcu_launch_img_draw_text(float* img, int32_t w, int32_t h, const int32_t* glyphs, int32_t n, float r, float g,
+                             float b, cudaStream_t st);
+
 /* k_matmul_exact.cu: R[b][i*r_ld + j] = (accumulate ? R : 0) + sum_k X[b][i*K+k]*Y[b][k*N+j],
  * summed k = 0..K-1 in order with separately rounded multiply and add. */
 int mcu_launch_matmul_exact(float* r, const float* x, const float* y, int64_t batch, int64_t M, int64_t K,

@@ -140,6 +140,10 @@ def load_library(path: str = LIB_PATH):
         "mag_cuda_sto_read_directory": ([C.c_char_p, vp, C.c_uint32, C.POINTER(C.c_uint32), C.POINTER(C.c_uint32)],
                                         C.c_int),
         "mag_cuda_tensor_load": ([vp, C.c_char_p, vp, C.c_uint32], C.c_int),
+        "mag_cuda_img_from_u8": ([vp, vp, vp, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32], C.c_int),
+        "mag_cuda_img_to_u8": ([vp, vp, vp], C.c_int),
+        "mag_cuda_img_draw_box": ([vp, vp] + [C.c_int32] * 5 + [C.c_uint32], C.c_int),
+        "mag_cuda_img_draw_text": ([vp, vp, C.c_int32, C.c_int32, C.c_int32, C.c_uint32, C.c_char_p], C.c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
@@ -397,6 +401,24 @@ class Device:
         arr = (C.c_void_p * len(ts))(*[t.ptr for t in ts])
         check(self.L.mag_cuda_tensor_load(self.p, path.encode(), arr, len(ts)), "tensor_load")
         return ts
+
+    # ---- image tensors (c, h, w) (magnetron/magnetron.c:2159-2274, 3013-3109, pixel work on the device)
+    def image_from_u8(self, src: np.ndarray, w: int, h: int, c: int, rw: int = 0, rh: int = 0) -> Tensor:
+        src = np.ascontiguousarray(src, np.uint8)
+        t = self.tensor((c, rh, rw) if rw and rh else (c, h, w))
+        check(self.L.mag_cuda_img_from_u8(self.p, t.ptr, src.ctypes.data, w, h, c, rw, rh), "img_from_u8")
+        return t
+
+    def image_to_u8(self, t: Tensor) -> np.ndarray:
+        out = np.empty(t.numel, np.uint8)
+        check(self.L.mag_cuda_img_to_u8(self.p, t.ptr, out.ctypes.data), "img_to_u8")
+        return out
+
+    def draw_box(self, t: Tensor, x1: int, y1: int, x2: int, y2: int, wi: int, rgb: int):
+        check(self.L.mag_cuda_img_draw_box(self.p, t.ptr, x1, y1, x2, y2, wi, rgb), "img_draw_box")
+
+    def draw_text(self, t: Tensor, x: int, y: int, size: int, rgb: int, txt: str):
+        check(self.L.mag_cuda_img_draw_text(self.p, t.ptr, x, y, size, rgb, txt.encode("latin-1")), "img_draw_text")
 
     # ---- seeded fills (mag_tensor_fill*, magnetron/magnetron.c:1826-1876, on the device)
     def fill(self, t: Tensor, x: float):

@@ -271,3 +271,67 @@ class RefLib:
         if self.ctx:
             self.L.mag_ctx_destroy(self.ctx)
             self.ctx = None
+
+
+# ---------------------------------------------------------------------------- images
+# numpy float32 restatements (every op separately rounded, as the reference's x86 build
+# computes them) of the reference's image pixel work.
+
+def img_load(src: np.ndarray, w: int, h: int, c: int, rw: int = 0, rh: int = 0) -> np.ndarray:
+    """mag_tensor_load_image's conversion and bilinear resize (magnetron/magnetron.c:3013-3087)."""
+    f = np.float32
+    ori = (src.reshape(h, w, c).astype(f) / f(255.0)).transpose(2, 0, 1)  # planar [c][h][w]
+    if not (rw and rh):
+        return np.ascontiguousarray(ori).reshape(-1)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        ws = f(w - 1) / f(rw - 1)
+        hs = f(h - 1) / f(rh - 1)
+    part = np.empty((c, h, rw), f)
+    for cc in range(rw):
+        if cc == rw - 1 or w == 1:
+            part[:, :, cc] = ori[:, :, w - 1]
+        else:
+            sx = f(cc) * ws
+            ix = int(sx)
+            dx = sx - f(ix)
+            part[:, :, cc] = (f(1) - dx) * ori[:, :, ix] + dx * ori[:, :, ix + 1]
+    dst = np.empty((c, rh, rw), f)
+    for r in range(rh):
+        with np.errstate(invalid="ignore"):
+            sy = f(r) * hs
+        iy = 0 if np.isnan(sy) else int(sy)
+        dy = sy - f(iy)
+        dst[:, r, :] = (f(1) - dy) * part[:, iy, :]
+        if not (r == rh - 1 or h == 1):
+            dst[:, r, :] = dst[:, r, :] + dy * part[:, iy + 1, :]
+    return dst.reshape(-1)
+
+
+def img_save(x: np.ndarray, w: int, h: int, c: int) -> np.ndarray:
+    """mag_tensor_save_image's conversion (magnetron/magnetron.c:3089-3109): (uint8_t)(x * 255)
+    as x86-64 compiles it, truncation to int32 (INT32_MIN when out of range or NaN), low byte."""
+    v = (x.astype(np.float32) * np.float32(255.0)).reshape(c, h * w)
+    ok = (v >= -2147483648.0) & (v < 2147483648.0)
+    q = np.where(ok, np.trunc(np.where(ok, v, 0)), -2147483648.0).astype(np.int64)
+    return (q & 0xFF).astype(np.uint8).T.reshape(-1)
+
+
+def img_draw_box(img: np.ndarray, w: int, h: int, x1, y1, x2, y2, wi, rgb) -> np.ndarray:
+    """mag_tensor_img_draw_box (magnetron/magnetron.c:2159-2214) on planar RGB."""
+    out = img.astype(np.float32).copy()
+    col = [np.float32((rgb >> s) & 0xFF) / np.float32(255.0) for s in (16, 8, 0)]
+    plane = w * h
+
+    def put(x, y):
+        o = x + y * w
+        for k in range(3):
+            out[o + k * plane] = col[k]
+    for i in range(max(1, wi)):
+        xx1, yy1, xx2, yy2 = min(x1 + i, w - 1), min(y1 + i, h - 1), min(x2 - i, w - 1), min(y2 - i, h - 1)
+        for j in range(xx1, xx2 + 1):
+            put(j, yy1)
+            put(j, yy2)
+        for j in range(yy1, yy2 + 1):
+            put(xx1, j)
+            put(xx2, j)
+    return out
