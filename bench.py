@@ -53,6 +53,19 @@ def peaks():
         return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
 
 
+# The tensor-core matmul's operand split (MAG_CUDA_TC_SPLIT; the backend's default is f16).
+SPLIT_NAME = "3xTF32" if os.environ.get("MAG_CUDA_TC_SPLIT") == "tf32" else "3xFP16 (scaled)"
+
+
+def split_roofline(pk, pk_src):
+    """Effective f32-product peak of the split: three tensor-core products per f32 product at
+    the kind::f16 rate (the measured bf16 GEMM rate) or the kind::tf32 rate (half of it)."""
+    bf16 = pk.get("bf16_tflops_sustained", pk["bf16_tflops"])
+    if SPLIT_NAME == "3xTF32":
+        return bf16 / 2.0 / 3.0, f"3xTF32 effective = {pk_src} bf16 sustained / 2 (TF32 rate) / 3 (products)"
+    return bf16 / 3.0, f"3xFP16 effective = {pk_src} bf16 sustained (f16 rate) / 3 (products)"
+
+
 class ClockSampler:
     """SM clock and clock-event (throttle) reasons of one GPU, read through NVML
     every 5 ms while the timed region runs (read-only queries)."""
@@ -401,8 +414,7 @@ def run_ours(args):
     value = GLOBAL_BATCH * args.steps / (ms / 1e3)
     e2e_value = GLOBAL_BATCH * args.steps / (e2e_ms / 1e3)
     pk, pk_src = peaks()
-    tf32_peak = pk.get("bf16_tflops_sustained", pk["bf16_tflops"]) / 2.0
-    three_tf32_peak = tf32_peak / 3.0
+    split_peak, split_note = split_roofline(pk, pk_src)
     mm_flop_per_step = 2.0 * rows * (N_HID * D_IN * D_HID + D_HID * D_OUT)
     mm_ms_per_step = (us_mm / 1e3) / args.steps if args.steps else 0.0
     achieved = (mm_flop_per_step / (mm_ms_per_step / 1e3)) / 1e12 if mm_ms_per_step else 0.0
@@ -415,13 +427,13 @@ def run_ours(args):
                 "h2d_bytes_per_step": rows * D_IN * 4 * world,
                 "d2h_bytes_per_step": world * rows * D_OUT * 4},
         "gpu_launches": launches_timed,
-        "roofline": {"bound": "tensor", "achieved": achieved, "peak": three_tf32_peak, "unit": "TFLOP/s",
-                     "frac": achieved / three_tf32_peak if three_tf32_peak else None,
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": split_peak, "unit": "TFLOP/s",
+                     "frac": achieved / split_peak if split_peak else None,
                      "traffic": 8 * (1.450e9 + 0.363e9) * rows / 65536,
                      "traffic_note": "DRAM bytes per hidden-layer GEMM launch: ncu capture at 8192 rows "
                                      "(profiles/gemm_3xtf32_fused_layer_8192x4096.md) scaled by rows",
                      "kernel": "MATMUL op (per-op CUDA events inside the replayed graph)",
-                     "peak_note": f"3xTF32 effective = {pk_src} bf16 sustained / 2 (TF32 rate) / 3 (products)",
+                     "peak_note": split_note,
                      "matmul_ms_per_step": mm_ms_per_step, "matmul_launches": n_mm},
         "clocks": clk,
         "device": dev.name,
@@ -721,7 +733,7 @@ def run_sweep_full(args):
     dev = MB.Device()
     pk, pk_src = peaks()
     hbm = pk["hbm_gbs"]
-    tf = pk.get("bf16_tflops_sustained", pk["bf16_tflops"]) / 2.0 / 3.0
+    tf, _ = split_roofline(pk, pk_src)
     stream = torch.cuda.ExternalStream(dev.stream)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     rows_out = []
@@ -821,7 +833,7 @@ def run_sweep_full(args):
         c_ = dev.tensor((m * m,))
         ms = timeit(lambda: dev.L.mag_cuda_matmul_f32(dev.p, c_.data_ptr, a.data_ptr, a.data_ptr, m, m, m),
                     5 if m < 16384 else 2)
-        rec("matmul", f"square {m}^3 (3xTF32 tcgen05)", ms, 2.0 * m ** 3 / 1e12, "TFLOP/s", tf)
+        rec("matmul", f"square {m}^3 ({SPLIT_NAME} tcgen05)", ms, 2.0 * m ** 3 / 1e12, "TFLOP/s", tf)
         a.free()
         c_.free()
     k = nn = 4096
@@ -837,7 +849,7 @@ def run_sweep_full(args):
     bt, mm = 64, 512
     a, c_ = filled(bt * mm * mm, lambda c: c * (mm ** -0.25)), dev.tensor((bt * mm * mm,))
     ms = timeit(lambda: dev.L.mag_cuda_matmul_batched_f32(dev.p, c_.data_ptr, a.data_ptr, a.data_ptr, bt, mm, mm, mm), 5)
-    rec("matmul", "batched 64 x [512x512 . 512x512] (3xTF32 tcgen05, batch-indexed tiles)", ms,
+    rec("matmul", f"batched 64 x [512x512 . 512x512] ({SPLIT_NAME} tcgen05, batch-indexed tiles)", ms,
         2.0 * bt * mm ** 3 / 1e12, "TFLOP/s", tf)
     a.free()
     c_.free()
@@ -899,7 +911,7 @@ def run_sweep_full(args):
                 print(json.dumps({"cpu_reference_1thread": c}), flush=True)
     if args.out:
         with open(args.out, "w") as f:
-            json.dump({"gpu": rows_out, "cpu_reference_1thread": cpu, "peaks": {"hbm_gbs": hbm, "3xtf32_tflops": tf,
+            json.dump({"gpu": rows_out, "cpu_reference_1thread": cpu, "peaks": {"hbm_gbs": hbm, "split_tflops": tf, "split": SPLIT_NAME,
                                                                                  "source": pk_src},
                        "device": dev.name}, f, indent=1)
 

@@ -56,6 +56,12 @@ MAG_CUDA_EXPORT void mag_destroy_device_cuda(mag_compute_device_t* dvc);
 
 /* ---- device handle ---- */
 MAG_CUDA_EXPORT int mag_cuda_device_ordinal(mag_compute_device_t* dvc);
+/* Operand split of the tensor-core matmul: f16 hi/lo with exact power-of-two row/column
+ * scaling on kind::f16 (the default, twice the tensor rate), or tf32 hi/lo on kind::tf32
+ * (MAG_CUDA_TC_SPLIT=tf32 at init).  Both keep 22 significant bits per operand. */
+#define MAG_CUDA_TC_SPLIT_TF32 0
+#define MAG_CUDA_TC_SPLIT_F16 1
+MAG_CUDA_EXPORT int mag_cuda_set_tc_split(mag_compute_device_t* dvc, int split);
 MAG_CUDA_EXPORT void* mag_cuda_stream(mag_compute_device_t* dvc);          /* cudaStream_t */
 MAG_CUDA_EXPORT int mag_cuda_synchronize(mag_compute_device_t* dvc);       /* waits, reports async errors */
 MAG_CUDA_EXPORT int mag_cuda_last_error(mag_compute_device_t* dvc);        /* sticky error of the eager path */

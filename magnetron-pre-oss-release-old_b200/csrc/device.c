@@ -101,6 +101,7 @@ typedef struct mcu_device {
     int managed;      /* MAG_CUDA_MANAGED=1: unified memory, synchronous ops */
     int eager_zero;   /* MAG_CUDA_EAGER_ZERO=1: memset on allocation */
     int matmul_mode;  /* MAG_CUDA_MATMUL: 0 auto, 1 exact, 2 tensor cores */
+    int tc_f16;       /* tensor-core split: 1 scaled f16 (kind::f16), 0 tf32 (MAG_CUDA_TC_SPLIT=tf32) */
     int sticky_error;
     int capturing;
     mcu_block* tab;
@@ -466,8 +467,8 @@ static int exec_node(mcu_device* d, mag_tensor_t* r) {
                 rc = mcu_launch_matmul_skinny(fptr(r), px, py, M, K, N, r_ld, scratch, st);
                 if (!rc) mcu_count_launches(2);
             } else if (path == MM_TC) {
-                rc = mcu_launch_matmul_tc(fptr(r), px, py, M, K, N, scratch, d->d_status, st);
-                if (!rc) mcu_count_launches(3);
+                rc = mcu_launch_matmul_tc(fptr(r), px, py, M, K, N, scratch, d->d_status, st, d->tc_f16);
+                if (!rc) mcu_count_launches(d->tc_f16 ? 4 : 3);
             } else {
                 rc = mcu_launch_matmul_exact(fptr(r), px, py, 1, M, K, N, r_ld, accumulate, st);
                 if (!rc) mcu_count_launches(1);
@@ -565,6 +566,8 @@ mag_compute_device_t* mag_init_device_cuda(mag_ctx_t* ctx) {
     d->eager_zero = env_int("MAG_CUDA_EAGER_ZERO", 0);
     const char* mm = getenv("MAG_CUDA_MATMUL");
     d->matmul_mode = !mm ? 0 : (!strcmp(mm, "exact") ? 1 : (!strcmp(mm, "tc") ? 2 : 0));
+    const char* ts = getenv("MAG_CUDA_TC_SPLIT");
+    d->tc_f16 = !(ts && !strcmp(ts, "tf32"));
     MCU_CHECK(cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking));
     cudaMemPool_t pool;
     MCU_CHECK(cudaDeviceGetDefaultMemPool(&pool, ordinal));
@@ -665,6 +668,11 @@ int mag_cuda_set_matmul_mode(mag_compute_device_t* dvc, int mode) {
     dev_of(dvc)->matmul_mode = mode;
     return 0;
 }
+int mag_cuda_set_tc_split(mag_compute_device_t* dvc, int split) {
+    if (split != MAG_CUDA_TC_SPLIT_TF32 && split != MAG_CUDA_TC_SPLIT_F16) return MAG_CUDA_E_INVALID;
+    dev_of(dvc)->tc_f16 = split == MAG_CUDA_TC_SPLIT_F16;
+    return 0;
+}
 void* mag_cuda_stream(mag_compute_device_t* dvc) { return (void*)dev_of(dvc)->stream; }
 size_t mag_cuda_memory_in_use(mag_compute_device_t* dvc) { return dev_of(dvc)->bytes_live; }
 int mag_cuda_last_error(mag_compute_device_t* dvc) { return dev_of(dvc)->sticky_error; }
@@ -739,8 +747,8 @@ int mag_cuda_matmul_f32(mag_compute_device_t* dvc, float* r, const float* x, con
         if (!rc) mcu_count_launches(2);
     } else if (path == MM_TC) {
         rc = mcu_launch_matmul_tc(r, x, y, M, K, N, scratch_get(d, mcu_matmul_tc_scratch_bytes(M, K, N)),
-                                  d->d_status, d->stream);
-        if (!rc) mcu_count_launches(3);
+                                  d->d_status, d->stream, d->tc_f16);
+        if (!rc) mcu_count_launches(d->tc_f16 ? 4 : 3);
     } else {
         rc = mcu_launch_matmul_exact(r, x, y, 1, M, K, N, N, 0, d->stream);
         if (!rc) mcu_count_launches(1);
@@ -1001,8 +1009,8 @@ int mag_cuda_matmul_batched_f32(mag_compute_device_t* dvc, float* r, const float
     if (d->matmul_mode != 1 && mcu_matmul_tc_supported() && M >= 128 && N >= 64 && K >= 32 &&
         (double)batch * M * N * K >= 1.0e9) {
         void* scratch = scratch_get(d, mcu_matmul_tc_batched_scratch_bytes(batch, M, K, N));
-        rc = mcu_launch_matmul_tc_batched(r, x, y, batch, M, K, N, scratch, d->d_status, d->stream);
-        if (!rc) mcu_count_launches(3);
+        rc = mcu_launch_matmul_tc_batched(r, x, y, batch, M, K, N, scratch, d->d_status, d->stream, d->tc_f16);
+        if (!rc) mcu_count_launches(d->tc_f16 ? 4 : 3);
     } else {
         rc = mcu_launch_matmul_exact(r, x, y, batch, M, K, N, N, 0, d->stream);
         if (!rc) mcu_count_launches(1);
@@ -1185,7 +1193,7 @@ static size_t plan_fusion(mcu_device* d, mag_tensor_t** nodes, size_t n, mag_ten
         /* the next MATMUL reads this layer's output: hand it the split operand */
         mag_tensor_t* out = plan[i].out;
         const int64_t N = m->shape[1];
-        if (out != root && users[last] == 1 && N % 32 == 0) {
+        if (!d->tc_f16 && out != root && users[last] == 1 && N % 32 == 0) { /* the f16 split scales whole rows itself */
             size_t in2 = user_of[last];
             mag_tensor_t* m2 = nodes[in2];
             if (m2->op_inputs[0] == out && m2->op_inputs[1] != out && tc_matmul_ok(d, m2)) {
@@ -1231,8 +1239,9 @@ static int exec_planned_matmul(mcu_device* d, mag_tensor_t* m, const mcu_plan_it
             ep.kp_out = (N + 31) / 32 * 32;
         }
     }
-    int rc = mcu_launch_matmul_tc_ex(fptr(out), fptr(x), fptr(y), M, K, N, scratch, d->d_status, d->stream, &ep);
-    if (!rc) mcu_count_launches(it->a_split >= 0 ? 2 : 3);
+    int rc = mcu_launch_matmul_tc_ex(fptr(out), fptr(x), fptr(y), M, K, N, scratch, d->d_status, d->stream, &ep,
+                                     d->tc_f16);
+    if (!rc) mcu_count_launches(d->tc_f16 ? 4 : (it->a_split >= 0 ? 2 : 3));
     return rc;
 }
 
@@ -1241,7 +1250,8 @@ static int graph_exec_impl(mag_compute_device_t* dvc, mag_tensor_t* root, int fu
     mcu_device* d = dev_of(dvc);
     size_t n = 0;
     mag_tensor_t** nodes = topo_order(root, &n);
-    uint64_t sig = graph_signature(nodes, n);
+    /* the matmul path and split kind are baked into a captured graph: part of its key */
+    uint64_t sig = graph_signature(nodes, n) ^ ((uint64_t)(1 + d->tc_f16 + 2 * d->matmul_mode) * 0x9E3779B97F4A7C15ull);
     mcu_graph* g = d->graphs;
     while (g && (g->root != root || g->fused != fuse)) g = g->next;
     if (g && g->sig == sig) {

@@ -1,4 +1,4 @@
-// k_matmul_tc.cu - f32 matmul on the sm_100a tensor cores with a 3xTF32 split.
+// k_matmul_tc.cu - f32 matmul on the sm_100a tensor cores with a three-product split.
 //
 // R[M,N] = X[M,K] Y[K,N], all row-major f32 (the buffer interpretation of
 // mag_blas_matmul_f32, magnetron/magnetron_cpu.c:2151-2185).  A TF32 product
@@ -10,20 +10,29 @@
 // about 2^-22 relative, so results stay within f32 rounding of the exact
 // product (the matmul tolerance is 1e-5 relative, norm-wise).
 //
+// The same split in f16 (11 significant bits, like tf32) runs the kind::f16
+// tensor-core path at twice the kind::tf32 rate.  f16's narrow exponent range is
+// handled by exact power-of-two scaling: each row of X and each column of Y is
+// scaled so its largest magnitude lies in [2^14, 2^15) before the split, and the
+// epilogue multiplies the sum by 2^-(row exponent + column exponent).  Errors are
+// then bounded relative to the row and column maxima, as for tf32.
+//
 // Kernels
-//   split_rows     X -> Xhi, Xlo     [M][Kp]    (Kp = K rounded up to 32, zero padded)
-//   split_cols_t   Y -> Yhi^T, Ylo^T [N][Kp]    (transposed so both operands are K-major)
-//   gemm_3xtf32    persistent, warp-specialised:
-//     warp 0      TMA producer: 64B-swizzled 128x16 (X) and BNx16 (Y) tiles, hi and lo,
-//                 into a 4-deep shared-memory ring (mbarrier complete_tx)
-//     warp 1      TMEM allocator; lane 0 issues tcgen05.mma kind::tf32 (M=128, N=BN, K=8),
-//                 three per k-step, and tcgen05.commit to free ring slots / publish tiles
-//     warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns -> registers -> global,
-//                 from one of two TMEM accumulators so it overlaps the next tile's MMAs
+//   split_rows[_f16]     X -> Xhi, Xlo     [M][Kp]  (Kp = K rounded up to 32, zero padded)
+//   split_cols_t[_f16]   Y -> Yhi^T, Ylo^T [N][Kp]  (transposed so both operands are K-major)
+//   gemm_3x              persistent, warp-specialised:
+//     warp 0      TMA producer: 64B-swizzled 128-row (X) and BN-row (Y) tiles of 64 bytes of K
+//                 (16 tf32 or 32 f16), hi and lo, into a 4-deep shared-memory ring
+//     warp 1      TMEM allocator; lane 0 issues tcgen05.mma kind::tf32 or kind::f16
+//                 (M=128, N=BN, 32 bytes of K), three per k-step, and tcgen05.commit to
+//                 free ring slots / publish accumulators
+//     warps 2..9  epilogue: tcgen05.ld 32 lanes x 32 columns -> registers -> global,
+//                 from one of two TMEM accumulators so it overlaps the next segment's MMAs
 // Every mbarrier wait is bounded: on expiry the kernel records a status code,
 // all roles leave their loops, and TMEM is released before the CTA exits.
 // No load uses cluster multicast; the same kernel serves multi-GPU runs.
 #include <cuda.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 #include <cstdint>
@@ -32,7 +41,9 @@
 namespace {
 
 constexpr int BM = 128;          // UMMA M (one CTA, TMEM lanes 0..127)
-constexpr int BK = 16;           // f32 per 64-byte swizzle row (one ring stage holds K = 16)
+constexpr int ROW_BYTES = 64;    // K bytes per swizzled smem row: one ring stage holds 64 bytes of K
+constexpr int BK = 16;           // f32 per 64-byte row (the tf32 split)
+constexpr int BK16 = 32;         // f16 per 64-byte row (the f16 split)
 constexpr int KPAD = 32;         // K padding of the split operands
 constexpr int kEpiWarps = 8;   // two per TMEM lane quadrant, each owning half of the tile's columns
 constexpr int kThreads = 32 * (2 + kEpiWarps);
@@ -103,14 +114,24 @@ __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* ba
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-// D(tmem) (+)= A(smem) * B(smem)^T, kind::tf32, issued by one thread.
-__device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                          uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+// D(tmem) (+)= A(smem) * B(smem)^T, kind::tf32 or kind::f16 (both operands the same
+// type), issued by one thread.
+template <bool F16>
+__device__ __forceinline__ void umma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                     uint32_t accumulate) {
+    if constexpr (F16) {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+            "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+    } else {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "setp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+            "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+    }
 }
 
 // Arrives on `bar` once every tcgen05.mma issued so far by this thread has completed.
@@ -119,10 +140,10 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
                  : "memory");
 }
 
-// Shared-memory matrix descriptor: K-major rows of BK*4 bytes, swizzled (64B
-// or 128B), 8-row atoms 8*BK*4 bytes apart.
+// Shared-memory matrix descriptor: K-major rows of ROW_BYTES bytes, swizzled (64B
+// or 128B), 8-row atoms 8*ROW_BYTES bytes apart.
 __device__ __forceinline__ uint64_t sw_desc(uint32_t saddr) {
-    constexpr uint32_t row_bytes = BK * 4;
+    constexpr uint32_t row_bytes = ROW_BYTES;
     uint64_t d = 0;
     d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
     d |= (uint64_t)1 << 16;                         // leading byte offset (unused for swizzled K-major)
@@ -132,9 +153,17 @@ __device__ __forceinline__ uint64_t sw_desc(uint32_t saddr) {
     return d;
 }
 
-// Instruction descriptor, kind::tf32: D f32, A/B tf32, both K-major, M=128, N=BN.
-__host__ __device__ constexpr uint32_t idesc_tf32(int n) {
-    return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+// Instruction descriptor: D f32, A/B tf32 (format 2, kind::tf32) or f16 (format 0,
+// kind::f16), both K-major, M=128, N=BN.
+__host__ __device__ constexpr uint32_t idesc_3x(int n, bool f16) {
+    const uint32_t fmt = f16 ? 0u : 2u;
+    return (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+// v * 2^-s, exact unless the result is subnormal or overflows (then correctly rounded).
+__device__ __forceinline__ float unscale(float v, int s) {
+    if (s >= -126 && s <= 126) return __fmul_rn(v, __int_as_float((127 - s) << 23));
+    return scalbnf(v, -s);
 }
 
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
@@ -168,8 +197,8 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb
 // ------------------------------------------------------------ the GEMM
 template <int BN, int STAGES>
 struct Cfg {
-    static constexpr int A_BYTES = BM * BK * 4;
-    static constexpr int B_BYTES = BN * BK * 4;
+    static constexpr int A_BYTES = BM * ROW_BYTES;
+    static constexpr int B_BYTES = BN * ROW_BYTES;
     static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
     static constexpr int TMEM_COLS = 2 * BN;
     static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 512;
@@ -180,10 +209,12 @@ struct Cfg {
 // product, its tf32 hi/lo split in [M][Kp_out] layout.
 struct Epi {
     const float* bias;  // same row-major index as the result, or null
-    float* out_hi;      // split output (null: none)
+    float* out_hi;      // split output (null: none; tf32 split only)
     float* out_lo;
     int64_t kp_out;
     int act;            // 0 none, 1 GELU (the reference's vector-lane formula)
+    const int* row_exp; // f16 split: power-of-two exponents of X's rows ([B*M]) and Y's columns ([B*N])
+    const int* col_exp;
 };
 
 __device__ __forceinline__ float rna_tf32_dev(float x) {
@@ -199,9 +230,9 @@ __device__ __forceinline__ float gelu_lane(float x) {
     return __fmul_rn(0.5f, __fmul_rn(x, b));
 }
 
-template <int BN, int STAGES, bool FUSED>
+template <int BN, int STAGES, bool FUSED, bool F16>
 __global__ void __maxnreg__(168)
-    gemm_3xtf32(const __grid_constant__ CUtensorMap map_xhi, const __grid_constant__ CUtensorMap map_xlo,
+    gemm_3x(const __grid_constant__ CUtensorMap map_xhi, const __grid_constant__ CUtensorMap map_xlo,
                 const __grid_constant__ CUtensorMap map_yhi, const __grid_constant__ CUtensorMap map_ylo,
                 float* __restrict__ r, int M, int N, int Kp, int64_t ldr, int* status, const Epi epi,
                 int seg_kb, int batch) {
@@ -223,7 +254,8 @@ __global__ void __maxnreg__(168)
     const int num_n = (N + BN - 1) / BN;
     const int tiles_per_batch = num_m * num_n;
     const int tiles = tiles_per_batch * batch;  // batch b's operands start at rows b*M (X) and b*N (Y)
-    const int nk = Kp / BK;
+    constexpr int KE = F16 ? BK16 : BK;          // K elements per ring stage
+    const int nk = Kp / KE;
     Abort ab{abort_flag, status};
 
     if (threadIdx.x == 0) {
@@ -266,16 +298,16 @@ __global__ void __maxnreg__(168)
                     if (!mbar_wait(&empty[s], (round & 1) ^ 1, ab, 1)) goto done;
                     uint8_t* st = ring + s * C::STAGE_BYTES;
                     mbar_expect_tx(&full[s], C::STAGE_BYTES);
-                    tma_load_2d(&map_xhi, &full[s], st, kb * BK, xrow);
-                    tma_load_2d(&map_xlo, &full[s], st + C::A_BYTES, kb * BK, xrow);
-                    tma_load_2d(&map_yhi, &full[s], st + 2 * C::A_BYTES, kb * BK, yrow);
-                    tma_load_2d(&map_ylo, &full[s], st + 2 * C::A_BYTES + C::B_BYTES, kb * BK, yrow);
+                    tma_load_2d(&map_xhi, &full[s], st, kb * KE, xrow);
+                    tma_load_2d(&map_xlo, &full[s], st + C::A_BYTES, kb * KE, xrow);
+                    tma_load_2d(&map_yhi, &full[s], st + 2 * C::A_BYTES, kb * KE, yrow);
+                    tma_load_2d(&map_ylo, &full[s], st + 2 * C::A_BYTES + C::B_BYTES, kb * KE, yrow);
                 }
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {  // ---- MMA issuer: one TMEM accumulator per K segment, two in flight
-            constexpr uint32_t idesc = idesc_tf32(BN);
+            constexpr uint32_t idesc = idesc_3x(BN, F16);
             uint32_t it = 0, gseg = 0;
             for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
                 for (int kb0 = 0; kb0 < nk; kb0 += seg_kb, ++gseg) {
@@ -290,14 +322,14 @@ __global__ void __maxnreg__(168)
                         tc_fence_after();
                         const uint32_t base = smem_u32(ring + s * C::STAGE_BYTES);
 #pragma unroll
-                        for (int kk = 0; kk < BK / 8; ++kk) {
+                        for (int kk = 0; kk < ROW_BYTES / 32; ++kk) {  // one MMA consumes 32 bytes of K
                             const uint64_t xhi = sw_desc(base + kk * 32);
                             const uint64_t xlo = sw_desc(base + C::A_BYTES + kk * 32);
                             const uint64_t yhi = sw_desc(base + 2 * C::A_BYTES + kk * 32);
                             const uint64_t ylo = sw_desc(base + 2 * C::A_BYTES + C::B_BYTES + kk * 32);
-                            umma_tf32(d, xlo, yhi, idesc, (kb != kb0 || kk != 0) ? 1u : 0u);
-                            umma_tf32(d, xhi, ylo, idesc, 1);
-                            umma_tf32(d, xhi, yhi, idesc, 1);
+                            umma<F16>(d, xlo, yhi, idesc, (kb != kb0 || kk != 0) ? 1u : 0u);
+                            umma<F16>(d, xhi, ylo, idesc, 1);
+                            umma<F16>(d, xhi, yhi, idesc, 1);
                         }
                         umma_commit(&empty[s]);
                     }
@@ -350,11 +382,30 @@ __global__ void __maxnreg__(168)
             const int colh = nb * BN + h * HC;
             float* out = r + (int64_t)bt * M * ldr + (int64_t)row * ldr + colh;
             const bool vec = ((ldr & 3) == 0) && ((((uintptr_t)r) & 15) == 0);
+            int ea = 0;
+            if constexpr (F16) ea = epi.row_exp[(int64_t)bt * M + row];
 #pragma unroll
             for (int c = 0; c < HC / 32; ++c) {
                 float* v = sum + c * 32;
                 const int cb = colh + c * 32;
                 const bool full = cb + 32 <= N;
+                if constexpr (F16) {  // undo the operands' power-of-two scaling
+                    const int* ce = epi.col_exp + (int64_t)bt * N + cb;
+                    if (full && ((((int64_t)bt * N) & 3) == 0)) {  // 16-byte aligned exponent groups
+#pragma unroll
+                        for (int j = 0; j < 32; j += 4) {
+                            const int4 e4 = *(const int4*)(ce + j);
+                            v[j] = unscale(v[j], ea + e4.x);
+                            v[j + 1] = unscale(v[j + 1], ea + e4.y);
+                            v[j + 2] = unscale(v[j + 2], ea + e4.z);
+                            v[j + 3] = unscale(v[j + 3], ea + e4.w);
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (cb + j < N) v[j] = unscale(v[j], ea + ce[j]);
+                    }
+                }
                 if constexpr (FUSED) {
                     if (epi.bias) {
                         const float* pb = epi.bias + (int64_t)row * N + cb;
@@ -477,6 +528,117 @@ __global__ void __launch_bounds__(256) split_cols_t(const float* __restrict__ y,
     }
 }
 
+// f16 split with power-of-two scaling: a row (or column) with largest magnitude
+// m = f * 2^E, f in [1, 2), is multiplied by 2^(14 - E) so it peaks in [2^14, 2^15),
+// inside f16's range with 2^-24 absolute resolution left for the lo parts.
+__device__ __forceinline__ int scale_exp(float amax) {
+    if (!(amax > 0.0f) || isinf(amax)) return 0;  // zero row, or inf/NaN that no scaling keeps finite
+    int e = 14 - ilogbf(amax);
+    return e > 126 ? 126 : e;  // 2^e stays a normal f32
+}
+
+__device__ __forceinline__ uint32_t pack2(__half a, __half b) {
+    return (uint32_t)__half_as_ushort(a) | ((uint32_t)__half_as_ushort(b) << 16);
+}
+
+__device__ __forceinline__ void split_f16(float v, float scale, __half& hi, __half& lo) {
+    const float s = __fmul_rn(v, scale);  // exact: a power of two
+    hi = __float2half_rn(s);
+    lo = __float2half_rn(__fsub_rn(s, __half2float(hi)));  // the difference is exact in f32
+}
+
+// X[M][K] -> hi/lo [M][Kp] f16 and row_exp[M]: one warp per row, the row read twice
+// (the second read hits L2).
+__global__ void __launch_bounds__(256) split_rows_f16(const float* __restrict__ x, __half* __restrict__ hi,
+                                                      __half* __restrict__ lo, int* __restrict__ row_exp, int64_t M,
+                                                      int64_t K, int64_t Kp) {
+    const int64_t m = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (m >= M) return;
+    const float* xr = x + m * K;
+    const bool vec = (K % 4 == 0) && ((((uintptr_t)x) & 15) == 0);
+    float amax = 0.0f;
+    if (vec) {
+        for (int64_t k = lane * 4; k < K; k += 128) {
+            const float4 t = *(const float4*)(xr + k);
+            amax = fmaxf(amax, fmaxf(fmaxf(fabsf(t.x), fabsf(t.y)), fmaxf(fabsf(t.z), fabsf(t.w))));
+        }
+    } else {
+        for (int64_t k = lane; k < K; k += 32) amax = fmaxf(amax, fabsf(xr[k]));
+    }
+    // (fmaxf skips NaN: a NaN element stays NaN through the split and its outputs are NaN)
+#pragma unroll
+    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const int e = scale_exp(amax);
+    const float scale = __int_as_float((127 + e) << 23);
+    if (lane == 0) row_exp[m] = e;
+    __half* hr = hi + m * Kp;
+    __half* lr = lo + m * Kp;
+    for (int64_t k = lane * 4; k < Kp; k += 128) {
+        float v[4];
+        if (vec && k + 4 <= K) {
+            const float4 t = __ldcs((const float4*)(xr + k));
+            v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+        } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) v[j] = (k + j < K) ? xr[k + j] : 0.0f;
+        }
+        __half h[4], l[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) split_f16(v[j], scale, h[j], l[j]);
+        *(uint2*)(hr + k) = make_uint2(pack2(h[0], h[1]), pack2(h[2], h[3]));
+        *(uint2*)(lr + k) = make_uint2(pack2(l[0], l[1]), pack2(l[2], l[3]));
+    }
+}
+
+// Column maxima of Y[b][K][N] as f32 bits (|y| compares as an unsigned integer; NaN above inf).
+__global__ void __launch_bounds__(256) col_absmax(const float* __restrict__ y, unsigned* __restrict__ cmax, int64_t K,
+                                                  int64_t N) {
+    const int64_t n = (int64_t)blockIdx.x * 256 + threadIdx.x;
+    if (n >= N) return;
+    y += (int64_t)blockIdx.z * K * N;
+    const int64_t k0 = (int64_t)blockIdx.y * 128, k1 = k0 + 128 < K ? k0 + 128 : K;
+    unsigned m = 0;
+    for (int64_t k = k0; k < k1; ++k) m = max(m, __float_as_uint(y[k * N + n]) & 0x7FFFFFFFu);
+    atomicMax(cmax + (int64_t)blockIdx.z * N + n, m);
+}
+
+// Y[K][N] -> hi/lo transposed [N][Kp] f16 through a 32x32 shared tile, scaled per column;
+// col_exp[N] written by the first k-block.
+__global__ void __launch_bounds__(256) split_cols_t_f16(const float* __restrict__ y, const unsigned* __restrict__ cmax,
+                                                        __half* __restrict__ hi, __half* __restrict__ lo,
+                                                        int* __restrict__ col_exp, int64_t K, int64_t N, int64_t Kp) {
+    __shared__ float tile[32][33];
+    __shared__ float scl[32];
+    y += (int64_t)blockIdx.z * K * N;
+    hi += (int64_t)blockIdx.z * N * Kp;
+    lo += (int64_t)blockIdx.z * N * Kp;
+    cmax += (int64_t)blockIdx.z * N;
+    col_exp += (int64_t)blockIdx.z * N;
+    const int64_t k0 = (int64_t)blockIdx.y * 32, n0 = (int64_t)blockIdx.x * 32;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+    if (threadIdx.x < 32 && n0 + tx < N) {
+        const unsigned b = cmax[n0 + tx];
+        const int e = b > 0x7F800000u ? 0 : scale_exp(__uint_as_float(b));
+        scl[tx] = __int_as_float((127 + e) << 23);
+        if (blockIdx.y == 0) col_exp[n0 + tx] = e;
+    }
+    for (int j = ty; j < 32; j += 8) {
+        const int64_t k = k0 + j, n = n0 + tx;
+        tile[j][tx] = (k < K && n < N) ? y[k * N + n] : 0.0f;
+    }
+    __syncthreads();
+    for (int j = ty; j < 32; j += 8) {
+        const int64_t n = n0 + j, k = k0 + tx;
+        if (n < N && k < Kp) {
+            __half h, l;
+            split_f16(tile[tx][j], scl[j], h, l);
+            hi[n * Kp + k] = h;
+            lo[n * Kp + k] = l;
+        }
+    }
+}
+
 // ------------------------------------------------------------ host side
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -490,37 +652,49 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-// 2-D map over a [rows][Kp] f32 array, box = box_rows x 32, 128-byte swizzle.
-bool make_map(CUtensorMap* m, const float* base, int64_t rows, int64_t kp, int box_rows) {
+// 2-D map over a [rows][Kp] array of f32 or f16, box = box_rows x 64 bytes, 64-byte swizzle.
+bool make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t kp, int box_rows, bool f16) {
     auto fn = encode_fn();
     if (!fn) return false;
+    const int es = f16 ? 2 : 4;
     cuuint64_t dims[2] = {(cuuint64_t)kp, (cuuint64_t)rows};
-    cuuint64_t strides[1] = {(cuuint64_t)(kp * 4)};
-    cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(kp * es)};
+    cuuint32_t box[2] = {(cuuint32_t)(ROW_BYTES / es), (cuuint32_t)box_rows};
     cuuint32_t estr[2] = {1, 1};
-    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void*)base, dims, strides, box, estr,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, BK == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+    CUresult r = fn(m, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void*)base, dims,
+                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
 
 int64_t round_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
 
+// Scratch of one product: split operands, and for the f16 split the row/column
+// exponents and column maxima.  Sized for the tf32 split, which needs the most.
 struct Layout {
     int64_t kp;
-    size_t xhi, xlo, yhi, ylo, total;
+    size_t xhi, xlo, yhi, ylo, rexp, cexp, cmax, total;
 };
 
-Layout layout(int64_t M, int64_t K, int64_t N) {
+Layout layout(int64_t M, int64_t K, int64_t N, bool f16) {
     Layout l;
     l.kp = round_up(K < 1 ? 1 : K, KPAD);
-    size_t xs = (size_t)round_up(M * l.kp * 4, 1024), ys = (size_t)round_up(N * l.kp * 4, 1024);
+    const int es = f16 ? 2 : 4;
+    size_t xs = (size_t)round_up(M * l.kp * es, 1024), ys = (size_t)round_up(N * l.kp * es, 1024);
     l.xhi = 0;
     l.xlo = xs;
     l.yhi = 2 * xs;
     l.ylo = 2 * xs + ys;
-    l.total = 2 * xs + 2 * ys;
+    l.rexp = 2 * xs + 2 * ys;
+    l.cexp = l.rexp + (size_t)round_up(M * 4, 256);
+    l.cmax = l.cexp + (size_t)round_up(N * 4, 256);
+    l.total = f16 ? l.cmax + (size_t)round_up(N * 4, 256) : 2 * xs + 2 * ys;
     return l;
+}
+
+size_t scratch_bytes(int64_t M, int64_t K, int64_t N) {
+    const size_t a = layout(M, K, N, false).total, b = layout(M, K, N, true).total;
+    return a > b ? a : b;
 }
 
 constexpr int kBN = 256;
@@ -529,15 +703,27 @@ constexpr int kStages = 4;
 // K per TMEM accumulation segment (MAG_CUDA_TC_SEGMENT, default 256).  Tensor-core
 // f32 accumulation truncates; restarting the accumulator every segment and
 // adding segments with round-to-nearest bounds that error by the segment length
-// instead of K.  0 = one segment spanning K.
-int segment_kb() {
-    static int v = -1;
-    if (v < 0) {
+// instead of K.  0 = one segment spanning K.  Returned in ring stages.
+int segment_kb(bool f16) {
+    static int k = -2;
+    if (k == -2) {
         const char* e = getenv("MAG_CUDA_TC_SEGMENT");
-        int k = (e && *e) ? atoi(e) : 256;
-        v = k <= 0 ? (1 << 30) : (k + BK - 1) / BK;
+        k = (e && *e) ? atoi(e) : 256;
     }
-    return v;
+    const int ke = f16 ? BK16 : BK;
+    return k <= 0 ? (1 << 30) : (k + ke - 1) / ke;
+}
+
+template <bool FUSED, bool F16>
+int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c, const CUtensorMap& d, float* r,
+                int64_t M, int64_t N, int64_t kp, int* status, const Epi& epi, int64_t B, int grid, cudaStream_t st) {
+    using C = Cfg<kBN, kStages>;
+    auto kern = gemm_3x<kBN, kStages, FUSED, F16>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (e != cudaSuccess) return (int)e;
+    kern<<<grid, kThreads, C::SMEM, st>>>(a, b, c, d, r, (int)M, (int)N, (int)kp, (int64_t)N, status, epi,
+                                          segment_kb(F16), (int)B);
+    return (int)cudaGetLastError();
 }
 
 }  // namespace
@@ -547,82 +733,92 @@ extern "C" int mcu_matmul_tc_supported(void) {
     return encode_fn() != nullptr;
 }
 
-extern "C" size_t mcu_matmul_tc_scratch_bytes(int64_t M, int64_t K, int64_t N) { return layout(M, K, N).total; }
+extern "C" size_t mcu_matmul_tc_scratch_bytes(int64_t M, int64_t K, int64_t N) { return scratch_bytes(M, K, N); }
 
 static int launch_tc(float* r, const float* x, const float* y, int64_t B, int64_t M, int64_t K, int64_t N,
-                     void* scratch, int* status, cudaStream_t st, const mcu_tc_epilogue* ep);
+                     void* scratch, int* status, cudaStream_t st, const mcu_tc_epilogue* ep, int f16);
 
 extern "C" int mcu_launch_matmul_tc_ex(float* r, const float* x, const float* y, int64_t M, int64_t K, int64_t N,
-                                       void* scratch, int* status, cudaStream_t st, const mcu_tc_epilogue* ep) {
-    return launch_tc(r, x, y, 1, M, K, N, scratch, status, st, ep);
+                                       void* scratch, int* status, cudaStream_t st, const mcu_tc_epilogue* ep,
+                                       int f16) {
+    return launch_tc(r, x, y, 1, M, K, N, scratch, status, st, ep, f16);
 }
 
 extern "C" size_t mcu_matmul_tc_batched_scratch_bytes(int64_t B, int64_t M, int64_t K, int64_t N) {
-    return layout(B * M, K, B * N).total;
+    return scratch_bytes(B * M, K, B * N);
 }
 
 extern "C" int mcu_launch_matmul_tc_batched(float* r, const float* x, const float* y, int64_t B, int64_t M, int64_t K,
-                                            int64_t N, void* scratch, int* status, cudaStream_t st) {
-    return launch_tc(r, x, y, B, M, K, N, scratch, status, st, nullptr);
+                                            int64_t N, void* scratch, int* status, cudaStream_t st, int f16) {
+    return launch_tc(r, x, y, B, M, K, N, scratch, status, st, nullptr, f16);
 }
 
 static int launch_tc(float* r, const float* x, const float* y, int64_t B, int64_t M, int64_t K, int64_t N,
-                     void* scratch, int* status, cudaStream_t st, const mcu_tc_epilogue* ep) {
+                     void* scratch, int* status, cudaStream_t st, const mcu_tc_epilogue* ep, int f16) {
     if (B <= 0 || M <= 0 || N <= 0) return (int)cudaSuccess;
     if (B * M >= (1ll << 31) || B * N >= (1ll << 31) || K >= (1ll << 21) || !scratch) return (int)cudaErrorInvalidValue;
     if (B > 1 && ep) return (int)cudaErrorInvalidValue;
-    const Layout l = layout(B * M, K, B * N);
+    const Layout l = layout(B * M, K, B * N, f16 != 0);
     char* base = (char*)scratch;
-    float* xhi = (float*)(base + l.xhi);
-    float* xlo = (float*)(base + l.xlo);
-    float* yhi = (float*)(base + l.yhi);
-    float* ylo = (float*)(base + l.ylo);
-    const bool presplit = ep && ep->a_hi && ep->a_lo;
+    void* xhi = base + l.xhi;
+    void* xlo = base + l.xlo;
+    void* yhi = base + l.yhi;
+    void* ylo = base + l.ylo;
+    int* rexp = (int*)(base + l.rexp);
+    int* cexp = (int*)(base + l.cexp);
+    unsigned* cmax = (unsigned*)(base + l.cmax);
+    // the tf32 split can take X already split by the previous layer's epilogue; the f16
+    // split scales whole rows, so it always splits X itself
+    const bool presplit = !f16 && ep && ep->a_hi && ep->a_lo;
     if (presplit) {
-        xhi = (float*)ep->a_hi;
-        xlo = (float*)ep->a_lo;
+        xhi = (void*)ep->a_hi;
+        xlo = (void*)ep->a_lo;
+    } else if (f16) {
+        split_rows_f16<<<(unsigned)((B * M + 7) / 8), 256, 0, st>>>(x, (__half*)xhi, (__half*)xlo, rexp, B * M, K,
+                                                                   l.kp);
     } else {
         int64_t n = B * M * (l.kp / 4);  // X of all batches is one (B*M) x K row-major matrix
         int64_t g = (n + 255) / 256;
         if (g > 8 * sm_count()) g = 8 * sm_count();
-        split_rows<<<(unsigned)g, 256, 0, st>>>(x, xhi, xlo, B * M, K, l.kp);
+        split_rows<<<(unsigned)g, 256, 0, st>>>(x, (float*)xhi, (float*)xlo, B * M, K, l.kp);
     }
-    {
+    if (f16) {
+        cudaError_t e = cudaMemsetAsync(cmax, 0, (size_t)(B * N) * 4, st);
+        if (e != cudaSuccess) return (int)e;
+        dim3 gm((unsigned)((N + 255) / 256), (unsigned)((K + 127) / 128), (unsigned)B);
+        col_absmax<<<gm, 256, 0, st>>>(y, cmax, K, N);
         dim3 grid((unsigned)((N + 31) / 32), (unsigned)(l.kp / 32), (unsigned)B);
-        split_cols_t<<<grid, 256, 0, st>>>(y, yhi, ylo, K, N, l.kp);
+        split_cols_t_f16<<<grid, 256, 0, st>>>(y, cmax, (__half*)yhi, (__half*)ylo, cexp, K, N, l.kp);
+    } else {
+        dim3 grid((unsigned)((N + 31) / 32), (unsigned)(l.kp / 32), (unsigned)B);
+        split_cols_t<<<grid, 256, 0, st>>>(y, (float*)yhi, (float*)ylo, K, N, l.kp);
     }
     CUtensorMap mxh, mxl, myh, myl;
-    if (!make_map(&mxh, xhi, B * M, l.kp, BM) || !make_map(&mxl, xlo, B * M, l.kp, BM) ||
-        !make_map(&myh, yhi, B * N, l.kp, kBN) || !make_map(&myl, ylo, B * N, l.kp, kBN))
+    const bool h = f16 != 0;
+    if (!make_map(&mxh, xhi, B * M, l.kp, BM, h) || !make_map(&mxl, xlo, B * M, l.kp, BM, h) ||
+        !make_map(&myh, yhi, B * N, l.kp, kBN, h) || !make_map(&myl, ylo, B * N, l.kp, kBN, h))
         return (int)cudaErrorInvalidValue;
-    using C = Cfg<kBN, kStages>;
     const int64_t tiles = B * ((M + BM - 1) / BM) * ((N + kBN - 1) / kBN);
     const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
     Epi epi{};
-    const bool fused = ep && (ep->bias || ep->act || ep->out_hi);
+    epi.row_exp = rexp;
+    epi.col_exp = cexp;
+    const bool fused = ep && (ep->bias || ep->act || (ep->out_hi && !f16));
     if (fused) {
-        if (ep->out_hi && (N % 32 != 0 || ep->kp_out != round_up(N, KPAD))) return (int)cudaErrorInvalidValue;
+        if (!f16 && ep->out_hi && (N % 32 != 0 || ep->kp_out != round_up(N, KPAD))) return (int)cudaErrorInvalidValue;
         epi.bias = ep->bias;
-        epi.out_hi = ep->out_hi;
-        epi.out_lo = ep->out_lo;
+        epi.out_hi = f16 ? nullptr : ep->out_hi;
+        epi.out_lo = f16 ? nullptr : ep->out_lo;
         epi.kp_out = ep->kp_out;
         epi.act = ep->act;
-        auto kern = gemm_3xtf32<kBN, kStages, true>;
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-        if (e != cudaSuccess) return (int)e;
-        kern<<<grid, kThreads, C::SMEM, st>>>(mxh, mxl, myh, myl, r, (int)M, (int)N, (int)l.kp, (int64_t)N, status, epi,
-                                              segment_kb(), (int)B);
-    } else {
-        auto kern = gemm_3xtf32<kBN, kStages, false>;
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-        if (e != cudaSuccess) return (int)e;
-        kern<<<grid, kThreads, C::SMEM, st>>>(mxh, mxl, myh, myl, r, (int)M, (int)N, (int)l.kp, (int64_t)N, status, epi,
-                                              segment_kb(), (int)B);
+        return f16 ? launch_gemm<true, true>(mxh, mxl, myh, myl, r, M, N, l.kp, status, epi, B, grid, st)
+                   : launch_gemm<true, false>(mxh, mxl, myh, myl, r, M, N, l.kp, status, epi, B, grid, st);
     }
-    return (int)cudaGetLastError();
+    return f16 ? launch_gemm<false, true>(mxh, mxl, myh, myl, r, M, N, l.kp, status, epi, B, grid, st)
+               : launch_gemm<false, false>(mxh, mxl, myh, myl, r, M, N, l.kp, status, epi, B, grid, st);
 }
 
 extern "C" int mcu_launch_matmul_tc(float* r, const float* x, const float* y, int64_t M, int64_t K, int64_t N,
-                                    void* scratch, int* status, cudaStream_t st) {
-    return mcu_launch_matmul_tc_ex(r, x, y, M, K, N, scratch, status, st, nullptr);
+                                    void* scratch, int* status, cudaStream_t st, int f16) {
+    return mcu_launch_matmul_tc_ex(r, x, y, M, K, N, scratch, status, st, nullptr, f16);
 }

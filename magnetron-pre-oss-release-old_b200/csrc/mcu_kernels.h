@@ -62,18 +62,20 @@ int mcu_launch_matmul_skinny(float* r, const float* x, const float* y, int64_t M
 size_t mcu_skinny_noalloc_limit(void);
 int mcu_skinny_noalloc_scratch(void** out);
 
-/* k_matmul_tc.cu: 3xTF32 tcgen05 GEMM, R[M,N] = X[M,K] Y[K,N] (row-major).
- * scratch needs mcu_matmul_tc_scratch_bytes(M, K, N) bytes. */
+/* k_matmul_tc.cu: tcgen05 GEMM with a three-product split, R[M,N] = X[M,K] Y[K,N] (row-major);
+ * f16 = 0: tf32 hi/lo split (kind::tf32), f16 = 1: scaled f16 hi/lo split (kind::f16).
+ * scratch needs mcu_matmul_tc_scratch_bytes(M, K, N) bytes (either split). */
 size_t mcu_matmul_tc_scratch_bytes(int64_t M, int64_t K, int64_t N);
 int mcu_launch_matmul_tc(float* r, const float* x, const float* y, int64_t M, int64_t K, int64_t N,
-                         void* scratch, int* status, cudaStream_t st);
+                         void* scratch, int* status, cudaStream_t st, int f16);
 int mcu_matmul_tc_supported(void);
 
 /* Fused dense-layer epilogue for the tensor-core GEMM: out = act(X Y + bias) with
  * bias at the result's row-major index (or NULL), act 0 = none, 1 = GELU; when
  * out_hi/out_lo are set the tf32 hi/lo split of out is also written in the
  * [M][kp_out] layout the next product reads (kp_out = N rounded up to 32, N % 32 == 0).
- * a_hi/a_lo, when set, are X already split in that layout (no split pass). */
+ * a_hi/a_lo, when set, are X already split in that layout (no split pass).  The split
+ * fields apply to the tf32 split only; the f16 split always splits X itself. */
 typedef struct mcu_tc_epilogue {
     const float* a_hi;
     const float* a_lo;
@@ -85,9 +87,9 @@ typedef struct mcu_tc_epilogue {
 } mcu_tc_epilogue;
 size_t mcu_matmul_tc_batched_scratch_bytes(int64_t B, int64_t M, int64_t K, int64_t N);
 int mcu_launch_matmul_tc_batched(float* r, const float* x, const float* y, int64_t B, int64_t M, int64_t K,
-                                 int64_t N, void* scratch, int* status, cudaStream_t st);
+                                 int64_t N, void* scratch, int* status, cudaStream_t st, int f16);
 int mcu_launch_matmul_tc_ex(float* r, const float* x, const float* y, int64_t M, int64_t K, int64_t N,
-                            void* scratch, int* status, cudaStream_t st, const mcu_tc_epilogue* ep);
+                            void* scratch, int* status, cudaStream_t st, const mcu_tc_epilogue* ep, int f16);
 
 #ifdef __cplusplus
 }

@@ -46,6 +46,7 @@ INPLACE_OK = UNARY | SCALAR | BINARY | {"MATMUL"}
 TFLAG_OWNER, TFLAG_VIEW = 1, 2
 
 E_INVALID, E_DEVICE_WAIT, E_UNSUPPORTED, E_SCRATCH_LIMIT, E_IO = 10001, 10002, 10003, 10004, 10005
+TC_SPLIT_TF32, TC_SPLIT_F16 = 0, 1  # mag_cuda_set_tc_split
 
 
 # ---------------------------------------------------------------- ABI structs
@@ -105,6 +106,7 @@ def load_library(path: str = LIB_PATH):
         "mag_destroy_device_cuda": ([vp], None),
         "mag_cuda_device_ordinal": ([vp], C.c_int),
         "mag_cuda_set_matmul_mode": ([vp, C.c_int], C.c_int),
+        "mag_cuda_set_tc_split": ([vp, C.c_int], C.c_int),
         "mag_cuda_stream": ([vp], vp),
         "mag_cuda_synchronize": ([vp], C.c_int),
         "mag_cuda_last_error": ([vp], C.c_int),

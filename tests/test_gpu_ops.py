@@ -292,12 +292,28 @@ def test_deferred_graph_replays_with_new_inputs():
     dev.graph_release(out)
 
 
+SPLITS = [MB.TC_SPLIT_TF32, MB.TC_SPLIT_F16]
+
+
+@pytest.fixture(autouse=True)
+def _default_split():
+    yield
+    device().L.mag_cuda_set_tc_split(device().p, MB.TC_SPLIT_F16)
+
+
+def _split(dev, split):
+    MB.check(dev.L.mag_cuda_set_tc_split(dev.p, split), "tc split")
+
+
+@pytest.mark.parametrize("split", SPLITS)
 @pytest.mark.parametrize("mkn", [(128, 32, 256), (300, 100, 700), (1000, 777, 300), (2048, 1024, 4096),
                                  (256, 4096, 1000), (4096, 4096, 4096)])
-def test_matmul_tensor_core_normwise(mkn):
-    """3xTF32 tcgen05 path through the vtable; within 1e-5 of the exact product, norm-wise."""
+def test_matmul_tensor_core_normwise(mkn, split):
+    """tcgen05 path (tf32 or scaled f16 split) through the vtable; within 1e-5 of the exact
+    product, norm-wise."""
     m, k, n = mkn
     dev = device()
+    _split(dev, split)
     o = oracle()
     s = o.stream(7300 + m + n)
     x = s.uniform(m * k, -1.0, 1.0)
@@ -311,10 +327,12 @@ def test_matmul_tensor_core_normwise(mkn):
     assert _normwise_ok(got, x, y, m, k, n)
 
 
-def test_matmul_tensor_core_large_k_sampled():
+@pytest.mark.parametrize("split", SPLITS)
+def test_matmul_tensor_core_large_k_sampled(split):
     """K = 16384 through the automatic path: norm-wise against the exact product,
     and sampled rows against the oracle's sequential f32 product relative to max|C|."""
     dev = device()
+    _split(dev, split)
     o = oracle()
     m, k, n = 256, 16384, 512
     s = o.stream(7400)
@@ -347,10 +365,12 @@ def _build_mlp(dev, rows, dims, inplace_gelu=True):
     return X, Ws, Bs, h
 
 
+@pytest.mark.parametrize("split", SPLITS)
 @pytest.mark.parametrize("inplace", [True, False])
-def test_fused_graph_matches_unfused_bitwise(inplace):
+def test_fused_graph_matches_unfused_bitwise(inplace, split):
     """Dense layers fused into the GEMM epilogue give the same bits as the op-by-op graph."""
     dev = device()
+    _split(dev, split)
     o = oracle()
     rows, dims = 256, [512, 384, 256, 96]
     X, Ws, Bs, root = _build_mlp(dev, rows, dims, inplace)
@@ -380,9 +400,11 @@ def test_fused_graph_matches_unfused_bitwise(inplace):
     assert not bits_equal(fused, fused2).all()
 
 
-def test_matmul_batched_tensor_core():
+@pytest.mark.parametrize("split", SPLITS)
+def test_matmul_batched_tensor_core(split):
     """Batched product large enough for the tensor-core path (tiles indexed by batch)."""
     dev = device()
+    _split(dev, split)
     o = oracle()
     b, m, k, n = 16, 520, 512, 264  # M, N not multiples of the 128 x 256 tile: tiles straddle batches
     s = o.stream(7200)
@@ -397,3 +419,28 @@ def test_matmul_batched_tensor_core():
     for i in range(b):
         assert _normwise_ok(got[i * m * n:(i + 1) * m * n], x[i * m * k:(i + 1) * m * k],
                             y[i * k * n:(i + 1) * k * n], m, k, n), i
+
+
+def test_matmul_f16_split_scaling_extremes():
+    """Rows and columns spanning 2^-60 .. 2^60, a zero row and a zero column: the f16
+    split's power-of-two scaling keeps every element within 1e-5 of |X||Y|."""
+    dev = device()
+    _split(dev, MB.TC_SPLIT_F16)
+    o = oracle()
+    m, k, n = 384, 512, 320
+    s = o.stream(7600)
+    x = s.uniform(m * k, -1.0, 1.0).reshape(m, k)
+    y = s.uniform(k * n, -1.0, 1.0).reshape(k, n)
+    x *= np.float32(2.0) ** ((np.arange(m) % 121) - 60).astype(np.float32)[:, None]
+    y *= np.float32(2.0) ** (((np.arange(n) * 7) % 121) - 60).astype(np.float32)[None, :]
+    x[5] = 0
+    y[:, 9] = 0
+    x, y = x.astype(np.float32).reshape(-1), y.astype(np.float32).reshape(-1)
+    MB.check(dev.L.mag_cuda_set_matmul_mode(dev.p, 2), "tc mode")
+    try:
+        got, _, _ = run_op(dev, "MATMUL", [x, y], [(m, k), (k, n)])
+    finally:
+        dev.L.mag_cuda_set_matmul_mode(dev.p, 0)
+    assert dev.L.mag_cuda_synchronize(dev.p) == 0
+    assert np.all(got.reshape(m, n)[5] == 0) and np.all(got.reshape(m, n)[:, 9] == 0)
+    assert _normwise_ok(got, x, y, m, k, n)
