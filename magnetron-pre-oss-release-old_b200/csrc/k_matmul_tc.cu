@@ -26,8 +26,11 @@
 //     warp 1      TMEM allocator; lane 0 issues tcgen05.mma kind::tf32 or kind::f16
 //                 (M=128, N=BN, 32 bytes of K), three per k-step, and tcgen05.commit to
 //                 free ring slots / publish accumulators
-//     warps 2..9  epilogue: tcgen05.ld 32 lanes x 32 columns -> registers -> global,
-//                 from one of two TMEM accumulators so it overlaps the next segment's MMAs
+//     warps 4..11 epilogue: tcgen05.ld 32 lanes x 32 columns -> registers -> global,
+//                 from one of two TMEM accumulators so it overlaps the next segment's MMAs;
+//                 a fused layer's bias arrives by TMA in 32 x 32 chunks staged in shared memory
+//   Warpgroup 0 (producer, MMA issuer, two idle warps) gives registers to the two epilogue
+//   warpgroups with setmaxnreg, so the 128 per-thread segment sums never spill.
 // Every mbarrier wait is bounded: on expiry the kernel records a status code,
 // all roles leave their loops, and TMEM is released before the CTA exits.
 // No load uses cluster multicast; the same kernel serves multi-GPU runs.
@@ -36,6 +39,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 #include <cstdint>
+#include <cstring>
 #include "mcu_kernels.h"
 
 namespace {
@@ -46,7 +50,13 @@ constexpr int BK = 16;           // f32 per 64-byte row (the tf32 split)
 constexpr int BK16 = 32;         // f16 per 64-byte row (the f16 split)
 constexpr int KPAD = 32;         // K padding of the split operands
 constexpr int kEpiWarps = 8;   // two per TMEM lane quadrant, each owning half of the tile's columns
-constexpr int kThreads = 32 * (2 + kEpiWarps);
+constexpr int kEpiWarp0 = 4;   // warpgroup 0: producer, MMA issuer, two idle warps; warpgroups 1-2: epilogue
+constexpr int kThreads = 32 * (kEpiWarp0 + kEpiWarps);
+// Register split (setmaxnreg): the launch gives every thread kLaunchRegs; warpgroup 0 drops to
+// kCtrlRegs and the two epilogue warpgroups rise to kEpiRegs, so the epilogue holds its
+// 128-column segment sums without spilling.  128*kCtrlRegs + 256*kEpiRegs == kThreads*kLaunchRegs.
+constexpr int kLaunchRegs = 168, kCtrlRegs = 40, kEpiRegs = 232;
+static_assert(128 * kCtrlRegs + 256 * kEpiRegs == kThreads * kLaunchRegs, "register split must match the launch");
 constexpr uint32_t kWaitLimit = 1u << 22;
 
 int sm_count() {
@@ -160,10 +170,12 @@ __host__ __device__ constexpr uint32_t idesc_3x(int n, bool f16) {
     return (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 }
 
-// v * 2^-s, exact unless the result is subnormal or overflows (then correctly rounded).
+// v * 2^-s for s in [-252, 252] (row and column exponents lie in [-113, 126]): two
+// multiplications by normal powers of two that scale the same way, so the product is
+// exact unless the result is subnormal or overflows, and then rounded once.
 __device__ __forceinline__ float unscale(float v, int s) {
-    if (s >= -126 && s <= 126) return __fmul_rn(v, __int_as_float((127 - s) << 23));
-    return scalbnf(v, -s);
+    const int s1 = s >> 1, s2 = s - s1;
+    return __fmul_rn(__fmul_rn(v, __int_as_float((127 - s1) << 23)), __int_as_float((127 - s2) << 23));
 }
 
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
@@ -202,7 +214,11 @@ struct Cfg {
     static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
     static constexpr int TMEM_COLS = 2 * BN;
     static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 512;
+    // fused epilogue: each epilogue warp stages its 32 x 32 f32 bias chunk (4 KB, 128B-swizzled)
+    static constexpr int BIAS_BYTES = kEpiWarps * 32 * 32 * 4;
+    static constexpr int SMEM_BIAS = STAGES * STAGE_BYTES + 1024 + BIAS_BYTES + 1024;
     static_assert(TMEM_COLS <= 512, "two accumulators must fit TMEM");
+    static_assert(SMEM_BIAS <= 227 * 1024, "ring and bias staging must fit shared memory");
 };
 
 // Epilogue of a fused dense layer: out = act(acc + bias) and, for the next
@@ -215,6 +231,7 @@ struct Epi {
     int act;            // 0 none, 1 GELU (the reference's vector-lane formula)
     const int* row_exp; // f16 split: power-of-two exponents of X's rows ([B*M]) and Y's columns ([B*N])
     const int* col_exp;
+    int bias_map;       // the bias is also described by map_bias (32 x 32 boxes): staged through shared memory
 };
 
 __device__ __forceinline__ float rna_tf32_dev(float x) {
@@ -231,10 +248,10 @@ __device__ __forceinline__ float gelu_lane(float x) {
 }
 
 template <int BN, int STAGES, bool FUSED, bool F16>
-__global__ void __maxnreg__(168)
+__global__ void __maxnreg__(kLaunchRegs)
     gemm_3x(const __grid_constant__ CUtensorMap map_xhi, const __grid_constant__ CUtensorMap map_xlo,
                 const __grid_constant__ CUtensorMap map_yhi, const __grid_constant__ CUtensorMap map_ylo,
-                float* __restrict__ r, int M, int N, int Kp, int64_t ldr, int* status, const Epi epi,
+                const __grid_constant__ CUtensorMap map_bias, float* __restrict__ r, int M, int N, int Kp, int64_t ldr, int* status, const Epi epi,
                 int seg_kb, int batch) {
     using C = Cfg<BN, STAGES>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -245,7 +262,9 @@ __global__ void __maxnreg__(168)
     uint64_t* acc_full = empty + STAGES;
     uint64_t* acc_empty = acc_full + 2;
     uint64_t* drain = acc_empty + 2;
-    uint32_t* tmem_slot = (uint32_t*)(drain + 1);
+    uint64_t* bias_full = drain + 1;  // one per epilogue warp
+    uint32_t* tmem_slot = (uint32_t*)(bias_full + kEpiWarps);
+    uint8_t* bias_smem = smem + STAGES * C::STAGE_BYTES + 1024;  // 1024-aligned for the 128B swizzle
     volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -268,6 +287,7 @@ __global__ void __maxnreg__(168)
             mbar_init(&acc_empty[a], 32 * kEpiWarps);
         }
         mbar_init(drain, 1);
+        for (int e = 0; e < kEpiWarps; ++e) mbar_init(&bias_full[e], 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -281,7 +301,9 @@ __global__ void __maxnreg__(168)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
-    if (warp == 0) {
+    if (warp < kEpiWarp0) {
+      asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kCtrlRegs));
+      if (warp == 0) {
         if (lane == 0) {  // ---- TMA producer
             asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&map_xhi) : "memory");
             asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&map_xlo) : "memory");
@@ -337,10 +359,16 @@ __global__ void __maxnreg__(168)
                 }
             }
         }
+      }
     } else {  // ---- epilogue warps: TMEM lanes 32*(warp%4) .. +31, columns [h*BN/2, (h+1)*BN/2)
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kEpiRegs));
         constexpr int HC = BN / 2;   // columns per thread
         const int q = warp & 3;
-        const int h = (warp - 2) >> 2;
+        const int h = (warp - kEpiWarp0) >> 2;
+        const int ew = warp - kEpiWarp0;  // this warp's bias staging slot and barrier
+        uint8_t* bbuf = bias_smem + ew * 4096;
+        uint32_t bphase = 0;
+        const bool vec = ((ldr & 3) == 0) && ((((uintptr_t)r) & 15) == 0);
         uint32_t gseg = 0;
         for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
             int mb, nb;
@@ -356,10 +384,26 @@ __global__ void __maxnreg__(168)
                         if (nb * BN + h * HC + j < N) asm volatile("prefetch.global.L2 [%0];" ::"l"(pb + j));
                 }
             }
+            const int row0 = mb * BM + q * 32;  // this warp's first row
+            const int colh = nb * BN + h * HC;
+            // the bias chunk of 32 columns goes through shared memory when the map covers it
+            auto stage_bias = [&](int cb) {
+                if (lane == 0) {
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // earlier reads of the slot
+                    mbar_expect_tx(&bias_full[ew], 32 * 32 * 4);
+                    tma_load_2d(&map_bias, &bias_full[ew], bbuf, cb, row0);
+                }
+            };
+            const bool map_ok = FUSED && epi.bias_map && vec && row0 < M;
+            bool staged0 = false;
             // segment sums are added in registers with round-to-nearest
             float sum[HC];
             for (int kb0 = 0; kb0 < nk; kb0 += seg_kb, ++gseg) {
                 const uint32_t b = gseg & 1, bround = gseg >> 1;
+                if (map_ok && !staged0 && kb0 + seg_kb >= nk && colh + 32 <= N) {
+                    stage_bias(colh);  // the first chunk loads while the last segment accumulates
+                    staged0 = true;
+                }
                 if (!mbar_wait(&acc_full[b], bround & 1, ab, 4)) goto done;
                 tc_fence_after();
 #pragma unroll
@@ -377,80 +421,90 @@ __global__ void __maxnreg__(168)
                 tc_fence_before();
                 mbar_arrive(&acc_empty[b]);
             }
-            const int row = mb * BM + q * 32 + lane;
-            if (row >= M) continue;
-            const int colh = nb * BN + h * HC;
-            float* out = r + (int64_t)bt * M * ldr + (int64_t)row * ldr + colh;
-            const bool vec = ((ldr & 3) == 0) && ((((uintptr_t)r) & 15) == 0);
+            if (row0 >= M) continue;  // the whole warp is past the last row
+            const int row = row0 + lane;
+            const bool row_ok = row < M;
+            const int rowc = row_ok ? row : row0;  // lanes past M compute but store nothing
+            float* out = r + (int64_t)bt * M * ldr + (int64_t)rowc * ldr + colh;
             int ea = 0;
-            if constexpr (F16) ea = epi.row_exp[(int64_t)bt * M + row];
+            if constexpr (F16) ea = epi.row_exp[(int64_t)bt * M + rowc];
 #pragma unroll
             for (int c = 0; c < HC / 32; ++c) {
                 float* v = sum + c * 32;
                 const int cb = colh + c * 32;
                 const bool full = cb + 32 <= N;
-                if constexpr (F16) {  // undo the operands' power-of-two scaling
-                    const int* ce = epi.col_exp + (int64_t)bt * N + cb;
-                    if (full && ((((int64_t)bt * N) & 3) == 0)) {  // 16-byte aligned exponent groups
+                const bool fast = full && vec && (!F16 || ((((int64_t)bt * N) & 3) == 0));
+                const bool staged = map_ok && full;
+                if (staged) {
+                    if (c > 0 || !staged0) stage_bias(cb);
+                    if (!mbar_wait(&bias_full[ew], bphase, ab, 5)) goto done;
+                    bphase ^= 1;
+                }
+                if (fast) {
+                    // one float4 at a time through unscale, bias, GELU, split and store: short live
+                    // ranges keep the 128-column segment sum in registers without spills
+                    const int* ce = F16 ? epi.col_exp + (int64_t)bt * N + cb : nullptr;
+                    const float* pb = FUSED && epi.bias && !staged ? epi.bias + (int64_t)rowc * N + cb : nullptr;
 #pragma unroll
-                        for (int j = 0; j < 32; j += 4) {
+                    for (int j = 0; j < 32; j += 4) {
+                        float a[4] = {v[j], v[j + 1], v[j + 2], v[j + 3]};
+                        if constexpr (F16) {  // undo the operands' power-of-two scaling
                             const int4 e4 = *(const int4*)(ce + j);
-                            v[j] = unscale(v[j], ea + e4.x);
-                            v[j + 1] = unscale(v[j + 1], ea + e4.y);
-                            v[j + 2] = unscale(v[j + 2], ea + e4.z);
-                            v[j + 3] = unscale(v[j + 3], ea + e4.w);
+                            a[0] = unscale(a[0], ea + e4.x);
+                            a[1] = unscale(a[1], ea + e4.y);
+                            a[2] = unscale(a[2], ea + e4.z);
+                            a[3] = unscale(a[3], ea + e4.w);
                         }
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 32; ++j)
-                            if (cb + j < N) v[j] = unscale(v[j], ea + ce[j]);
-                    }
-                }
-                if constexpr (FUSED) {
-                    if (epi.bias) {
-                        const float* pb = epi.bias + (int64_t)row * N + cb;
-                        if (full && vec) {
-#pragma unroll
-                            for (int j = 0; j < 32; j += 4) {
-                                const float4 b4 = __ldcs((const float4*)(pb + j));
-                                v[j] = __fadd_rn(v[j], b4.x);
-                                v[j + 1] = __fadd_rn(v[j + 1], b4.y);
-                                v[j + 2] = __fadd_rn(v[j + 2], b4.z);
-                                v[j + 3] = __fadd_rn(v[j + 3], b4.w);
+                        if constexpr (FUSED) {
+                            if (staged || pb) {  // row `lane` of the staged chunk: 16-byte unit j/4, swizzled
+                                const float4 b4 = staged ? *(const float4*)(bbuf + lane * 128 + (((j >> 2) ^ (lane & 7)) << 4))
+                                                         : __ldcs((const float4*)(pb + j));
+                                a[0] = __fadd_rn(a[0], b4.x);
+                                a[1] = __fadd_rn(a[1], b4.y);
+                                a[2] = __fadd_rn(a[2], b4.z);
+                                a[3] = __fadd_rn(a[3], b4.w);
                             }
-                        } else {
+                            if (epi.act == 1) {
 #pragma unroll
-                            for (int j = 0; j < 32; ++j)
-                                if (cb + j < N) v[j] = __fadd_rn(v[j], pb[j]);
+                                for (int u = 0; u < 4; ++u) a[u] = gelu_lane(a[u]);
+                            }
+                            if (!F16 && epi.out_hi && row_ok) {
+                                float4 hh, ll;
+                                hh.x = rna_tf32_dev(a[0]); ll.x = rna_tf32_dev(a[0] - hh.x);
+                                hh.y = rna_tf32_dev(a[1]); ll.y = rna_tf32_dev(a[1] - hh.y);
+                                hh.z = rna_tf32_dev(a[2]); ll.z = rna_tf32_dev(a[2] - hh.z);
+                                hh.w = rna_tf32_dev(a[3]); ll.w = rna_tf32_dev(a[3] - hh.w);
+                                *(float4*)(epi.out_hi + (int64_t)row * epi.kp_out + cb + j) = hh;
+                                *(float4*)(epi.out_lo + (int64_t)row * epi.kp_out + cb + j) = ll;
+                            }
                         }
+                        if (row_ok) *(float4*)(out + c * 32 + j) = make_float4(a[0], a[1], a[2], a[3]);
                     }
-                    if (epi.act == 1) {
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) v[j] = gelu_lane(v[j]);
-                    }
-                    if (epi.out_hi && full) {
-                        float* ph = epi.out_hi + (int64_t)row * epi.kp_out + cb;
-                        float* pl = epi.out_lo + (int64_t)row * epi.kp_out + cb;
-#pragma unroll
-                        for (int j = 0; j < 32; j += 4) {
-                            float4 hh, ll;
-                            hh.x = rna_tf32_dev(v[j]);     ll.x = rna_tf32_dev(v[j] - hh.x);
-                            hh.y = rna_tf32_dev(v[j + 1]); ll.y = rna_tf32_dev(v[j + 1] - hh.y);
-                            hh.z = rna_tf32_dev(v[j + 2]); ll.z = rna_tf32_dev(v[j + 2] - hh.z);
-                            hh.w = rna_tf32_dev(v[j + 3]); ll.w = rna_tf32_dev(v[j + 3] - hh.w);
-                            *(float4*)(ph + j) = hh;
-                            *(float4*)(pl + j) = ll;
-                        }
-                    }
+                    if (staged) __syncwarp();  // every lane has read the slot before it is refilled
+                    continue;
                 }
-                if (vec && full) {
+                if (staged) __syncwarp();  // (a staged chunk is always on the fast path: full and vec)
+                if (!row_ok) continue;
+                // ragged edge or unaligned result: element by element, bias from global memory
+                const float* pb = FUSED && epi.bias ? epi.bias + (int64_t)row * N + cb : nullptr;
+                const int* ce = F16 ? epi.col_exp + (int64_t)bt * N + cb : nullptr;
 #pragma unroll
-                    for (int j = 0; j < 32; j += 4)
-                        *(float4*)(out + c * 32 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        if (cb + j < N) out[c * 32 + j] = v[j];
+                for (int j = 0; j < 32; ++j) {
+                    if (cb + j >= N) break;
+                    float a = v[j];
+                    if constexpr (F16) a = unscale(a, ea + ce[j]);
+                    if constexpr (FUSED) {
+                        if (pb) a = __fadd_rn(a, pb[j]);
+                        if (epi.act == 1) a = gelu_lane(a);
+                        if constexpr (!F16) {
+                            if (epi.out_hi && full) {
+                                const float hh = rna_tf32_dev(a);
+                                epi.out_hi[(int64_t)row * epi.kp_out + cb + j] = hh;
+                                epi.out_lo[(int64_t)row * epi.kp_out + cb + j] = rna_tf32_dev(a - hh);
+                            }
+                        }
+                    }
+                    out[c * 32 + j] = a;
                 }
             }
         }
@@ -714,15 +768,30 @@ int segment_kb(bool f16) {
     return k <= 0 ? (1 << 30) : (k + ke - 1) / ke;
 }
 
+// 2-D map over the fused epilogue's row-major [M][N] f32 bias, box 32 x 32, 128-byte swizzle.
+bool make_bias_map(CUtensorMap* m, const float* bias, int64_t M, int64_t N) {
+    auto fn = encode_fn();
+    if (!fn || (N & 3) || (((uintptr_t)bias) & 15)) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)M};
+    cuuint64_t strides[1] = {(cuuint64_t)(N * 4)};
+    cuuint32_t box[2] = {32, 32};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void*)bias, dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <bool FUSED, bool F16>
-int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c, const CUtensorMap& d, float* r,
-                int64_t M, int64_t N, int64_t kp, int* status, const Epi& epi, int64_t B, int grid, cudaStream_t st) {
+int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c, const CUtensorMap& d,
+                const CUtensorMap& bias, float* r, int64_t M, int64_t N, int64_t kp, int* status, const Epi& epi,
+                int64_t B, int grid, cudaStream_t st) {
     using C = Cfg<kBN, kStages>;
     auto kern = gemm_3x<kBN, kStages, FUSED, F16>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    const int smem = FUSED ? C::SMEM_BIAS : C::SMEM;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return (int)e;
-    kern<<<grid, kThreads, C::SMEM, st>>>(a, b, c, d, r, (int)M, (int)N, (int)kp, (int64_t)N, status, epi,
-                                          segment_kb(F16), (int)B);
+    kern<<<grid, kThreads, smem, st>>>(a, b, c, d, bias, r, (int)M, (int)N, (int)kp, (int64_t)N, status, epi,
+                                       segment_kb(F16), (int)B);
     return (int)cudaGetLastError();
 }
 
@@ -811,11 +880,14 @@ static int launch_tc(float* r, const float* x, const float* y, int64_t B, int64_
         epi.out_lo = f16 ? nullptr : ep->out_lo;
         epi.kp_out = ep->kp_out;
         epi.act = ep->act;
-        return f16 ? launch_gemm<true, true>(mxh, mxl, myh, myl, r, M, N, l.kp, status, epi, B, grid, st)
-                   : launch_gemm<true, false>(mxh, mxl, myh, myl, r, M, N, l.kp, status, epi, B, grid, st);
+        CUtensorMap mb;
+        memset(&mb, 0, sizeof(mb));
+        epi.bias_map = ep->bias && make_bias_map(&mb, ep->bias, M, N);
+        return f16 ? launch_gemm<true, true>(mxh, mxl, myh, myl, mb, r, M, N, l.kp, status, epi, B, grid, st)
+                   : launch_gemm<true, false>(mxh, mxl, myh, myl, mb, r, M, N, l.kp, status, epi, B, grid, st);
     }
-    return f16 ? launch_gemm<false, true>(mxh, mxl, myh, myl, r, M, N, l.kp, status, epi, B, grid, st)
-               : launch_gemm<false, false>(mxh, mxl, myh, myl, r, M, N, l.kp, status, epi, B, grid, st);
+    return f16 ? launch_gemm<false, true>(mxh, mxl, myh, myl, mxh, r, M, N, l.kp, status, epi, B, grid, st)
+               : launch_gemm<false, false>(mxh, mxl, myh, myl, mxh, r, M, N, l.kp, status, epi, B, grid, st);
 }
 
 extern "C" int mcu_launch_matmul_tc(float* r, const float* x, const float* y, int64_t M, int64_t K, int64_t N,
