@@ -754,18 +754,21 @@ size_t scratch_bytes(int64_t M, int64_t K, int64_t N) {
 constexpr int kBN = 256;
 constexpr int kStages = 4;
 
-// K per TMEM accumulation segment (MAG_CUDA_TC_SEGMENT, default 256).  Tensor-core
-// f32 accumulation truncates; restarting the accumulator every segment and
-// adding segments with round-to-nearest bounds that error by the segment length
-// instead of K.  0 = one segment spanning K.  Returned in ring stages.
+// K per TMEM accumulation segment (MAG_CUDA_TC_SEGMENT; default 512 for the f16 split,
+// 256 for tf32).  Tensor-core f32 accumulation truncates; restarting the accumulator
+// every segment and adding segments with round-to-nearest bounds that error by the
+// segment length instead of K (at K = 16384: 2.0e-6 of max|C| for f16 at 512, 2.1e-6 for
+// tf32 at 256).  Longer segments give the epilogue more time per accumulator.  0 = one
+// segment spanning K.  Returned in ring stages.
 int segment_kb(bool f16) {
     static int k = -2;
     if (k == -2) {
         const char* e = getenv("MAG_CUDA_TC_SEGMENT");
-        k = (e && *e) ? atoi(e) : 256;
+        k = (e && *e) ? atoi(e) : -1;
     }
+    const int seg = k == -1 ? (f16 ? 512 : 256) : k;
     const int ke = f16 ? BK16 : BK;
-    return k <= 0 ? (1 << 30) : (k + ke - 1) / ke;
+    return seg <= 0 ? (1 << 30) : (seg + ke - 1) / ke;
 }
 
 // 2-D map over the fused epilogue's row-major [M][N] f32 bias, box 32 x 32, 128-byte swizzle.
