@@ -120,6 +120,23 @@ MAG_CUDA_EXPORT int mag_cuda_softmax_rows_f32(mag_compute_device_t* dvc, float* 
 MAG_CUDA_EXPORT int mag_cuda_matmul_batched_f32(mag_compute_device_t* dvc, float* r, const float* x,
                                                 const float* y, int64_t batch, int64_t M, int64_t K, int64_t N);
 
+/* ---- asynchronous host copies (no counterpart in the reference, whose storage copies are
+ * synchronous: magnetron/magnetron.c:1820-1824) ----
+ * Queue a copy between pinned host memory and a tensor's storage on the device's copy
+ * stream, so it overlaps kernels queued on the compute stream.  The copy starts after all
+ * work queued on the compute stream before the call (which still sees the old contents);
+ * every later op, graph replay or storage callback that touches the tensor waits for it.
+ * host must be pinned (cudaHostAlloc / cudaHostRegister) and must stay untouched until the
+ * copy has finished: mag_cuda_copies_synchronize, or any host read of the tensor.  An upload
+ * shorter than the buffer leaves the rest zero.  Returns MAG_CUDA_E_INVALID for pageable
+ * memory, a foreign pointer, a size beyond the buffer, or during a graph capture. */
+MAG_CUDA_EXPORT int mag_cuda_tensor_upload_async(mag_compute_device_t* dvc, mag_tensor_t* t, const void* src,
+                                                 size_t bytes);
+MAG_CUDA_EXPORT int mag_cuda_tensor_download_async(mag_compute_device_t* dvc, mag_tensor_t* t, void* dst,
+                                                   size_t bytes);
+/* Waits for every queued asynchronous host copy of the device. */
+MAG_CUDA_EXPORT int mag_cuda_copies_synchronize(mag_compute_device_t* dvc);
+
 /* ---- seeded fills on the device ----
  * The core fills tensors on the host only (magnetron/magnetron.c:1826-1876 assert a
  * CPU context).  These generate the same PCG stream on the device: *state and inc are

@@ -69,6 +69,8 @@ typedef struct mcu_block {
     uint8_t zero_pending; /* contents are zero by contract, the memset is not issued yet */
     uint8_t known_zero;   /* nothing has written the buffer since it was zeroed */
     uint8_t state;        /* 0 empty, 1 live, 2 deleted */
+    uint8_t io_pending;   /* an async copy on the copy stream touches the buffer: io_ev marks its end */
+    cudaEvent_t io_ev;
 } mcu_block;
 
 typedef struct mcu_graph {
@@ -98,6 +100,8 @@ typedef struct mcu_device {
     int ordinal;
     int sm_count;
     cudaStream_t stream;
+    cudaStream_t copy_stream; /* async uploads/downloads, ordered after the compute stream's tail */
+    cudaEvent_t tail_ev;
     int managed;      /* MAG_CUDA_MANAGED=1: unified memory, synchronous ops */
     int eager_zero;   /* MAG_CUDA_EAGER_ZERO=1: memset on allocation */
     int matmul_mode;  /* MAG_CUDA_MATMUL: 0 auto, 1 exact, 2 tensor cores */
@@ -133,6 +137,7 @@ static size_t hash_ptr(uintptr_t p, size_t cap) {
 }
 
 static void tab_insert(mcu_device* d, uintptr_t base, size_t size, int zero_pending, int known_zero);
+static mcu_block* tab_find(mcu_device* d, uintptr_t base);
 
 static void tab_grow(mcu_device* d) {
     size_t old_cap = d->tab_cap;
@@ -141,8 +146,13 @@ static void tab_grow(mcu_device* d) {
     d->tab = (mcu_block*)calloc(d->tab_cap, sizeof(mcu_block));
     if (!d->tab) mcu_panic("out of host memory");
     d->tab_live = d->tab_used = 0;
-    for (size_t i = 0; i < old_cap; ++i)
-        if (old[i].state == 1) tab_insert(d, old[i].base, old[i].size, old[i].zero_pending, old[i].known_zero);
+    for (size_t i = 0; i < old_cap; ++i) {
+        if (old[i].state != 1) continue;
+        tab_insert(d, old[i].base, old[i].size, old[i].zero_pending, old[i].known_zero);
+        mcu_block* nb = tab_find(d, old[i].base);
+        nb->io_pending = old[i].io_pending;
+        nb->io_ev = old[i].io_ev;
+    }
     free(old);
 }
 
@@ -151,7 +161,7 @@ static void tab_insert(mcu_device* d, uintptr_t base, size_t size, int zero_pend
     size_t i = hash_ptr(base, d->tab_cap);
     while (d->tab[i].state == 1) i = (i + 1) & (d->tab_cap - 1);
     if (d->tab[i].state == 0) d->tab_used++;
-    d->tab[i] = (mcu_block){base, size, (uint8_t)zero_pending, (uint8_t)known_zero, 1};
+    d->tab[i] = (mcu_block){base, size, (uint8_t)zero_pending, (uint8_t)known_zero, 1, 0, NULL};
     d->tab_live++;
 }
 
@@ -165,9 +175,20 @@ static mcu_block* tab_find(mcu_device* d, uintptr_t base) {
     return NULL;
 }
 
+/* The compute stream waits for an async copy of the buffer still in flight on the copy
+ * stream (mag_cuda_tensor_upload_async / _download_async) before touching it.  Graph
+ * captures never contain such a wait: pending copies are waited for before a capture
+ * and before each replay. */
+static void io_wait(mcu_device* d, mcu_block* b) {
+    if (!b || !b->io_pending || d->capturing) return;
+    MCU_CHECK(cudaStreamWaitEvent(d->stream, b->io_ev, 0));
+    b->io_pending = 0;
+}
+
 /* Clears a pending buffer before its first read or partial write. */
 static void materialize(mcu_device* d, uintptr_t base) {
     mcu_block* b = tab_find(d, base);
+    io_wait(d, b);
     if (b && b->zero_pending) {
         MCU_CHECK(cudaMemsetAsync((void*)b->base, 0, b->size, d->stream));
         b->zero_pending = 0;
@@ -177,6 +198,7 @@ static void materialize(mcu_device* d, uintptr_t base) {
 /* The op about to run overwrites every byte of the buffer: no clear needed. */
 static void overwritten(mcu_device* d, uintptr_t base) {
     mcu_block* b = tab_find(d, base);
+    io_wait(d, b);
     if (b) b->zero_pending = b->known_zero = 0;
 }
 
@@ -216,6 +238,7 @@ static void sto_set(mag_storage_buffer* sto, size_t offs, uint8_t x) {
     if (offs > sto->size) mcu_panic("set: offset %zu beyond buffer of %zu bytes", offs, sto->size);
     if (offs == 0 && x == 0 && !d->eager_zero && !d->managed && !d->capturing) {
         mcu_block* b = tab_find(d, sto->base);
+        io_wait(d, b);
         if (b) {
             b->zero_pending = b->known_zero = 1;
             return;
@@ -255,6 +278,7 @@ static void sto_cpy_device_host(mag_storage_buffer* sto, size_t offs, void* dst,
     if (offs + n > sto->size) mcu_panic("device->host copy of %zu bytes at %zu overflows %zu", n, offs, sto->size);
     if (!n) return;
     mcu_block* b = tab_find(d, sto->base);
+    io_wait(d, b);
     if (b && b->zero_pending) { /* never written: the contents are zero by contract */
         memset(dst, 0, n);
         return;
@@ -308,6 +332,11 @@ static void dvc_alloc_storage(mag_compute_device_t* dvc, mag_storage_buffer* out
 static void dvc_free_storage(mag_compute_device_t* dvc, mag_storage_buffer* buf) {
     mcu_device* d = dev_of(dvc);
     mcu_block* b = tab_find(d, buf->base);
+    io_wait(d, b); /* the stream-ordered free follows any copy still in flight */
+    if (b && b->io_ev) {
+        cudaEventDestroy(b->io_ev);
+        b->io_ev = NULL;
+    }
     if (b) {
         b->state = 2;
         d->tab_live--;
@@ -569,6 +598,8 @@ mag_compute_device_t* mag_init_device_cuda(mag_ctx_t* ctx) {
     const char* ts = getenv("MAG_CUDA_TC_SPLIT");
     d->tc_f16 = !(ts && !strcmp(ts, "tf32"));
     MCU_CHECK(cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking));
+    MCU_CHECK(cudaStreamCreateWithFlags(&d->copy_stream, cudaStreamNonBlocking));
+    MCU_CHECK(cudaEventCreateWithFlags(&d->tail_ev, cudaEventDisableTiming));
     cudaMemPool_t pool;
     MCU_CHECK(cudaDeviceGetDefaultMemPool(&pool, ordinal));
     uint64_t thresh = UINT64_MAX;
@@ -628,6 +659,11 @@ void mag_destroy_device_cuda(mag_compute_device_t* dvc) {
     }
     cudaStreamSynchronize(d->stream);
     cudaFree(d->d_status);
+    cudaStreamSynchronize(d->copy_stream);
+    for (size_t i = 0; i < d->tab_cap; ++i)
+        if (d->tab[i].io_ev) cudaEventDestroy(d->tab[i].io_ev);
+    cudaEventDestroy(d->tail_ev);
+    cudaStreamDestroy(d->copy_stream);
     cudaStreamDestroy(d->stream);
     free(d->tab);
     free(d);
@@ -817,6 +853,44 @@ int mag_cuda_softmax_rows_f32(mag_compute_device_t* dvc, float* r, const float* 
     int rc = mcu_launch_softmax_rows(r, x, rows, cols, d->stream);
     if (!rc) mcu_count_launches(1);
     return rc;
+}
+
+/* ------------------------------------------------ async host copies --- */
+
+/* Queues a copy between pinned host memory and a tensor's storage on the copy stream, after
+ * everything queued so far on the compute stream, and marks the buffer so the next
+ * compute-stream access waits for it. */
+static int io_async(mag_compute_device_t* dvc, mag_tensor_t* t, void* host, size_t bytes, int upload) {
+    if (!dvc || !t || !host) return MAG_CUDA_E_INVALID;
+    mcu_device* d = dev_of(dvc);
+    mcu_block* b = tab_find(d, t->storage.base);
+    if (!b || bytes > b->size || d->capturing || d->managed || !host_is_pinned(host)) return MAG_CUDA_E_INVALID;
+    if (!bytes) return 0;
+    if (upload) result_written(d, b->base, bytes >= b->size); /* the rest of a partial upload reads as zero */
+    else materialize(d, b->base);
+    b = tab_find(d, t->storage.base);
+    if (!b->io_ev) MCU_CHECK(cudaEventCreateWithFlags(&b->io_ev, cudaEventDisableTiming));
+    MCU_CHECK(cudaEventRecord(d->tail_ev, d->stream));
+    MCU_CHECK(cudaStreamWaitEvent(d->copy_stream, d->tail_ev, 0));
+    cudaError_t e = upload ? cudaMemcpyAsync((void*)b->base, host, bytes, cudaMemcpyHostToDevice, d->copy_stream)
+                           : cudaMemcpyAsync(host, (const void*)b->base, bytes, cudaMemcpyDeviceToHost, d->copy_stream);
+    if (e != cudaSuccess) return (int)e;
+    MCU_CHECK(cudaEventRecord(b->io_ev, d->copy_stream));
+    b->io_pending = 1;
+    return 0;
+}
+
+int mag_cuda_tensor_upload_async(mag_compute_device_t* dvc, mag_tensor_t* t, const void* src, size_t bytes) {
+    return io_async(dvc, t, (void*)src, bytes, 1);
+}
+
+int mag_cuda_tensor_download_async(mag_compute_device_t* dvc, mag_tensor_t* t, void* dst, size_t bytes) {
+    return io_async(dvc, t, dst, bytes, 0);
+}
+
+int mag_cuda_copies_synchronize(mag_compute_device_t* dvc) {
+    if (!dvc) return MAG_CUDA_E_INVALID;
+    return (int)cudaStreamSynchronize(dev_of(dvc)->copy_stream);
 }
 
 int mag_cuda_fill_uniform_pcg_f32(mag_compute_device_t* dvc, float* r, int64_t n, float min, float max,
@@ -1254,6 +1328,7 @@ static int graph_exec_impl(mag_compute_device_t* dvc, mag_tensor_t* root, int fu
     uint64_t sig = graph_signature(nodes, n) ^ ((uint64_t)(1 + d->tc_f16 + 2 * d->matmul_mode) * 0x9E3779B97F4A7C15ull);
     mcu_graph* g = d->graphs;
     while (g && (g->root != root || g->fused != fuse)) g = g->next;
+    for (size_t i = 0; i < n; ++i) io_wait(d, tab_find(d, nodes[i]->storage.base)); /* outside any capture */
     if (g && g->sig == sig) {
         free(nodes);
         g->ran = g->n_ev > 0;

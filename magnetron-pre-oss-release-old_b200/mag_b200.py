@@ -135,6 +135,9 @@ def load_library(path: str = LIB_PATH):
         "mag_cuda_fill_normal_pcg_f32": ([vp, vp, i64, C.c_float, C.c_float, C.POINTER(C.c_uint64), C.c_uint64],
                                          C.c_int),
         "mag_cuda_fill_f32": ([vp, vp, i64, C.c_float], C.c_int),
+        "mag_cuda_tensor_upload_async": ([vp, vp, vp, C.c_size_t], C.c_int),
+        "mag_cuda_tensor_download_async": ([vp, vp, vp, C.c_size_t], C.c_int),
+        "mag_cuda_copies_synchronize": ([vp], C.c_int),
         "mag_cuda_sto_parse": ([vp, C.c_size_t, C.c_size_t, vp, C.c_uint32, C.POINTER(C.c_uint32),
                                 C.POINTER(C.c_uint32)], C.c_int),
         "mag_cuda_sto_write_header": ([vp, C.c_uint32, vp, C.c_size_t, C.POINTER(C.c_size_t)], C.c_int),
@@ -421,6 +424,16 @@ class Device:
 
     def draw_text(self, t: Tensor, x: int, y: int, size: int, rgb: int, txt: str):
         check(self.L.mag_cuda_img_draw_text(self.p, t.ptr, x, y, size, rgb, txt.encode("latin-1")), "img_draw_text")
+
+    # ---- asynchronous host copies (pinned host memory; ordered against the compute stream)
+    def upload_async(self, t: Tensor, host_ptr: int, nbytes: int):
+        check(self.L.mag_cuda_tensor_upload_async(self.p, t.ptr, host_ptr, nbytes), "tensor_upload_async")
+
+    def download_async(self, t: Tensor, host_ptr: int, nbytes: int):
+        check(self.L.mag_cuda_tensor_download_async(self.p, t.ptr, host_ptr, nbytes), "tensor_download_async")
+
+    def copies_sync(self):
+        check(self.L.mag_cuda_copies_synchronize(self.p), "copies_synchronize")
 
     # ---- seeded fills (mag_tensor_fill*, magnetron/magnetron.c:1826-1876, on the device)
     def fill(self, t: Tensor, x: float):
