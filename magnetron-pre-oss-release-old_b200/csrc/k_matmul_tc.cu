@@ -121,15 +121,58 @@ __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* ba
         : "memory");
 }
 
+// ---- CTA pairs (2-CTA clusters): the leader (rank 0) issues the MMAs for both CTAs
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// The shared::cluster address of `saddr` (a shared::cta address) in the CTA of rank `rank`.
+__device__ __forceinline__ uint32_t mapa_rank(uint32_t saddr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Arrive on an mbarrier given by its shared::cluster address (this CTA's or the peer's).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t caddr) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(caddr) : "memory");
+}
+// TMA load into this CTA's shared memory whose completion is counted on an mbarrier of
+// either CTA of the pair (no multicast).
+__device__ __forceinline__ void tma_load_2d_pair(const CUtensorMap* map, uint32_t bar_caddr, void* dst, int c0, int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::
+            "r"(smem_u32(dst)),
+        "l"((uint64_t)map), "r"(bar_caddr), "r"(c0), "r"(c1)
+        : "memory");
+}
+
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
 // D(tmem) (+)= A(smem) * B(smem)^T, kind::tf32 or kind::f16 (both operands the same
 // type), issued by one thread.
-template <bool F16>
+template <bool F16, bool PAIR = false>
 __device__ __forceinline__ void umma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                      uint32_t accumulate) {
-    if constexpr (F16) {
+    if constexpr (PAIR) {  // M = 256 across the pair: A rows and half of B from each CTA's shared memory
+        if constexpr (F16) {
+            asm volatile(
+                "{\n\t.reg .pred p;\n\t"
+                "setp.ne.b32 p, %4, 0;\n\t"
+                "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+                "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+        } else {
+            asm volatile(
+                "{\n\t.reg .pred p;\n\t"
+                "setp.ne.b32 p, %4, 0;\n\t"
+                "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+                "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+        }
+    } else if constexpr (F16) {
         asm volatile(
             "{\n\t.reg .pred p;\n\t"
             "setp.ne.b32 p, %4, 0;\n\t"
@@ -149,6 +192,19 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                  : "memory");
 }
+// Pair form: arrives on the barrier at the same offset in both CTAs of the pair.
+__device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+            smem_u32(bar)),
+        "h"((uint16_t)0x3)
+        : "memory");
+}
+// Pair form, this CTA's barrier only.
+__device__ __forceinline__ void umma_commit_pair_local(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
 
 // Shared-memory matrix descriptor: K-major rows of ROW_BYTES bytes, swizzled (64B
 // or 128B), 8-row atoms 8*ROW_BYTES bytes apart.
@@ -164,10 +220,10 @@ __device__ __forceinline__ uint64_t sw_desc(uint32_t saddr) {
 }
 
 // Instruction descriptor: D f32, A/B tf32 (format 2, kind::tf32) or f16 (format 0,
-// kind::f16), both K-major, M=128, N=BN.
-__host__ __device__ constexpr uint32_t idesc_3x(int n, bool f16) {
+// kind::f16), both K-major, M = 128 (one CTA) or 256 (a CTA pair), N=BN.
+__host__ __device__ constexpr uint32_t idesc_3x(int n, bool f16, int m = BM) {
     const uint32_t fmt = f16 ? 0u : 2u;
-    return (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+    return (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
 // v * 2^-s for s in [-252, 252] (row and column exponents lie in [-113, 126]): two
@@ -207,10 +263,10 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb
 }
 
 // ------------------------------------------------------------ the GEMM
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool PAIR = false>
 struct Cfg {
     static constexpr int A_BYTES = BM * ROW_BYTES;
-    static constexpr int B_BYTES = BN * ROW_BYTES;
+    static constexpr int B_BYTES = (PAIR ? BN / 2 : BN) * ROW_BYTES;  // a pair splits Y's rows between its CTAs
     static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
     static constexpr int TMEM_COLS = 2 * BN;
     static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 512;
@@ -247,13 +303,13 @@ __device__ __forceinline__ float gelu_lane(float x) {
     return __fmul_rn(0.5f, __fmul_rn(x, b));
 }
 
-template <int BN, int STAGES, bool FUSED, bool F16>
+template <int BN, int STAGES, bool FUSED, bool F16, bool PAIR>
 __global__ void __maxnreg__(kLaunchRegs)
     gemm_3x(const __grid_constant__ CUtensorMap map_xhi, const __grid_constant__ CUtensorMap map_xlo,
                 const __grid_constant__ CUtensorMap map_yhi, const __grid_constant__ CUtensorMap map_ylo,
                 const __grid_constant__ CUtensorMap map_bias, float* __restrict__ r, int M, int N, int Kp, int64_t ldr, int* status, const Epi epi,
                 int seg_kb, int batch) {
-    using C = Cfg<BN, STAGES>;
+    using C = Cfg<BN, STAGES, PAIR>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t* ring = smem;
@@ -269,7 +325,13 @@ __global__ void __maxnreg__(kLaunchRegs)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int num_m = (M + BM - 1) / BM;
+    // a pair computes 256-row tiles: CTA `rank` owns rows [128*rank, 128*rank + 128) of each
+    // and loads Y's rows [BN/2*rank, BN/2*rank + BN/2) of its column block
+    constexpr int TM = PAIR ? 2 * BM : BM;
+    const uint32_t rank = PAIR ? cluster_rank() : 0;
+    const int unit = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;  // this CTA's (pair's) tile stream
+    const int units = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+    const int num_m = (M + TM - 1) / TM;
     const int num_n = (N + BN - 1) / BN;
     const int tiles_per_batch = num_m * num_n;
     const int tiles = tiles_per_batch * batch;  // batch b's operands start at rows b*M (X) and b*N (Y)
@@ -284,7 +346,7 @@ __global__ void __maxnreg__(kLaunchRegs)
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&acc_full[a], 1);
-            mbar_init(&acc_empty[a], 32 * kEpiWarps);
+            mbar_init(&acc_empty[a], PAIR ? 2 * kEpiWarps : 32 * kEpiWarps);  // a pair: one arrive per warp
         }
         mbar_init(drain, 1);
         for (int e = 0; e < kEpiWarps; ++e) mbar_init(&bias_full[e], 1);
@@ -292,12 +354,21 @@ __global__ void __maxnreg__(kLaunchRegs)
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"((uint32_t)C::TMEM_COLS));
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+        if constexpr (PAIR) {  // warp 1 of both CTAs: each gets the same columns in its own TMEM
+            asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                             smem_u32(tmem_slot)),
+                         "r"((uint32_t)C::TMEM_COLS));
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+        } else {
+            asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                             smem_u32(tmem_slot)),
+                         "r"((uint32_t)C::TMEM_COLS));
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+        }
     }
     tc_fence_before();
-    __syncthreads();
+    if constexpr (PAIR) cluster_sync();  // barriers of both CTAs are initialised before any remote use
+    else __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
@@ -310,28 +381,39 @@ __global__ void __maxnreg__(kLaunchRegs)
             asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&map_yhi) : "memory");
             asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&map_ylo) : "memory");
             uint32_t it = 0;
-            for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+            for (int t = unit; t < tiles; t += units) {
                 int mb, nb;
                 const int bt = t / tiles_per_batch;
                 tile_coords(t - bt * tiles_per_batch, num_m, num_n, mb, nb);
-                const int xrow = bt * M + mb * BM, yrow = bt * N + nb * BN;
+                const int xrow = bt * M + mb * TM + (int)rank * BM;
+                const int yrow = bt * N + nb * BN + (int)rank * (BN / 2) * (PAIR ? 1 : 0);
                 for (int kb = 0; kb < nk; ++kb, ++it) {
                     const uint32_t s = it % STAGES, round = it / STAGES;
                     if (!mbar_wait(&empty[s], (round & 1) ^ 1, ab, 1)) goto done;
                     uint8_t* st = ring + s * C::STAGE_BYTES;
-                    mbar_expect_tx(&full[s], C::STAGE_BYTES);
-                    tma_load_2d(&map_xhi, &full[s], st, kb * KE, xrow);
-                    tma_load_2d(&map_xlo, &full[s], st + C::A_BYTES, kb * KE, xrow);
-                    tma_load_2d(&map_yhi, &full[s], st + 2 * C::A_BYTES, kb * KE, yrow);
-                    tma_load_2d(&map_ylo, &full[s], st + 2 * C::A_BYTES + C::B_BYTES, kb * KE, yrow);
+                    if constexpr (PAIR) {
+                        // both CTAs' loads complete on the leader's full barrier, which expects both
+                        const uint32_t fb = mapa_rank(smem_u32(&full[s]), 0);
+                        if (rank == 0) mbar_expect_tx(&full[s], 2 * C::STAGE_BYTES);
+                        tma_load_2d_pair(&map_xhi, fb, st, kb * KE, xrow);
+                        tma_load_2d_pair(&map_xlo, fb, st + C::A_BYTES, kb * KE, xrow);
+                        tma_load_2d_pair(&map_yhi, fb, st + 2 * C::A_BYTES, kb * KE, yrow);
+                        tma_load_2d_pair(&map_ylo, fb, st + 2 * C::A_BYTES + C::B_BYTES, kb * KE, yrow);
+                    } else {
+                        mbar_expect_tx(&full[s], C::STAGE_BYTES);
+                        tma_load_2d(&map_xhi, &full[s], st, kb * KE, xrow);
+                        tma_load_2d(&map_xlo, &full[s], st + C::A_BYTES, kb * KE, xrow);
+                        tma_load_2d(&map_yhi, &full[s], st + 2 * C::A_BYTES, kb * KE, yrow);
+                        tma_load_2d(&map_ylo, &full[s], st + 2 * C::A_BYTES + C::B_BYTES, kb * KE, yrow);
+                    }
                 }
             }
         }
     } else if (warp == 1) {
-        if (lane == 0) {  // ---- MMA issuer: one TMEM accumulator per K segment, two in flight
-            constexpr uint32_t idesc = idesc_3x(BN, F16);
+        if (lane == 0 && rank == 0) {  // ---- MMA issuer (a pair's leader): one TMEM accumulator per K segment, two in flight
+            constexpr uint32_t idesc = idesc_3x(BN, F16, TM);
             uint32_t it = 0, gseg = 0;
-            for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+            for (int t = unit; t < tiles; t += units) {
                 for (int kb0 = 0; kb0 < nk; kb0 += seg_kb, ++gseg) {
                     const uint32_t b = gseg & 1, bround = gseg >> 1;
                     if (!mbar_wait(&acc_empty[b], (bround & 1) ^ 1, ab, 2)) goto done;
@@ -349,13 +431,15 @@ __global__ void __maxnreg__(kLaunchRegs)
                             const uint64_t xlo = sw_desc(base + C::A_BYTES + kk * 32);
                             const uint64_t yhi = sw_desc(base + 2 * C::A_BYTES + kk * 32);
                             const uint64_t ylo = sw_desc(base + 2 * C::A_BYTES + C::B_BYTES + kk * 32);
-                            umma<F16>(d, xlo, yhi, idesc, (kb != kb0 || kk != 0) ? 1u : 0u);
-                            umma<F16>(d, xhi, ylo, idesc, 1);
-                            umma<F16>(d, xhi, yhi, idesc, 1);
+                            umma<F16, PAIR>(d, xlo, yhi, idesc, (kb != kb0 || kk != 0) ? 1u : 0u);
+                            umma<F16, PAIR>(d, xhi, ylo, idesc, 1);
+                            umma<F16, PAIR>(d, xhi, yhi, idesc, 1);
                         }
-                        umma_commit(&empty[s]);
+                        if constexpr (PAIR) umma_commit_pair(&empty[s]);  // frees the stage in both CTAs
+                        else umma_commit(&empty[s]);
                     }
-                    umma_commit(&acc_full[b]);
+                    if constexpr (PAIR) umma_commit_pair(&acc_full[b]);
+                    else umma_commit(&acc_full[b]);
                 }
             }
         }
@@ -370,13 +454,14 @@ __global__ void __maxnreg__(kLaunchRegs)
         uint32_t bphase = 0;
         const bool vec = ((ldr & 3) == 0) && ((((uintptr_t)r) & 15) == 0);
         uint32_t gseg = 0;
-        for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+        for (int t = unit; t < tiles; t += units) {
             int mb, nb;
             const int bt = t / tiles_per_batch;
             tile_coords(t - bt * tiles_per_batch, num_m, num_n, mb, nb);
+            const int mrow = mb * TM + (int)rank * BM;  // this CTA's first row of the tile
             if constexpr (FUSED) {
                 // bring this thread's bias row slice toward L2 now; it is read after the last segment
-                const int prow = mb * BM + q * 32 + lane;
+                const int prow = mrow + q * 32 + lane;
                 if (epi.bias && prow < M) {
                     const float* pb = epi.bias + (int64_t)prow * N + nb * BN + h * HC;
 #pragma unroll
@@ -384,7 +469,7 @@ __global__ void __maxnreg__(kLaunchRegs)
                         if (nb * BN + h * HC + j < N) asm volatile("prefetch.global.L2 [%0];" ::"l"(pb + j));
                 }
             }
-            const int row0 = mb * BM + q * 32;  // this warp's first row
+            const int row0 = mrow + q * 32;  // this warp's first row
             const int colh = nb * BN + h * HC;
             // the bias chunk of 32 columns goes through shared memory when the map covers it
             auto stage_bias = [&](int cb) {
@@ -419,7 +504,12 @@ __global__ void __maxnreg__(kLaunchRegs)
                     }
                 }
                 tc_fence_before();
-                mbar_arrive(&acc_empty[b]);
+                if constexpr (PAIR) {  // release the accumulator on the leader's barrier, once per warp
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_cluster(mapa_rank(smem_u32(&acc_empty[b]), 0));
+                } else {
+                    mbar_arrive(&acc_empty[b]);
+                }
             }
             if (row0 >= M) continue;  // the whole warp is past the last row
             const int row = row0 + lane;
@@ -511,16 +601,25 @@ __global__ void __maxnreg__(kLaunchRegs)
     }
 done:
     __syncthreads();
+    if (warp == 1 && lane == 0 && rank == 0 && *abort_flag) {
+        // let MMAs still in flight finish before the accumulators are released
+        if constexpr (PAIR) umma_commit_pair_local(drain);
+        else umma_commit(drain);
+        for (uint32_t i = 0; i < kWaitLimit && !mbar_test(drain, 0); ++i) __nanosleep(64);
+    }
+    if constexpr (PAIR) {  // neither CTA leaves while its peer may still signal it or write its TMEM
+        tc_fence_before();
+        cluster_sync();
+    }
     if (warp == 1) {
-        if (*abort_flag && lane == 0) {
-            // let MMAs still in flight finish before the accumulator is released
-            umma_commit(drain);
-            for (uint32_t i = 0; i < kWaitLimit && !mbar_test(drain, 0); ++i) __nanosleep(64);
-        }
         __syncwarp();
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
-                     "r"((uint32_t)C::TMEM_COLS));
+        if constexpr (PAIR)
+            asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                         "r"((uint32_t)C::TMEM_COLS));
+        else
+            asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                         "r"((uint32_t)C::TMEM_COLS));
     }
 }
 
@@ -640,6 +739,57 @@ __global__ void __launch_bounds__(256) split_rows_f16(const float* __restrict__ 
         __half h[4], l[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) split_f16(v[j], scale, h[j], l[j]);
+        *(uint2*)(hr + k) = make_uint2(pack2(h[0], h[1]), pack2(h[2], h[3]));
+        *(uint2*)(lr + k) = make_uint2(pack2(l[0], l[1]), pack2(l[2], l[3]));
+    }
+}
+
+// The same split for rows of up to 1024*V elements: one 256-thread CTA per row keeps the row
+// in registers (V float4 per thread), so X is read from HBM once.
+template <int V>
+__global__ void __launch_bounds__(256) split_rows_f16_block(const float* __restrict__ x, __half* __restrict__ hi,
+                                                            __half* __restrict__ lo, int* __restrict__ row_exp,
+                                                            int64_t K, int64_t Kp) {
+    __shared__ float wmax[8];
+    const int64_t m = blockIdx.x;
+    const float* xr = x + m * K;
+    const bool vec = (K % 4 == 0) && ((((uintptr_t)x) & 15) == 0);
+    float4 v[V];
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+        const int64_t k = ((int64_t)i * 256 + threadIdx.x) * 4;
+        if (vec && k + 4 <= K) {
+            v[i] = __ldcs((const float4*)(xr + k));
+        } else {
+            v[i].x = k < K ? xr[k] : 0.0f;
+            v[i].y = k + 1 < K ? xr[k + 1] : 0.0f;
+            v[i].z = k + 2 < K ? xr[k + 2] : 0.0f;
+            v[i].w = k + 3 < K ? xr[k + 3] : 0.0f;
+        }
+        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = amax;
+    __syncthreads();
+    amax = wmax[0];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) amax = fmaxf(amax, wmax[w]);
+    const int e = scale_exp(amax);
+    const float scale = __int_as_float((127 + e) << 23);
+    if (threadIdx.x == 0) row_exp[m] = e;
+    __half* hr = hi + m * Kp;
+    __half* lr = lo + m * Kp;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+        const int64_t k = ((int64_t)i * 256 + threadIdx.x) * 4;
+        if (k >= Kp) break;
+        __half h[4], l[4];
+        split_f16(v[i].x, scale, h[0], l[0]);
+        split_f16(v[i].y, scale, h[1], l[1]);
+        split_f16(v[i].z, scale, h[2], l[2]);
+        split_f16(v[i].w, scale, h[3], l[3]);
         *(uint2*)(hr + k) = make_uint2(pack2(h[0], h[1]), pack2(h[2], h[3]));
         *(uint2*)(lr + k) = make_uint2(pack2(l[0], l[1]), pack2(l[2], l[3]));
     }
@@ -784,18 +934,60 @@ bool make_bias_map(CUtensorMap* m, const float* bias, int64_t M, int64_t N) {
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <bool FUSED, bool F16>
+constexpr int kStagesPair = 6;  // 32 KB stages: A rows and half of Y's rows per CTA
+
+// Tensor-core products use CTA pairs (M = 256 per MMA, half of Y per CTA, so each SM
+// stages a third less per k-step) unless MAG_CUDA_TC_PAIR=0.
+bool use_pairs() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("MAG_CUDA_TC_PAIR");
+        v = (e && *e == '0') ? 0 : 1;
+    }
+    return v == 1;
+}
+
+template <bool FUSED, bool F16, bool PAIR>
 int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c, const CUtensorMap& d,
                 const CUtensorMap& bias, float* r, int64_t M, int64_t N, int64_t kp, int* status, const Epi& epi,
-                int64_t B, int grid, cudaStream_t st) {
-    using C = Cfg<kBN, kStages>;
-    auto kern = gemm_3x<kBN, kStages, FUSED, F16>;
+                int64_t B, cudaStream_t st) {
+    constexpr int STG = PAIR ? kStagesPair : kStages;
+    using C = Cfg<kBN, STG, PAIR>;
+    auto kern = gemm_3x<kBN, STG, FUSED, F16, PAIR>;
     const int smem = FUSED ? C::SMEM_BIAS : C::SMEM;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return (int)e;
-    kern<<<grid, kThreads, smem, st>>>(a, b, c, d, bias, r, (int)M, (int)N, (int)kp, (int64_t)N, status, epi,
-                                       segment_kb(F16), (int)B);
-    return (int)cudaGetLastError();
+    const int64_t tm = PAIR ? 2 * BM : BM;
+    const int64_t tiles = B * ((M + tm - 1) / tm) * ((N + kBN - 1) / kBN);
+    if constexpr (!PAIR) {
+        const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
+        kern<<<grid, kThreads, smem, st>>>(a, b, c, d, bias, r, (int)M, (int)N, (int)kp, (int64_t)N, status, epi,
+                                           segment_kb(F16), (int)B);
+        return (int)cudaGetLastError();
+    } else {
+        cudaLaunchConfig_t cfg = {};
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = (size_t)smem;
+        cfg.stream = st;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        cfg.gridDim = dim3((unsigned)sm_count());
+        int max_clusters = 0;
+        if (cudaOccupancyMaxActiveClusters(&max_clusters, kern, &cfg) != cudaSuccess || max_clusters <= 0) {
+            cudaGetLastError();
+            max_clusters = sm_count() / 2;
+        }
+        const int64_t clusters = tiles < max_clusters ? tiles : max_clusters;
+        cfg.gridDim = dim3((unsigned)(2 * clusters));
+        e = cudaLaunchKernelEx(&cfg, kern, a, b, c, d, bias, r, (int)M, (int)N, (int)kp, (int64_t)N, status, epi,
+                               segment_kb(F16), (int)B);
+        return (int)e;
+    }
 }
 
 }  // namespace
@@ -846,8 +1038,13 @@ static int launch_tc(float* r, const float* x, const float* y, int64_t B, int64_
         xhi = (void*)ep->a_hi;
         xlo = (void*)ep->a_lo;
     } else if (f16) {
-        split_rows_f16<<<(unsigned)((B * M + 7) / 8), 256, 0, st>>>(x, (__half*)xhi, (__half*)xlo, rexp, B * M, K,
-                                                                   l.kp);
+        __half *h16 = (__half*)xhi, *l16 = (__half*)xlo;
+        const unsigned rows = (unsigned)(B * M);
+        if (l.kp <= 1024) split_rows_f16_block<1><<<rows, 256, 0, st>>>(x, h16, l16, rexp, K, l.kp);
+        else if (l.kp <= 2048) split_rows_f16_block<2><<<rows, 256, 0, st>>>(x, h16, l16, rexp, K, l.kp);
+        else if (l.kp <= 4096) split_rows_f16_block<4><<<rows, 256, 0, st>>>(x, h16, l16, rexp, K, l.kp);
+        else if (l.kp <= 8192) split_rows_f16_block<8><<<rows, 256, 0, st>>>(x, h16, l16, rexp, K, l.kp);
+        else split_rows_f16<<<(unsigned)((B * M + 7) / 8), 256, 0, st>>>(x, h16, l16, rexp, B * M, K, l.kp);
     } else {
         int64_t n = B * M * (l.kp / 4);  // X of all batches is one (B*M) x K row-major matrix
         int64_t g = (n + 255) / 256;
@@ -867,11 +1064,11 @@ static int launch_tc(float* r, const float* x, const float* y, int64_t B, int64_
     }
     CUtensorMap mxh, mxl, myh, myl;
     const bool h = f16 != 0;
+    const bool pair = h && use_pairs();
+    const int yrows = pair ? kBN / 2 : kBN;
     if (!make_map(&mxh, xhi, B * M, l.kp, BM, h) || !make_map(&mxl, xlo, B * M, l.kp, BM, h) ||
-        !make_map(&myh, yhi, B * N, l.kp, kBN, h) || !make_map(&myl, ylo, B * N, l.kp, kBN, h))
+        !make_map(&myh, yhi, B * N, l.kp, yrows, h) || !make_map(&myl, ylo, B * N, l.kp, yrows, h))
         return (int)cudaErrorInvalidValue;
-    const int64_t tiles = B * ((M + BM - 1) / BM) * ((N + kBN - 1) / kBN);
-    const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
     Epi epi{};
     epi.row_exp = rexp;
     epi.col_exp = cexp;
@@ -886,11 +1083,13 @@ static int launch_tc(float* r, const float* x, const float* y, int64_t B, int64_
         CUtensorMap mb;
         memset(&mb, 0, sizeof(mb));
         epi.bias_map = ep->bias && make_bias_map(&mb, ep->bias, M, N);
-        return f16 ? launch_gemm<true, true>(mxh, mxl, myh, myl, mb, r, M, N, l.kp, status, epi, B, grid, st)
-                   : launch_gemm<true, false>(mxh, mxl, myh, myl, mb, r, M, N, l.kp, status, epi, B, grid, st);
+        if (pair) return launch_gemm<true, true, true>(mxh, mxl, myh, myl, mb, r, M, N, l.kp, status, epi, B, st);
+        return f16 ? launch_gemm<true, true, false>(mxh, mxl, myh, myl, mb, r, M, N, l.kp, status, epi, B, st)
+                   : launch_gemm<true, false, false>(mxh, mxl, myh, myl, mb, r, M, N, l.kp, status, epi, B, st);
     }
-    return f16 ? launch_gemm<false, true>(mxh, mxl, myh, myl, mxh, r, M, N, l.kp, status, epi, B, grid, st)
-               : launch_gemm<false, false>(mxh, mxl, myh, myl, mxh, r, M, N, l.kp, status, epi, B, grid, st);
+    if (pair) return launch_gemm<false, true, true>(mxh, mxl, myh, myl, mxh, r, M, N, l.kp, status, epi, B, st);
+    return f16 ? launch_gemm<false, true, false>(mxh, mxl, myh, myl, mxh, r, M, N, l.kp, status, epi, B, st)
+               : launch_gemm<false, false, false>(mxh, mxl, myh, myl, mxh, r, M, N, l.kp, status, epi, B, st);
 }
 
 extern "C" int mcu_launch_matmul_tc(float* r, const float* x, const float* y, int64_t M, int64_t K, int64_t N,
