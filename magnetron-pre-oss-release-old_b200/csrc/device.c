@@ -389,10 +389,11 @@ enum { MM_EXACT, MM_SKINNY, MM_TC };
 
 static int matmul_path(mcu_device* d, int64_t M, int64_t K, int64_t N) {
     if (d->matmul_mode == 1) return MM_EXACT;
-    int tc_ok = mcu_matmul_tc_supported() && M >= 128 && N >= 64 && K >= 32;
+    int tc_ok = mcu_matmul_tc_supported() && M >= 32 && N >= 64 && K >= 32;
     if (d->matmul_mode == 2 && tc_ok) return MM_TC;
+    if (M < 32 && K * N >= ((int64_t)1 << 20)) return MM_SKINNY; /* HBM-bound: Y is read once */
+    if (tc_ok && (double)M * (double)N * (double)K >= 1.0e9) return MM_TC; /* split K fills the GPU */
     if (M <= 64 && K * N >= ((int64_t)1 << 20)) return MM_SKINNY;
-    if (tc_ok && (double)M * (double)N * (double)K >= 1.0e9) return MM_TC;
     return MM_EXACT;
 }
 
@@ -497,7 +498,7 @@ static int exec_node(mcu_device* d, mag_tensor_t* r) {
                 if (!rc) mcu_count_launches(2);
             } else if (path == MM_TC) {
                 rc = mcu_launch_matmul_tc(fptr(r), px, py, M, K, N, scratch, d->d_status, st, d->tc_f16);
-                if (!rc) mcu_count_launches(d->tc_f16 ? 4 : 3);
+                if (!rc) mcu_count_launches(mcu_matmul_tc_kernels(M, K, N, d->tc_f16, 0));
             } else {
                 rc = mcu_launch_matmul_exact(fptr(r), px, py, 1, M, K, N, r_ld, accumulate, st);
                 if (!rc) mcu_count_launches(1);
@@ -784,7 +785,7 @@ int mag_cuda_matmul_f32(mag_compute_device_t* dvc, float* r, const float* x, con
     } else if (path == MM_TC) {
         rc = mcu_launch_matmul_tc(r, x, y, M, K, N, scratch_get(d, mcu_matmul_tc_scratch_bytes(M, K, N)),
                                   d->d_status, d->stream, d->tc_f16);
-        if (!rc) mcu_count_launches(d->tc_f16 ? 4 : 3);
+        if (!rc) mcu_count_launches(mcu_matmul_tc_kernels(M, K, N, d->tc_f16, 0));
     } else {
         rc = mcu_launch_matmul_exact(r, x, y, 1, M, K, N, N, 0, d->stream);
         if (!rc) mcu_count_launches(1);
@@ -1315,7 +1316,7 @@ static int exec_planned_matmul(mcu_device* d, mag_tensor_t* m, const mcu_plan_it
     }
     int rc = mcu_launch_matmul_tc_ex(fptr(out), fptr(x), fptr(y), M, K, N, scratch, d->d_status, d->stream, &ep,
                                      d->tc_f16);
-    if (!rc) mcu_count_launches(d->tc_f16 ? 4 : (it->a_split >= 0 ? 2 : 3));
+    if (!rc) mcu_count_launches(mcu_matmul_tc_kernels(M, K, N, d->tc_f16, it->a_split >= 0));
     return rc;
 }
 

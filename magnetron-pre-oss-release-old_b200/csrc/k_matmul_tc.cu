@@ -308,7 +308,7 @@ __global__ void __maxnreg__(kLaunchRegs)
     gemm_3x(const __grid_constant__ CUtensorMap map_xhi, const __grid_constant__ CUtensorMap map_xlo,
                 const __grid_constant__ CUtensorMap map_yhi, const __grid_constant__ CUtensorMap map_ylo,
                 const __grid_constant__ CUtensorMap map_bias, float* __restrict__ r, int M, int N, int Kp, int64_t ldr, int* status, const Epi epi,
-                int seg_kb, int batch) {
+                int seg_kb, int batch, int kparts, float* __restrict__ part_out) {
     using C = Cfg<BN, STAGES, PAIR>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -337,6 +337,10 @@ __global__ void __maxnreg__(kLaunchRegs)
     const int tiles = tiles_per_batch * batch;  // batch b's operands start at rows b*M (X) and b*N (Y)
     constexpr int KE = F16 ? BK16 : BK;          // K elements per ring stage
     const int nk = Kp / KE;
+    // split K (kparts > 1, one batch, no fused epilogue): work unit u is part u % kparts of tile
+    // u / kparts, K stages [part*kpc, part*kpc + kpc), written to part_out[part] for a fixed-order sum
+    const int kpc = (nk + kparts - 1) / kparts;
+    const int work = tiles * kparts;
     Abort ab{abort_flag, status};
 
     if (threadIdx.x == 0) {
@@ -381,13 +385,15 @@ __global__ void __maxnreg__(kLaunchRegs)
             asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&map_yhi) : "memory");
             asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&map_ylo) : "memory");
             uint32_t it = 0;
-            for (int t = unit; t < tiles; t += units) {
+            for (int u = unit; u < work; u += units) {
+                const int t = u / kparts, part = u - t * kparts;
+                const int kbeg = part * kpc, kend = min(nk, kbeg + kpc);
                 int mb, nb;
                 const int bt = t / tiles_per_batch;
                 tile_coords(t - bt * tiles_per_batch, num_m, num_n, mb, nb);
                 const int xrow = bt * M + mb * TM + (int)rank * BM;
                 const int yrow = bt * N + nb * BN + (int)rank * (BN / 2) * (PAIR ? 1 : 0);
-                for (int kb = 0; kb < nk; ++kb, ++it) {
+                for (int kb = kbeg; kb < kend; ++kb, ++it) {
                     const uint32_t s = it % STAGES, round = it / STAGES;
                     if (!mbar_wait(&empty[s], (round & 1) ^ 1, ab, 1)) goto done;
                     uint8_t* st = ring + s * C::STAGE_BYTES;
@@ -413,13 +419,15 @@ __global__ void __maxnreg__(kLaunchRegs)
         if (lane == 0 && rank == 0) {  // ---- MMA issuer (a pair's leader): one TMEM accumulator per K segment, two in flight
             constexpr uint32_t idesc = idesc_3x(BN, F16, TM);
             uint32_t it = 0, gseg = 0;
-            for (int t = unit; t < tiles; t += units) {
-                for (int kb0 = 0; kb0 < nk; kb0 += seg_kb, ++gseg) {
+            for (int u = unit; u < work; u += units) {
+                const int part = u % kparts;
+                const int kbeg = part * kpc, kend = min(nk, kbeg + kpc);
+                for (int kb0 = kbeg; kb0 < kend; kb0 += seg_kb, ++gseg) {
                     const uint32_t b = gseg & 1, bround = gseg >> 1;
                     if (!mbar_wait(&acc_empty[b], (bround & 1) ^ 1, ab, 2)) goto done;
                     tc_fence_after();
                     const uint32_t d = tmem_base + b * BN;
-                    const int kb1 = min(kb0 + seg_kb, nk);
+                    const int kb1 = min(kb0 + seg_kb, kend);
                     for (int kb = kb0; kb < kb1; ++kb, ++it) {
                         const uint32_t s = it % STAGES, round = it / STAGES;
                         if (!mbar_wait(&full[s], round & 1, ab, 3)) goto done;
@@ -454,7 +462,10 @@ __global__ void __maxnreg__(kLaunchRegs)
         uint32_t bphase = 0;
         const bool vec = ((ldr & 3) == 0) && ((((uintptr_t)r) & 15) == 0);
         uint32_t gseg = 0;
-        for (int t = unit; t < tiles; t += units) {
+        for (int u = unit; u < work; u += units) {
+            const int t = u / kparts, part = u - t * kparts;
+            const int kbeg = part * kpc, kend = min(nk, kbeg + kpc);
+            float* const rb = kparts > 1 ? part_out + (int64_t)part * M * N : r;  // (kparts > 1: one batch)
             int mb, nb;
             const int bt = t / tiles_per_batch;
             tile_coords(t - bt * tiles_per_batch, num_m, num_n, mb, nb);
@@ -483,9 +494,9 @@ __global__ void __maxnreg__(kLaunchRegs)
             bool staged0 = false;
             // segment sums are added in registers with round-to-nearest
             float sum[HC];
-            for (int kb0 = 0; kb0 < nk; kb0 += seg_kb, ++gseg) {
+            for (int kb0 = kbeg; kb0 < kend; kb0 += seg_kb, ++gseg) {
                 const uint32_t b = gseg & 1, bround = gseg >> 1;
-                if (map_ok && !staged0 && kb0 + seg_kb >= nk && colh + 32 <= N) {
+                if (map_ok && !staged0 && kb0 + seg_kb >= kend && colh + 32 <= N) {
                     stage_bias(colh);  // the first chunk loads while the last segment accumulates
                     staged0 = true;
                 }
@@ -495,7 +506,7 @@ __global__ void __maxnreg__(kLaunchRegs)
                 for (int c = 0; c < HC / 32; ++c) {
                     uint32_t v[32];
                     tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + b * BN + h * HC + c * 32, v);
-                    if (kb0 == 0) {
+                    if (kb0 == kbeg) {
 #pragma unroll
                         for (int j = 0; j < 32; ++j) sum[c * 32 + j] = __uint_as_float(v[j]);
                     } else {
@@ -515,7 +526,7 @@ __global__ void __maxnreg__(kLaunchRegs)
             const int row = row0 + lane;
             const bool row_ok = row < M;
             const int rowc = row_ok ? row : row0;  // lanes past M compute but store nothing
-            float* out = r + (int64_t)bt * M * ldr + (int64_t)rowc * ldr + colh;
+            float* out = rb + (int64_t)bt * M * ldr + (int64_t)rowc * ldr + colh;
             int ea = 0;
             if constexpr (F16) ea = epi.row_exp[(int64_t)bt * M + rowc];
 #pragma unroll
@@ -795,50 +806,96 @@ __global__ void __launch_bounds__(256) split_rows_f16_block(const float* __restr
     }
 }
 
-// Column maxima of Y[b][K][N] as f32 bits (|y| compares as an unsigned integer; NaN above inf).
+// Split-K: r = part[0] + part[1] + ... in that order (f32 adds, so the result does not
+// depend on which parts finished first), then a fused layer's bias, GELU and tf32 operand
+// split exactly as the GEMM epilogue (and the separate ADD and GELU ops) apply them.
+__global__ void __launch_bounds__(256) sum_parts(float* __restrict__ r, const float* __restrict__ part, int64_t M,
+                                                 int64_t N, int parts, const Epi epi) {
+    const int64_t n = M * N;
+    if (!epi.out_hi && (n & 3) == 0 && ((((uintptr_t)r) & 15) == 0) && (!epi.bias || ((((uintptr_t)epi.bias) & 15) == 0))) {
+        for (int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x; i < n / 4; i += (int64_t)gridDim.x * 256) {
+            float4 a = __ldcs((const float4*)part + i);
+            for (int p = 1; p < parts; ++p) {
+                const float4 b = __ldcs((const float4*)(part + (int64_t)p * n) + i);
+                a.x = __fadd_rn(a.x, b.x); a.y = __fadd_rn(a.y, b.y);
+                a.z = __fadd_rn(a.z, b.z); a.w = __fadd_rn(a.w, b.w);
+            }
+            if (epi.bias) {
+                const float4 b = ((const float4*)epi.bias)[i];
+                a.x = __fadd_rn(a.x, b.x); a.y = __fadd_rn(a.y, b.y);
+                a.z = __fadd_rn(a.z, b.z); a.w = __fadd_rn(a.w, b.w);
+            }
+            if (epi.act == 1) {
+                a.x = gelu_lane(a.x); a.y = gelu_lane(a.y); a.z = gelu_lane(a.z); a.w = gelu_lane(a.w);
+            }
+            ((float4*)r)[i] = a;
+        }
+        return;
+    }
+    for (int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x; i < n; i += (int64_t)gridDim.x * 256) {
+        float a = __ldcs(part + i);
+        for (int p = 1; p < parts; ++p) a = __fadd_rn(a, __ldcs(part + (int64_t)p * n + i));
+        if (epi.bias) a = __fadd_rn(a, epi.bias[i]);
+        if (epi.act == 1) a = gelu_lane(a);
+        r[i] = a;
+        if (epi.out_hi) {
+            const int64_t row = i / N, col = i - row * N;
+            const float hh = rna_tf32_dev(a);
+            epi.out_hi[row * epi.kp_out + col] = hh;
+            epi.out_lo[row * epi.kp_out + col] = rna_tf32_dev(a - hh);
+        }
+    }
+}
+
+// Column maxima of Y[b][K][N] as f32 bits (|y| compares as an unsigned integer; NaN above inf):
+// a thread per column and 32-row chunk, eight independent loads in flight.
 __global__ void __launch_bounds__(256) col_absmax(const float* __restrict__ y, unsigned* __restrict__ cmax, int64_t K,
                                                   int64_t N) {
     const int64_t n = (int64_t)blockIdx.x * 256 + threadIdx.x;
     if (n >= N) return;
     y += (int64_t)blockIdx.z * K * N;
-    const int64_t k0 = (int64_t)blockIdx.y * 128, k1 = k0 + 128 < K ? k0 + 128 : K;
+    const int64_t k0 = (int64_t)blockIdx.y * 32, k1 = k0 + 32 < K ? k0 + 32 : K;
     unsigned m = 0;
-    for (int64_t k = k0; k < k1; ++k) m = max(m, __float_as_uint(y[k * N + n]) & 0x7FFFFFFFu);
+#pragma unroll 8
+    for (int64_t k = k0; k < k1; ++k) m = max(m, __float_as_uint(__ldg(y + k * N + n)) & 0x7FFFFFFFu);
     atomicMax(cmax + (int64_t)blockIdx.z * N + n, m);
 }
 
-// Y[K][N] -> hi/lo transposed [N][Kp] f16 through a 32x32 shared tile, scaled per column;
-// col_exp[N] written by the first k-block.
+// Y[K][N] -> hi/lo transposed [N][Kp] f16 through a 64 (k) x 64 (n) shared tile, scaled per
+// column; each thread stores pairs of consecutive k as one 32-bit word.  col_exp[N] is
+// written by the first k-block.
 __global__ void __launch_bounds__(256) split_cols_t_f16(const float* __restrict__ y, const unsigned* __restrict__ cmax,
                                                         __half* __restrict__ hi, __half* __restrict__ lo,
                                                         int* __restrict__ col_exp, int64_t K, int64_t N, int64_t Kp) {
-    __shared__ float tile[32][33];
-    __shared__ float scl[32];
+    __shared__ float tile[64][65];
+    __shared__ float scl[64];
     y += (int64_t)blockIdx.z * K * N;
     hi += (int64_t)blockIdx.z * N * Kp;
     lo += (int64_t)blockIdx.z * N * Kp;
     cmax += (int64_t)blockIdx.z * N;
     col_exp += (int64_t)blockIdx.z * N;
-    const int64_t k0 = (int64_t)blockIdx.y * 32, n0 = (int64_t)blockIdx.x * 32;
-    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-    if (threadIdx.x < 32 && n0 + tx < N) {
-        const unsigned b = cmax[n0 + tx];
+    const int64_t k0 = (int64_t)blockIdx.y * 64, n0 = (int64_t)blockIdx.x * 64;
+    const int tx = threadIdx.x & 63, ty = threadIdx.x >> 6;  // 64 x 4
+    if (threadIdx.x < 64 && n0 + threadIdx.x < N) {
+        const unsigned b = cmax[n0 + threadIdx.x];
         const int e = b > 0x7F800000u ? 0 : scale_exp(__uint_as_float(b));
-        scl[tx] = __int_as_float((127 + e) << 23);
-        if (blockIdx.y == 0) col_exp[n0 + tx] = e;
+        scl[threadIdx.x] = __int_as_float((127 + e) << 23);
+        if (blockIdx.y == 0) col_exp[n0 + threadIdx.x] = e;
     }
-    for (int j = ty; j < 32; j += 8) {
+    for (int j = ty; j < 64; j += 4) {  // coalesced rows of Y
         const int64_t k = k0 + j, n = n0 + tx;
         tile[j][tx] = (k < K && n < N) ? y[k * N + n] : 0.0f;
     }
     __syncthreads();
-    for (int j = ty; j < 32; j += 8) {
-        const int64_t n = n0 + j, k = k0 + tx;
-        if (n < N && k < Kp) {
-            __half h, l;
-            split_f16(tile[tx][j], scl[j], h, l);
-            hi[n * Kp + k] = h;
-            lo[n * Kp + k] = l;
+    const int kk = (threadIdx.x & 31) * 2;  // two consecutive k per thread
+    for (int j = threadIdx.x >> 5; j < 64; j += 8) {
+        const int64_t n = n0 + j, k = k0 + kk;
+        if (n < N && k < Kp) {  // Kp is a multiple of 32: k and k + 1 are both inside
+            __half h0, l0, h1, l1;
+            split_f16(tile[kk][j], scl[j], h0, l0);
+            split_f16(tile[kk + 1][j], scl[j], h1, l1);
+            *(uint32_t*)(hi + n * Kp + k) = pack2(h0, h1);
+            *(uint32_t*)(lo + n * Kp + k) = pack2(l0, l1);
         }
     }
 }
@@ -877,8 +934,42 @@ int64_t round_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
 // exponents and column maxima.  Sized for the tf32 split, which needs the most.
 struct Layout {
     int64_t kp;
-    size_t xhi, xlo, yhi, ylo, rexp, cexp, cmax, total;
+    size_t xhi, xlo, yhi, ylo, rexp, cexp, cmax, parts, total;
+    int kparts;  // split-K factor of an unfused single product (1: none)
 };
+
+constexpr int kStagesPair = 6;  // 32 KB stages: A rows and half of Y's rows per CTA
+
+// Tensor-core products use CTA pairs (M = 256 per MMA, half of Y per CTA, so each SM
+// stages a third less per k-step) unless MAG_CUDA_TC_PAIR=0.
+bool use_pairs() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("MAG_CUDA_TC_PAIR");
+        v = (e && *e == '0') ? 0 : 1;
+    }
+    return v == 1;
+}
+
+// Pairs compute 256-row tiles: products with fewer rows run one CTA per 128-row tile.
+bool pair_for(int64_t M, bool f16) { return f16 && use_pairs() && M >= 2 * BM; }
+
+// Split K when a single product has too few tiles to occupy the GPU: up to 16 parts of
+// at least 4 ring stages each, so tiles x parts approaches the number of CTAs (pairs).
+int choose_parts(int64_t M, int64_t K, int64_t N, bool f16) {
+    const bool pair = pair_for(M, f16);
+    const int64_t tm = pair ? 256 : 128;
+    const int64_t tiles = ((M + tm - 1) / tm) * ((N + 255) / 256);
+    const int64_t units = pair ? sm_count() / 2 : sm_count();
+    const int64_t kp = (K + KPAD - 1) / KPAD * KPAD;
+    const int64_t nk = kp / (f16 ? BK16 : BK);
+    int64_t parts = units / (tiles ? tiles : 1);
+    if (parts > nk / 4) parts = nk / 4;
+    if (parts > 16) parts = 16;
+    if (parts < 2) return 1;
+    const int64_t kpc = (nk + parts - 1) / parts;
+    return (int)((nk + kpc - 1) / kpc);  // no empty part
+}
 
 Layout layout(int64_t M, int64_t K, int64_t N, bool f16) {
     Layout l;
@@ -892,7 +983,9 @@ Layout layout(int64_t M, int64_t K, int64_t N, bool f16) {
     l.rexp = 2 * xs + 2 * ys;
     l.cexp = l.rexp + (size_t)round_up(M * 4, 256);
     l.cmax = l.cexp + (size_t)round_up(N * 4, 256);
-    l.total = f16 ? l.cmax + (size_t)round_up(N * 4, 256) : 2 * xs + 2 * ys;
+    l.parts = l.cmax + (size_t)round_up(N * 4, 256);
+    l.kparts = choose_parts(M, K, N, f16);
+    l.total = l.parts + (l.kparts > 1 ? (size_t)round_up((int64_t)l.kparts * M * N * 4, 256) : 0);
     return l;
 }
 
@@ -934,23 +1027,10 @@ bool make_bias_map(CUtensorMap* m, const float* bias, int64_t M, int64_t N) {
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-constexpr int kStagesPair = 6;  // 32 KB stages: A rows and half of Y's rows per CTA
-
-// Tensor-core products use CTA pairs (M = 256 per MMA, half of Y per CTA, so each SM
-// stages a third less per k-step) unless MAG_CUDA_TC_PAIR=0.
-bool use_pairs() {
-    static int v = -1;
-    if (v < 0) {
-        const char* e = getenv("MAG_CUDA_TC_PAIR");
-        v = (e && *e == '0') ? 0 : 1;
-    }
-    return v == 1;
-}
-
 template <bool FUSED, bool F16, bool PAIR>
 int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c, const CUtensorMap& d,
                 const CUtensorMap& bias, float* r, int64_t M, int64_t N, int64_t kp, int* status, const Epi& epi,
-                int64_t B, cudaStream_t st) {
+                int64_t B, cudaStream_t st, int kparts, float* part_out) {
     constexpr int STG = PAIR ? kStagesPair : kStages;
     using C = Cfg<kBN, STG, PAIR>;
     auto kern = gemm_3x<kBN, STG, FUSED, F16, PAIR>;
@@ -958,11 +1038,11 @@ int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return (int)e;
     const int64_t tm = PAIR ? 2 * BM : BM;
-    const int64_t tiles = B * ((M + tm - 1) / tm) * ((N + kBN - 1) / kBN);
+    const int64_t tiles = B * ((M + tm - 1) / tm) * ((N + kBN - 1) / kBN) * kparts;
     if constexpr (!PAIR) {
         const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
         kern<<<grid, kThreads, smem, st>>>(a, b, c, d, bias, r, (int)M, (int)N, (int)kp, (int64_t)N, status, epi,
-                                           segment_kb(F16), (int)B);
+                                           segment_kb(F16), (int)B, kparts, part_out);
         return (int)cudaGetLastError();
     } else {
         cudaLaunchConfig_t cfg = {};
@@ -985,7 +1065,7 @@ int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c
         const int64_t clusters = tiles < max_clusters ? tiles : max_clusters;
         cfg.gridDim = dim3((unsigned)(2 * clusters));
         e = cudaLaunchKernelEx(&cfg, kern, a, b, c, d, bias, r, (int)M, (int)N, (int)kp, (int64_t)N, status, epi,
-                               segment_kb(F16), (int)B);
+                               segment_kb(F16), (int)B, kparts, part_out);
         return (int)e;
     }
 }
@@ -998,6 +1078,11 @@ extern "C" int mcu_matmul_tc_supported(void) {
 }
 
 extern "C" size_t mcu_matmul_tc_scratch_bytes(int64_t M, int64_t K, int64_t N) { return scratch_bytes(M, K, N); }
+
+extern "C" int mcu_matmul_tc_kernels(int64_t M, int64_t K, int64_t N, int f16, int presplit) {
+    const int split = f16 ? 3 : (presplit ? 1 : 2);  // operand split kernels
+    return split + 1 + (choose_parts(M, K, N, f16 != 0) > 1 ? 1 : 0);
+}
 
 static int launch_tc(float* r, const float* x, const float* y, int64_t B, int64_t M, int64_t K, int64_t N,
                      void* scratch, int* status, cudaStream_t st, const mcu_tc_epilogue* ep, int f16);
@@ -1054,9 +1139,9 @@ static int launch_tc(float* r, const float* x, const float* y, int64_t B, int64_
     if (f16) {
         cudaError_t e = cudaMemsetAsync(cmax, 0, (size_t)(B * N) * 4, st);
         if (e != cudaSuccess) return (int)e;
-        dim3 gm((unsigned)((N + 255) / 256), (unsigned)((K + 127) / 128), (unsigned)B);
+        dim3 gm((unsigned)((N + 255) / 256), (unsigned)((K + 31) / 32), (unsigned)B);
         col_absmax<<<gm, 256, 0, st>>>(y, cmax, K, N);
-        dim3 grid((unsigned)((N + 31) / 32), (unsigned)(l.kp / 32), (unsigned)B);
+        dim3 grid((unsigned)((N + 63) / 64), (unsigned)((l.kp + 63) / 64), (unsigned)B);
         split_cols_t_f16<<<grid, 256, 0, st>>>(y, cmax, (__half*)yhi, (__half*)ylo, cexp, K, N, l.kp);
     } else {
         dim3 grid((unsigned)((N + 31) / 32), (unsigned)(l.kp / 32), (unsigned)B);
@@ -1064,7 +1149,7 @@ static int launch_tc(float* r, const float* x, const float* y, int64_t B, int64_
     }
     CUtensorMap mxh, mxl, myh, myl;
     const bool h = f16 != 0;
-    const bool pair = h && use_pairs();
+    const bool pair = pair_for(M, h);
     const int yrows = pair ? kBN / 2 : kBN;
     if (!make_map(&mxh, xhi, B * M, l.kp, BM, h) || !make_map(&mxl, xlo, B * M, l.kp, BM, h) ||
         !make_map(&myh, yhi, B * N, l.kp, yrows, h) || !make_map(&myl, ylo, B * N, l.kp, yrows, h))
@@ -1073,7 +1158,9 @@ static int launch_tc(float* r, const float* x, const float* y, int64_t B, int64_
     epi.row_exp = rexp;
     epi.col_exp = cexp;
     const bool fused = ep && (ep->bias || ep->act || (ep->out_hi && !f16));
-    if (fused) {
+    const int kparts = B == 1 ? l.kparts : 1;
+    float* part = kparts > 1 ? (float*)(base + l.parts) : nullptr;
+    if (fused && kparts == 1) {
         if (!f16 && ep->out_hi && (N % 32 != 0 || ep->kp_out != round_up(N, KPAD))) return (int)cudaErrorInvalidValue;
         epi.bias = ep->bias;
         epi.out_hi = f16 ? nullptr : ep->out_hi;
@@ -1083,13 +1170,32 @@ static int launch_tc(float* r, const float* x, const float* y, int64_t B, int64_
         CUtensorMap mb;
         memset(&mb, 0, sizeof(mb));
         epi.bias_map = ep->bias && make_bias_map(&mb, ep->bias, M, N);
-        if (pair) return launch_gemm<true, true, true>(mxh, mxl, myh, myl, mb, r, M, N, l.kp, status, epi, B, st);
-        return f16 ? launch_gemm<true, true, false>(mxh, mxl, myh, myl, mb, r, M, N, l.kp, status, epi, B, st)
-                   : launch_gemm<true, false, false>(mxh, mxl, myh, myl, mb, r, M, N, l.kp, status, epi, B, st);
+        if (pair) return launch_gemm<true, true, true>(mxh, mxl, myh, myl, mb, r, M, N, l.kp, status, epi, B, st, 1, nullptr);
+        return f16 ? launch_gemm<true, true, false>(mxh, mxl, myh, myl, mb, r, M, N, l.kp, status, epi, B, st, 1, nullptr)
+                   : launch_gemm<true, false, false>(mxh, mxl, myh, myl, mb, r, M, N, l.kp, status, epi, B, st, 1, nullptr);
     }
-    if (pair) return launch_gemm<false, true, true>(mxh, mxl, myh, myl, mxh, r, M, N, l.kp, status, epi, B, st);
-    return f16 ? launch_gemm<false, true, false>(mxh, mxl, myh, myl, mxh, r, M, N, l.kp, status, epi, B, st)
-               : launch_gemm<false, false, false>(mxh, mxl, myh, myl, mxh, r, M, N, l.kp, status, epi, B, st);
+    Epi plain{};
+    plain.row_exp = rexp;
+    plain.col_exp = cexp;
+    int rc = pair ? launch_gemm<false, true, true>(mxh, mxl, myh, myl, mxh, r, M, N, l.kp, status, plain, B, st, kparts, part)
+         : f16 ? launch_gemm<false, true, false>(mxh, mxl, myh, myl, mxh, r, M, N, l.kp, status, plain, B, st, kparts, part)
+               : launch_gemm<false, false, false>(mxh, mxl, myh, myl, mxh, r, M, N, l.kp, status, plain, B, st, kparts, part);
+    if (rc || kparts == 1) return rc;
+    // a fused layer whose product was split: its epilogue runs after the sum, in the same order
+    Epi fe{};
+    if (fused) {
+        if (!f16 && ep->out_hi && (N % 32 != 0 || ep->kp_out != round_up(N, KPAD))) return (int)cudaErrorInvalidValue;
+        fe.bias = ep->bias;
+        fe.act = ep->act;
+        fe.out_hi = f16 ? nullptr : ep->out_hi;
+        fe.out_lo = f16 ? nullptr : ep->out_lo;
+        fe.kp_out = ep->kp_out;
+    }
+    const int64_t n = M * N;
+    int64_t g = (n + 255) / 256;
+    if (g > 8 * sm_count()) g = 8 * sm_count();
+    sum_parts<<<(unsigned)(g ? g : 1), 256, 0, st>>>(r, part, M, N, kparts, fe);
+    return (int)cudaGetLastError();
 }
 
 extern "C" int mcu_launch_matmul_tc(float* r, const float* x, const float* y, int64_t M, int64_t K, int64_t N,

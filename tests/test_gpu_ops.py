@@ -307,7 +307,8 @@ def _split(dev, split):
 
 @pytest.mark.parametrize("split", SPLITS)
 @pytest.mark.parametrize("mkn", [(128, 32, 256), (300, 100, 700), (1000, 777, 300), (2048, 1024, 4096),
-                                 (256, 4096, 1000), (4096, 4096, 4096)])
+                                 (256, 4096, 1000), (4096, 4096, 4096), (1024, 1024, 1024), (64, 4096, 2048),
+                                 (40, 1024, 4096)])
 def test_matmul_tensor_core_normwise(mkn, split):
     """tcgen05 path (tf32 or scaled f16 split) through the vtable; within 1e-5 of the exact
     product, norm-wise."""
