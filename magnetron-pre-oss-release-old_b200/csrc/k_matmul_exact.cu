@@ -183,12 +183,28 @@ __global__ void __launch_bounds__(kThreads) matmul_skinny_part(float* __restrict
     }
 }
 
+// Sum of the K slices: a CTA owns 32 consecutive outputs; warp w adds slices
+// [w*S/8, (w+1)*S/8) in order (lane = output), and the eight warp sums are added in
+// warp order, so the result does not depend on scheduling.
 __global__ void __launch_bounds__(kThreads) matmul_skinny_sum(float* __restrict__ r, const float* __restrict__ part,
                                                               int64_t MN, int nslices, int64_t N, int64_t r_ld) {
-    for (int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x; i < MN; i += (int64_t)gridDim.x * kThreads) {
-        float s = 0.0f;
-        for (int k = 0; k < nslices; ++k) s += part[(int64_t)k * MN + i];
-        r[(i / N) * r_ld + (i % N)] = s;
+    static_assert(kThreads == 256, "eight warps per CTA");
+    __shared__ float ws[8][32];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int64_t i = (int64_t)blockIdx.x * 32 + lane;
+    const int s0 = (int)((int64_t)nslices * w / 8), s1 = (int)((int64_t)nslices * (w + 1) / 8);
+    float s = 0.0f;
+    if (i < MN) {
+#pragma unroll 8
+        for (int k = s0; k < s1; ++k) s += __ldcs(part + (int64_t)k * MN + i);
+    }
+    ws[w][lane] = s;
+    __syncthreads();
+    if (w == 0 && i < MN) {
+        float t = ws[0][lane];
+#pragma unroll
+        for (int v = 1; v < 8; ++v) t += ws[v][lane];
+        r[(i / N) * r_ld + (i % N)] = t;
     }
 }
 
@@ -248,10 +264,8 @@ extern "C" int mcu_launch_matmul_skinny(float* r, const float* x, const float* y
         case 8: matmul_skinny_part<8><<<grid, kThreads, 0, st>>>(part, x, y, (int)M, K, N, kc); break;
         default: matmul_skinny_part<16><<<grid, kThreads, 0, st>>>(part, x, y, (int)M, K, N, kc); break;
     }
-    int64_t MN = M * N;
-    int64_t g = (MN + kThreads - 1) / kThreads;
-    if (g > 4 * sm_count()) g = 4 * sm_count();
-    matmul_skinny_sum<<<(unsigned)g, kThreads, 0, st>>>(r, part, MN, (int)slices, N, r_ld);
+    const int64_t MN = M * N;
+    matmul_skinny_sum<<<(unsigned)((MN + 31) / 32), kThreads, 0, st>>>(r, part, MN, (int)slices, N, r_ld);
     return (int)cudaGetLastError();
 }
 
