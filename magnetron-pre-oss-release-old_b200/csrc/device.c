@@ -851,8 +851,9 @@ int mag_cuda_softmax_rows_f32(mag_compute_device_t* dvc, float* r, const float* 
     mcu_device* d = dev_of(dvc);
     ext_in(d, x);
     ext_out(d, r, (size_t)(rows * cols * 4));
-    int rc = mcu_launch_softmax_rows(r, x, rows, cols, d->stream);
-    if (!rc) mcu_count_launches(1);
+    const size_t sb = mcu_softmax_rows_scratch_bytes(rows, cols);
+    int rc = mcu_launch_softmax_rows(r, x, rows, cols, sb ? scratch_get(d, sb) : NULL, d->stream);
+    if (!rc) mcu_count_launches(sb ? 2 : 1);
     return rc;
 }
 

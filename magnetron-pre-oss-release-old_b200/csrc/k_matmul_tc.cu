@@ -755,6 +755,53 @@ __global__ void __launch_bounds__(256) split_rows_f16(const float* __restrict__ 
     }
 }
 
+// The same split for rows of up to 128*V elements (V <= 8): one warp per row, the row in
+// registers, eight rows per CTA.
+template <int V>
+__global__ void __launch_bounds__(256) split_rows_f16_warp(const float* __restrict__ x, __half* __restrict__ hi,
+                                                           __half* __restrict__ lo, int* __restrict__ row_exp,
+                                                           int64_t M, int64_t K, int64_t Kp) {
+    const int64_t m = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (m >= M) return;
+    const float* xr = x + m * K;
+    const bool vec = (K % 4 == 0) && ((((uintptr_t)x) & 15) == 0);
+    float4 v[V];
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+        const int64_t k = ((int64_t)i * 32 + lane) * 4;
+        if (vec && k + 4 <= K) {
+            v[i] = __ldcs((const float4*)(xr + k));
+        } else {
+            v[i].x = k < K ? xr[k] : 0.0f;
+            v[i].y = k + 1 < K ? xr[k + 1] : 0.0f;
+            v[i].z = k + 2 < K ? xr[k + 2] : 0.0f;
+            v[i].w = k + 3 < K ? xr[k + 3] : 0.0f;
+        }
+        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const int e = scale_exp(amax);
+    const float scale = __int_as_float((127 + e) << 23);
+    if (lane == 0) row_exp[m] = e;
+    __half* hr = hi + m * Kp;
+    __half* lr = lo + m * Kp;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+        const int64_t k = ((int64_t)i * 32 + lane) * 4;
+        if (k >= Kp) break;
+        __half h[4], l[4];
+        split_f16(v[i].x, scale, h[0], l[0]);
+        split_f16(v[i].y, scale, h[1], l[1]);
+        split_f16(v[i].z, scale, h[2], l[2]);
+        split_f16(v[i].w, scale, h[3], l[3]);
+        *(uint2*)(hr + k) = make_uint2(pack2(h[0], h[1]), pack2(h[2], h[3]));
+        *(uint2*)(lr + k) = make_uint2(pack2(l[0], l[1]), pack2(l[2], l[3]));
+    }
+}
+
 // The same split for rows of up to 1024*V elements: one 256-thread CTA per row keeps the row
 // in registers (V float4 per thread), so X is read from HBM once.
 template <int V>
@@ -1125,7 +1172,11 @@ static int launch_tc(float* r, const float* x, const float* y, int64_t B, int64_
     } else if (f16) {
         __half *h16 = (__half*)xhi, *l16 = (__half*)xlo;
         const unsigned rows = (unsigned)(B * M);
-        if (l.kp <= 1024) split_rows_f16_block<1><<<rows, 256, 0, st>>>(x, h16, l16, rexp, K, l.kp);
+        const unsigned wrows = (rows + 7) / 8;
+        if (l.kp <= 128) split_rows_f16_warp<1><<<wrows, 256, 0, st>>>(x, h16, l16, rexp, B * M, K, l.kp);
+        else if (l.kp <= 256) split_rows_f16_warp<2><<<wrows, 256, 0, st>>>(x, h16, l16, rexp, B * M, K, l.kp);
+        else if (l.kp <= 512) split_rows_f16_warp<4><<<wrows, 256, 0, st>>>(x, h16, l16, rexp, B * M, K, l.kp);
+        else if (l.kp <= 1024) split_rows_f16_warp<8><<<wrows, 256, 0, st>>>(x, h16, l16, rexp, B * M, K, l.kp);
         else if (l.kp <= 2048) split_rows_f16_block<2><<<rows, 256, 0, st>>>(x, h16, l16, rexp, K, l.kp);
         else if (l.kp <= 4096) split_rows_f16_block<4><<<rows, 256, 0, st>>>(x, h16, l16, rexp, K, l.kp);
         else if (l.kp <= 8192) split_rows_f16_block<8><<<rows, 256, 0, st>>>(x, h16, l16, rexp, K, l.kp);

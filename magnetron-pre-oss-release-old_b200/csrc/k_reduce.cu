@@ -372,6 +372,78 @@ __global__ void __launch_bounds__(kSliceThreads, 1024 / kSliceThreads) softmax_r
     cluster.sync();  // peers may still read this CTA's slots
 }
 
+// Rows wider than 16 slices of 8192: two passes over x (12 B per element) instead of a
+// cluster that holds the whole row.  Pass 1 records each slice's max m_s and the double sum
+// of exp(x - m_s); pass 2 combines a row's slices in slice order (row max M, sum
+// S = sum_s S_s * exp(m_s - M) in f64), then writes exp(x - M) / S with the reference's
+// lane/tail exponential.  S differs from the one-pass sum only by the rounding of the
+// rescaled terms (about 1e-7 relative).
+struct SliceStat {
+    float m;
+    float pad;
+    double s;
+};
+constexpr int kStatThreads = 256;
+constexpr int kStatSlice = kStatThreads * 4 * kSliceVec;  // 8192 elements
+
+__global__ void __launch_bounds__(kStatThreads) softmax_slice_stats(SliceStat* __restrict__ st,
+                                                                    const float* __restrict__ x, uint32_t cols,
+                                                                    uint32_t nslices) {
+    __shared__ float sh_max[32];
+    __shared__ double sh_sum[32];
+    const uint64_t row = blockIdx.x / nslices;
+    const uint32_t c0 = (blockIdx.x % nslices) * (uint32_t)kStatSlice;
+    const float* px = x + row * cols;
+    const uint32_t vec_end = cols & ~3u;
+    const bool vec = (cols % 4 == 0) && ((((uintptr_t)px) & 15) == 0);
+    float4 v[kSliceVec];
+#pragma unroll
+    for (int i = 0; i < kSliceVec; ++i) v[i] = load4(px, c0 + (uint32_t)(threadIdx.x + kStatThreads * i) * 4, cols, vec);
+    float m = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < kSliceVec; ++i) m = fmaxf(m, max4(v[i]));
+    m = block_combine(m, WMax(), sh_max, -(float)INFINITY);
+    double s = 0.0;
+    if (m != -INFINITY) {
+#pragma unroll
+        for (int i = 0; i < kSliceVec; ++i)
+            (void)exp4(v[i], m, c0 + (uint32_t)(threadIdx.x + kStatThreads * i) * 4, cols, vec_end, s);
+    }
+    s = block_combine(s, WSum(), sh_sum, 0.0);
+    if (threadIdx.x == 0) st[blockIdx.x] = SliceStat{m, 0.0f, s};
+}
+
+__global__ void __launch_bounds__(kStatThreads) softmax_slice_apply(float* __restrict__ r, const float* __restrict__ x,
+                                                                    const SliceStat* __restrict__ st, uint32_t cols,
+                                                                    uint32_t nslices) {
+    __shared__ float sh_m, sh_inv;
+    const uint64_t row = blockIdx.x / nslices;
+    const uint32_t c0 = (blockIdx.x % nslices) * (uint32_t)kStatSlice;
+    if (threadIdx.x == 0) {
+        const SliceStat* p = st + row * nslices;
+        float gm = -INFINITY;
+        for (uint32_t k = 0; k < nslices; ++k) gm = fmaxf(gm, p[k].m);
+        double gs = 0.0;
+        for (uint32_t k = 0; k < nslices; ++k)
+            if (p[k].m != -INFINITY) gs += p[k].s * exp((double)p[k].m - (double)gm);
+        sh_m = gm;
+        sh_inv = __frcp_rn((float)gs);
+    }
+    __syncthreads();
+    const float gm = sh_m, inv = sh_inv;
+    const float* px = x + row * cols;
+    float* pr = r + row * cols;
+    const uint32_t vec_end = cols & ~3u;
+    const bool vec = (cols % 4 == 0) && ((((uintptr_t)px) | ((uintptr_t)pr)) & 15) == 0;
+    double unused = 0.0;
+#pragma unroll
+    for (int i = 0; i < kSliceVec; ++i) {
+        const uint32_t c = c0 + (uint32_t)(threadIdx.x + kStatThreads * i) * 4;
+        const float4 e = exp4(load4(px, c, cols, vec), gm, c, cols, vec_end, unused);
+        store4(pr, c, cols, vec, div4(e, inv));
+    }
+}
+
 // Rows longer than 16 slices: three passes from HBM.
 constexpr int kSoftmaxThreads = 512;
 __global__ void __launch_bounds__(kSoftmaxThreads) softmax_rows_global(float* __restrict__ r,
@@ -444,9 +516,28 @@ extern "C" int mcu_launch_reduce_rows(int op, float* r, const float* x, int64_t 
     }
 }
 
-extern "C" int mcu_launch_softmax_rows(float* r, const float* x, int64_t rows, int64_t cols, cudaStream_t st) {
+// Rows wider than this go through the two-pass slice kernels (scratch: one SliceStat per slice).
+constexpr int64_t kClusterRowMax = 16 * 8192;
+
+extern "C" size_t mcu_softmax_rows_scratch_bytes(int64_t rows, int64_t cols) {
+    if (cols <= kClusterRowMax) return 0;
+    return (size_t)rows * (size_t)((cols + kStatSlice - 1) / kStatSlice) * sizeof(SliceStat);
+}
+
+extern "C" int mcu_launch_softmax_rows(float* r, const float* x, int64_t rows, int64_t cols, void* scratch,
+                                       cudaStream_t st) {
     if (rows <= 0 || cols <= 0) return (int)cudaSuccess;
     if (cols >= (1ll << 31) || rows >= (1ll << 31)) return (int)cudaErrorInvalidValue;
+    if (cols > kClusterRowMax && scratch) {
+        const int64_t ns = (cols + kStatSlice - 1) / kStatSlice;
+        if (rows * ns < (1ll << 31)) {
+            SliceStat* stats = (SliceStat*)scratch;
+            softmax_slice_stats<<<(unsigned)(rows * ns), kStatThreads, 0, st>>>(stats, x, (uint32_t)cols, (uint32_t)ns);
+            softmax_slice_apply<<<(unsigned)(rows * ns), kStatThreads, 0, st>>>(r, x, stats, (uint32_t)cols,
+                                                                               (uint32_t)ns);
+            return (int)cudaGetLastError();
+        }
+    }
     if (cols <= kWarpRowMax) {
         uint64_t g = ((uint64_t)rows * 32 + 255) / 256;
         const uint64_t cap = (uint64_t)sm_count() * 16;

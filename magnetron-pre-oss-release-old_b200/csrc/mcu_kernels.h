@@ -29,7 +29,10 @@ size_t mcu_reduce_scratch_bytes(void);
 int mcu_launch_reduce(int op, float* r, const float* x, const int64_t* x_dims, const int64_t* x_strides,
                       void* scratch, cudaStream_t st);
 int mcu_launch_reduce_rows(int op, float* r, const float* x, int64_t rows, int64_t cols, cudaStream_t st);
-int mcu_launch_softmax_rows(float* r, const float* x, int64_t rows, int64_t cols, cudaStream_t st);
+/* Normalised row softmax; scratch needs mcu_softmax_rows_scratch_bytes(rows, cols) bytes
+ * (nonzero only for rows wider than 131072, which take two passes over slice statistics). */
+size_t mcu_softmax_rows_scratch_bytes(int64_t rows, int64_t cols);
+int mcu_launch_softmax_rows(float* r, const float* x, int64_t rows, int64_t cols, void* scratch, cudaStream_t st);
 
 /* k_fill.cu: PCG stream fills (normal != 0: Box-Muller pairs; p0, p1 = mean, stddev,
  * else p0, p1 = min, max - min) and constant fills. */
