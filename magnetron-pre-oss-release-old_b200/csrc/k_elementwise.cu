@@ -280,17 +280,14 @@ __global__ void __launch_bounds__(kThreads, 4) binary_rows(float* __restrict__ r
 // them with a carry, keeping x's and y's wrapped indices in step.
 constexpr uint32_t kRowChunk = 16;
 
-template <int OP>
-__global__ void __launch_bounds__(kThreads, 4) binary_rows_chunked(float* __restrict__ r, const float* __restrict__ x,
-                                                                   const float* __restrict__ y, const RowParams p,
-                                                                   uint32_t nrows, uint32_t nchunks) {
-    const int lane_id = threadIdx.x & 31;
-    const uint32_t warp = (uint32_t)(((uint64_t)blockIdx.x * kThreads + threadIdx.x) >> 5);
-    const uint32_t nwarps = (uint32_t)(((uint64_t)gridDim.x * kThreads) >> 5);
-    for (uint32_t ch = warp; ch < nchunks; ch += nwarps) {
-        uint32_t row0 = ch * kRowChunk;
-        uint32_t idx[6], xi[6], yi[6];
-        int64_t ro = 0, xo = 0, yo = 0;
+// One row's offsets, advanced by one row along dim 1 with a carry into dims 2..5; x's and
+// y's wrapped indices move in step.
+struct RowWalk {
+    uint32_t idx[6], xi[6], yi[6];
+    int64_t ro, xo, yo;
+
+    __device__ __forceinline__ void start(uint32_t row0, const RowParams& p) {
+        ro = xo = yo = 0;
         uint32_t q = row0;
 #pragma unroll
         for (int k = 1; k < 6; ++k) {
@@ -303,50 +300,93 @@ __global__ void __launch_bounds__(kThreads, 4) binary_rows_chunked(float* __rest
             xo += (int64_t)xi[k] * p.xs[k];
             yo += (int64_t)yi[k] * p.ys[k];
         }
+    }
+    __device__ __forceinline__ void next(const RowParams& p) {
+#pragma unroll
+        for (int k = 1; k < 6; ++k) {
+            ++idx[k];
+            ro += p.rs[k];
+            if (++xi[k] == p.xdim[k].d) { xi[k] = 0; xo -= (int64_t)(p.xdim[k].d - 1) * p.xs[k]; } else { xo += p.xs[k]; }
+            if (++yi[k] == p.ydim[k].d) { yi[k] = 0; yo -= (int64_t)(p.ydim[k].d - 1) * p.ys[k]; } else { yo += p.ys[k]; }
+            if (idx[k] < p.dim[k].d) break;
+            idx[k] = 0;
+            ro -= (int64_t)p.dim[k].d * p.rs[k];
+            // the wrapped indices of x and y restart at 0 together with idx[k]
+            xo -= (int64_t)xi[k] * p.xs[k];
+            yo -= (int64_t)yi[k] * p.ys[k];
+            xi[k] = 0;
+            yi[k] = 0;
+        }
+    }
+};
+
+// Rows of at most 128 * STEPS columns, vectorised: a warp walks kRowChunk consecutive rows,
+// decomposing the first row's indices once and carrying them to the next rows, with two
+// rows' loads in flight before their stores.
+template <int OP, int STEPS>
+__global__ void __launch_bounds__(kThreads, 2) binary_rows_chunked(float* __restrict__ r, const float* __restrict__ x,
+                                                                   const float* __restrict__ y, const RowParams p,
+                                                                   uint32_t nrows, uint32_t nchunks) {
+    const int lane_id = threadIdx.x & 31;
+    const uint32_t warp = (uint32_t)(((uint64_t)blockIdx.x * kThreads + threadIdx.x) >> 5);
+    const uint32_t nwarps = (uint32_t)(((uint64_t)gridDim.x * kThreads) >> 5);
+    auto load_x = [&](int64_t xo, float4 (&a)[STEPS]) {
+#pragma unroll
+        for (int u = 0; u < STEPS; ++u) {
+            const uint32_t c = 128u * u + 4u * (uint32_t)lane_id;
+            if (c < p.cols) {
+                const uint32_t xc = p.x_mod ? mod_by(c, p.xdim[0]) : c;
+                a[u] = *(const float4*)(x + xo + xc);
+            }
+        }
+    };
+    auto load_y = [&](int64_t yo, float4 (&b)[STEPS]) {
+#pragma unroll
+        for (int u = 0; u < STEPS; ++u) {
+            const uint32_t c = 128u * u + 4u * (uint32_t)lane_id;
+            if (c < p.cols) {
+                if (p.y_mode == 1) {
+                    const float t = y[yo];
+                    b[u] = make_float4(t, t, t, t);
+                } else {
+                    const uint32_t yc = p.y_mode == 0 ? c : mod_by(c, p.ydim[0]);
+                    b[u] = *(const float4*)(y + yo + yc);
+                }
+            }
+        }
+    };
+    auto store_row = [&](int64_t ro, const float4 (&a)[STEPS], const float4 (&b)[STEPS]) {
+#pragma unroll
+        for (int u = 0; u < STEPS; ++u) {
+            const uint32_t c = 128u * u + 4u * (uint32_t)lane_id;
+            if (c < p.cols) {
+                float4 o;
+                o.x = binop<OP>(a[u].x, b[u].x); o.y = binop<OP>(a[u].y, b[u].y);
+                o.z = binop<OP>(a[u].z, b[u].z); o.w = binop<OP>(a[u].w, b[u].w);
+                __stcs((float4*)(r + ro + c), o);
+            }
+        }
+    };
+    for (uint32_t ch = warp; ch < nchunks; ch += nwarps) {
+        const uint32_t row0 = ch * kRowChunk;
+        RowWalk w;
+        w.start(row0, p);
         const uint32_t rows_here = min(kRowChunk, nrows - row0);
-        for (uint32_t rr = 0; rr < rows_here; ++rr) {
-            float4 a[4], b[4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const uint32_t c = 128u * u + 4u * (uint32_t)lane_id;
-                if (u < p.steps && c < p.cols) {
-                    const uint32_t xc = p.x_mod ? mod_by(c, p.xdim[0]) : c;
-                    a[u] = *(const float4*)(x + xo + xc);
-                    if (p.y_mode == 1) {
-                        const float t = y[yo];
-                        b[u] = make_float4(t, t, t, t);
-                    } else {
-                        const uint32_t yc = p.y_mode == 0 ? c : mod_by(c, p.ydim[0]);
-                        b[u] = *(const float4*)(y + yo + yc);
-                    }
-                }
+        for (uint32_t rr = 0; rr < rows_here; rr += 2) {
+            float4 a0[STEPS], b0[STEPS], a1[STEPS], b1[STEPS];
+            const int64_t ro0 = w.ro;
+            load_x(w.xo, a0);
+            load_y(w.yo, b0);
+            w.next(p);
+            const bool two = rr + 1 < rows_here;
+            const int64_t ro1 = w.ro;
+            if (two) {
+                load_x(w.xo, a1);
+                load_y(w.yo, b1);
+                w.next(p);
             }
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const uint32_t c = 128u * u + 4u * (uint32_t)lane_id;
-                if (u < p.steps && c < p.cols) {
-                    float4 o;
-                    o.x = binop<OP>(a[u].x, b[u].x); o.y = binop<OP>(a[u].y, b[u].y);
-                    o.z = binop<OP>(a[u].z, b[u].z); o.w = binop<OP>(a[u].w, b[u].w);
-                    __stcs((float4*)(r + ro + c), o);
-                }
-            }
-            // next row: increment dim 1 with carry into dims 2..5
-#pragma unroll
-            for (int k = 1; k < 6; ++k) {
-                ++idx[k];
-                ro += p.rs[k];
-                if (++xi[k] == p.xdim[k].d) { xi[k] = 0; xo -= (int64_t)(p.xdim[k].d - 1) * p.xs[k]; } else { xo += p.xs[k]; }
-                if (++yi[k] == p.ydim[k].d) { yi[k] = 0; yo -= (int64_t)(p.ydim[k].d - 1) * p.ys[k]; } else { yo += p.ys[k]; }
-                if (idx[k] < p.dim[k].d) break;
-                idx[k] = 0;
-                ro -= (int64_t)p.dim[k].d * p.rs[k];
-                // the wrapped indices of x and y restart at 0 together with idx[k]
-                xo -= (int64_t)xi[k] * p.xs[k];
-                yo -= (int64_t)yi[k] * p.ys[k];
-                xi[k] = 0;
-                yi[k] = 0;
-            }
+            store_row(ro0, a0, b0);
+            if (two) store_row(ro1, a1, b1);
         }
     }
 }
@@ -388,8 +428,13 @@ cudaError_t launch_rows(float* r, const float* x, const float* y, const int64_t*
     }
     if (vec && p.steps <= 4 && dims[0] <= 512 && rows >= 4 * kRowChunk && rows < (1ull << 32)) {
         const uint32_t nchunks = (uint32_t)((rows + kRowChunk - 1) / kRowChunk);
-        binary_rows_chunked<OP><<<grid_for((uint64_t)nchunks * 32, kThreads), kThreads, 0, st>>>(
-            r, x, y, p, (uint32_t)rows, nchunks);
+        const unsigned g = grid_for((uint64_t)nchunks * 32, kThreads);
+        switch (p.steps) {
+            case 1: binary_rows_chunked<OP, 1><<<g, kThreads, 0, st>>>(r, x, y, p, (uint32_t)rows, nchunks); break;
+            case 2: binary_rows_chunked<OP, 2><<<g, kThreads, 0, st>>>(r, x, y, p, (uint32_t)rows, nchunks); break;
+            case 3: binary_rows_chunked<OP, 3><<<g, kThreads, 0, st>>>(r, x, y, p, (uint32_t)rows, nchunks); break;
+            default: binary_rows_chunked<OP, 4><<<g, kThreads, 0, st>>>(r, x, y, p, (uint32_t)rows, nchunks); break;
+        }
         return cudaGetLastError();
     }
     unsigned grid = grid_for(p.nseg * 32, kThreads);
