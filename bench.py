@@ -740,6 +740,88 @@ def run_case(args):
     print(json.dumps({"case": args.case, "size": n, "ms": ms, "rate": work / (ms / 1e3), "unit": unit}))
 
 
+def run_sharded(args):
+    """Element ranges sharded over the ranks (`--case sharded`, launched like the main bench):
+    ADD on each rank's contiguous range of the 2^28-element sweep vectors (kernel-aggregate
+    GB/s, and with the all-gather that collects r on every rank), and the full SUM with
+    one 24-byte record per rank all-gathered and combined in rank order.  Device time with
+    CUDA events on the backend's stream, max over ranks."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    import mag_b200 as MB
+    import dp
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    os.environ["MAG_CUDA_DEVICE"] = str(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    total = args.size or (1 << 28)
+    start, n = dp.shard_rows(total, world, rank)
+    dev = MB.Device()
+    stream = torch.cuda.ExternalStream(dev.stream, device=torch.device("cuda", local))
+    x, y, r = dev.tensor((n,)), dev.tensor((n,)), dev.tensor((n,))
+    dev.fill_random_normal(x, 0.0, 1.0, MB.Pcg(0x5EED0002 + 2 * rank))
+    dev.fill_random_normal(y, 0.0, 1.0, MB.Pcg(0x5EED0003 + 2 * rank))
+    res = dev.tensor((1,))
+    dims, st = MB.i64x6([n, 1, 1, 1, 1, 1]), MB.i64x6(MB.strides6([n, 1, 1, 1, 1, 1]))
+    local_r = torch.as_tensor(_CudaArray(r.data_ptr, n, dev.stream), device=f"cuda:{local}")
+
+    def add():
+        MB.check(dev.L.mag_cuda_binary_f32(dev.p, MB.OP["ADD"], r.data_ptr, x.data_ptr, y.data_ptr, dims, st, st,
+                                           dims, st), "add")
+
+    def add_gather():
+        add()
+        if world > 1:
+            with torch.cuda.stream(stream):
+                dp.gather_rows(local_r, total, 1, world, rank)
+
+    def full_sum():
+        if world > 1:
+            dp.reduce_full(dev, "SUM", x, res.data_ptr, world)
+        else:
+            MB.check(dev.L.mag_cuda_reduce_f32(dev.p, MB.OP["SUM"], res.data_ptr, x.data_ptr, dims, st), "sum")
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+        dev.sync()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            fn()
+        e1.record(stream)
+        dev.sync()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        if world > 1:
+            t = torch.tensor([ms], dtype=torch.float64, device=f"cuda:{local}")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    ms_add, ms_gather, ms_sum = timed(add), timed(add_gather), timed(full_sum)
+    sum_value = float(res.read()[0])
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps({
+            "case": "sharded", "n_gpus": world, "elements": total, "steps": args.steps, "warmup": args.warmup,
+            "add_ms": ms_add, "add_GBps": 12.0 * total / (ms_add / 1e3) / 1e9,
+            "add_with_gather_ms": ms_gather, "add_with_gather_GBps": 12.0 * total / (ms_gather / 1e3) / 1e9,
+            "sum_ms": ms_sum, "sum_GBps": 4.0 * total / (ms_sum / 1e3) / 1e9, "sum": sum_value,
+            "note": "ADD 12 B/element, SUM 4 B/element over all ranks; the gather moves (N-1)/N of r to every rank"}),
+            flush=True)
+
+
 def run_sweep_full(args):
     """Every other BASELINE configuration on one GPU: elementwise/broadcast/unary (config 2),
     row reductions and softmax (config 3), the matmul sweep (config 4), each with its roofline
@@ -941,7 +1023,7 @@ def main():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--case", default=None, choices=["gemm", "layer", "add", "sigmoid", "sum", "softmax", "softmax1k", "skinny", "tile", "bcast2",
-                                                      "fill_uniform", "fill_normal", "fill_const", "storage", "image"],
+                                                      "fill_uniform", "fill_normal", "fill_const", "storage", "image", "sharded"],
                     help="run one kernel family for a profiler instead of the benchmark")
     ap.add_argument("--size", type=int, default=None)
     ap.add_argument("--sweep-full", action="store_true", help="measure every other BASELINE configuration")
@@ -952,7 +1034,7 @@ def main():
         return
     if args.case:
         args.size = args.size or (8192 if args.case in ("gemm", "layer") else 1 << 28)
-        {"storage": run_storage, "image": run_image}.get(args.case, run_case)(args)
+        {"storage": run_storage, "image": run_image, "sharded": run_sharded}.get(args.case, run_case)(args)
         return
     if args.warmup < 3:
         args.warmup = 3

@@ -100,6 +100,21 @@ MAG_CUDA_EXPORT int mag_cuda_binary_f32(mag_compute_device_t* dvc, int op, float
 /* Full reduction (SUM/MEAN/MIN/MAX) of a 6-D tensor into r[0]. */
 MAG_CUDA_EXPORT int mag_cuda_reduce_f32(mag_compute_device_t* dvc, int op, float* r, const float* x,
                                         const int64_t* x_dims, const int64_t* x_strides);
+/* Sharded full reduction (no counterpart in the reference, whose reductions run on one host
+ * thread: mag_blas_{sum,mean,min,max}_f32, magnetron/magnetron_cpu.c:1034-1152).  Each shard
+ * writes one 24-byte record to device memory; the records of all shards (gathered in shard
+ * order, e.g. by an all-gather) combine into r[0]: the double sums added in record order and
+ * rounded to f32 once, MEAN = that sum / total count, MIN/MAX by fminf/fmaxf.  One record
+ * equals mag_cuda_reduce_f32 on the same tensor bit for bit.  Records must be 8-byte aligned. */
+typedef struct mag_cuda_reduce_part {
+    double sum;
+    float min, max;
+    uint64_t count;
+} mag_cuda_reduce_part;
+MAG_CUDA_EXPORT int mag_cuda_reduce_partial_f32(mag_compute_device_t* dvc, mag_cuda_reduce_part* part_device,
+                                                const float* x, const int64_t* x_dims, const int64_t* x_strides);
+MAG_CUDA_EXPORT int mag_cuda_reduce_combine_f32(mag_compute_device_t* dvc, int op, float* r,
+                                                const mag_cuda_reduce_part* parts_device, int nparts);
 /* R[M,N] = X[M,K] Y[K,N], all row-major. */
 MAG_CUDA_EXPORT int mag_cuda_matmul_f32(mag_compute_device_t* dvc, float* r, const float* x, const float* y,
                                         int64_t M, int64_t K, int64_t N);

@@ -769,6 +769,32 @@ int mag_cuda_reduce_f32(mag_compute_device_t* dvc, int op, float* r, const float
     return rc;
 }
 
+_Static_assert(sizeof(mag_cuda_reduce_part) == sizeof(McuReducePart), "reduce record layout");
+
+int mag_cuda_reduce_partial_f32(mag_compute_device_t* dvc, mag_cuda_reduce_part* part, const float* x,
+                                const int64_t* xd, const int64_t* xs) {
+    if (!part || ((uintptr_t)part & 7)) return MAG_CUDA_E_INVALID;
+    mcu_device* d = dev_of(dvc);
+    ext_in(d, x);
+    ext_out(d, part, sizeof(*part));
+    int rc = mcu_launch_reduce_partial((McuReducePart*)part, x, xd, xs, scratch_get(d, mcu_reduce_scratch_bytes()),
+                                       d->stream);
+    if (!rc) mcu_count_launches(2);
+    return rc;
+}
+
+int mag_cuda_reduce_combine_f32(mag_compute_device_t* dvc, int op, float* r, const mag_cuda_reduce_part* parts,
+                                int nparts) {
+    if (op < MAG_ABI_OP_MEAN || op > MAG_ABI_OP_SUM || !parts || nparts < 1 || ((uintptr_t)parts & 7))
+        return MAG_CUDA_E_INVALID;
+    mcu_device* d = dev_of(dvc);
+    ext_in(d, parts);
+    ext_out(d, r, 4);
+    int rc = mcu_launch_reduce_combine(op, r, (const McuReducePart*)parts, nparts, d->stream);
+    if (!rc) mcu_count_launches(1);
+    return rc;
+}
+
 int mag_cuda_matmul_f32(mag_compute_device_t* dvc, float* r, const float* x, const float* y, int64_t M, int64_t K,
                         int64_t N) {
     if (M < 0 || K < 0 || N < 0) return MAG_CUDA_E_INVALID;

@@ -130,9 +130,12 @@ __global__ void __launch_bounds__(kThreads) reduce_pass1(const float* __restrict
     }
 }
 
+// Pass 2: one block folds the block partials.  With `part` set it writes the
+// shard's record (double sum, min, max, element count) instead of a value.
 __global__ void __launch_bounds__(kThreads) reduce_pass2(int op, int nparts, double numel,
                                                          const double* __restrict__ psum, const float* __restrict__ pmin,
-                                                         const float* __restrict__ pmax, float* __restrict__ r) {
+                                                         const float* __restrict__ pmax, float* __restrict__ r,
+                                                         McuReducePart* __restrict__ part) {
     Acc a{0.0, INFINITY, -INFINITY};
     for (int i = threadIdx.x; i < nparts; i += kThreads) {
         a.sum += psum[i];
@@ -145,11 +148,33 @@ __global__ void __launch_bounds__(kThreads) reduce_pass2(int op, int nparts, dou
     float mn = block_combine(a.mn, WMin(), shf, (float)INFINITY);
     float mx = block_combine(a.mx, WMax(), shf, -(float)INFINITY);
     if (threadIdx.x == 0) {
-        if (op == OP_SUM) r[0] = (float)s;
+        if (part) *part = McuReducePart{s, mn, mx, (uint64_t)numel};
+        else if (op == OP_SUM) r[0] = (float)s;
         else if (op == OP_MEAN) r[0] = (float)(s / numel);
         else if (op == OP_MIN) r[0] = mn;
         else r[0] = mx;
     }
+}
+
+// Shard records -> r[0].  The double sums are added one after another in record
+// (rank) order, as the reference adds its row sums (mag_blas_sum_f32,
+// magnetron/magnetron_cpu.c:1034-1060); MEAN divides by the total element count.
+__global__ void reduce_combine(int op, const McuReducePart* __restrict__ parts, int nparts, float* __restrict__ r) {
+    if (threadIdx.x != 0) return;
+    double s = 0.0;
+    float mn = INFINITY, mx = -INFINITY;
+    uint64_t n = 0;
+    for (int i = 0; i < nparts; ++i) {
+        const McuReducePart p = parts[i];
+        s += p.sum;
+        mn = fminf(mn, p.min);
+        mx = fmaxf(mx, p.max);
+        n += p.count;
+    }
+    if (op == OP_SUM) r[0] = (float)s;
+    else if (op == OP_MEAN) r[0] = (float)(s / (double)n);
+    else if (op == OP_MIN) r[0] = mn;
+    else r[0] = mx;
 }
 
 // -------------------------------------------------------- row reductions ---
@@ -474,8 +499,8 @@ extern "C" size_t mcu_reduce_scratch_bytes(void) {
     return (size_t)kMaxPartials * (sizeof(double) + 2 * sizeof(float));
 }
 
-extern "C" int mcu_launch_reduce(int op, float* r, const float* x, const int64_t* xd, const int64_t* xs,
-                                 void* scratch, cudaStream_t st) {
+static int launch_reduce(int op, float* r, McuReducePart* part, const float* x, const int64_t* xd,
+                         const int64_t* xs, void* scratch, cudaStream_t st) {
     uint64_t n = 1;
     for (int k = 0; k < 6; ++k) {
         if (xd[k] <= 0) return (int)cudaErrorInvalidValue;
@@ -499,7 +524,23 @@ extern "C" int mcu_launch_reduce(int op, float* r, const float* x, const int64_t
     for (int k = 0; k < 5; ++k) d[k] = make_fastdiv((uint32_t)(xd[k] < (1ll << 32) ? xd[k] : 1));
     reduce_pass1<<<nparts, kThreads, 0, st>>>(x, n, canonical, d[0], d[1], d[2], d[3], d[4], xs[1], xs[2], xs[3],
                                               xs[4], xs[5], psum, pmin, pmax);
-    reduce_pass2<<<1, kThreads, 0, st>>>(op, nparts, (double)n, psum, pmin, pmax, r);
+    reduce_pass2<<<1, kThreads, 0, st>>>(op, nparts, (double)n, psum, pmin, pmax, r, part);
+    return (int)cudaGetLastError();
+}
+
+extern "C" int mcu_launch_reduce(int op, float* r, const float* x, const int64_t* xd, const int64_t* xs,
+                                 void* scratch, cudaStream_t st) {
+    return launch_reduce(op, r, nullptr, x, xd, xs, scratch, st);
+}
+
+extern "C" int mcu_launch_reduce_partial(McuReducePart* part, const float* x, const int64_t* xd, const int64_t* xs,
+                                         void* scratch, cudaStream_t st) {
+    return launch_reduce(OP_SUM, nullptr, part, x, xd, xs, scratch, st);
+}
+
+extern "C" int mcu_launch_reduce_combine(int op, float* r, const McuReducePart* parts, int nparts, cudaStream_t st) {
+    if (nparts < 1) return (int)cudaErrorInvalidValue;
+    reduce_combine<<<1, 32, 0, st>>>(op, parts, nparts, r);
     return (int)cudaGetLastError();
 }
 

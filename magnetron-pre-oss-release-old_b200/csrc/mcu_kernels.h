@@ -28,6 +28,15 @@ int mcu_launch_bcast2(int op, float* r, const float* x, const float* y, const in
 size_t mcu_reduce_scratch_bytes(void);
 int mcu_launch_reduce(int op, float* r, const float* x, const int64_t* x_dims, const int64_t* x_strides,
                       void* scratch, cudaStream_t st);
+/* One shard's full-reduction record (a sharded SUM/MEAN/MIN/MAX exchanges these). */
+typedef struct McuReducePart {
+    double sum;
+    float min, max;
+    uint64_t count;
+} McuReducePart;
+int mcu_launch_reduce_partial(McuReducePart* part, const float* x, const int64_t* x_dims, const int64_t* x_strides,
+                              void* scratch, cudaStream_t st);
+int mcu_launch_reduce_combine(int op, float* r, const McuReducePart* parts, int nparts, cudaStream_t st);
 int mcu_launch_reduce_rows(int op, float* r, const float* x, int64_t rows, int64_t cols, cudaStream_t st);
 /* Normalised row softmax; scratch needs mcu_softmax_rows_scratch_bytes(rows, cols) bytes
  * (nonzero only for rows wider than 131072, which take two passes over slice statistics). */

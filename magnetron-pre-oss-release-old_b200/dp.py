@@ -38,3 +38,33 @@ def gather_rows(local, total_rows: int, row_width: int, world: int, rank: int):
         _, n = shard_rows(total_rows, world, r)
         parts.append(out[r * cap * row_width: r * cap * row_width + n * row_width])
     return torch.cat(parts)
+
+
+def gather_records(local, world: int):
+    """All-gather one fixed-size record per rank (a 1-D tensor, same length on every
+    rank) into world records in rank order."""
+    import torch
+    import torch.distributed as dist
+
+    out = torch.empty(world * local.numel(), dtype=local.dtype, device=local.device)
+    dist.all_gather_into_tensor(out, local)
+    return out
+
+
+def reduce_full(dev, name: str, shard, r_ptr: int, world: int):
+    """Full SUM/MEAN/MIN/MAX of a tensor whose elements are split over the ranks
+    (`shard` is this rank's part, a backend tensor): one record per rank (double
+    sum, min, max, count), an all-gather of the world records in rank order on
+    the backend's stream, and a fixed-order combine into r[0] on every rank.
+    The exchange is 24 bytes per rank."""
+    import torch
+
+    device = torch.device("cuda", dev.ordinal)
+    stream = torch.cuda.ExternalStream(dev.stream, device=device)
+    with torch.cuda.stream(stream):
+        mine = torch.empty(3, dtype=torch.float64, device=device)  # one 24-byte record, 8-byte aligned
+        dev.reduce_partial(shard, mine.data_ptr())
+        parts = gather_records(mine, world)
+        dev.reduce_combine(name, r_ptr, parts.data_ptr(), world)
+        mine.record_stream(stream)
+        parts.record_stream(stream)

@@ -121,6 +121,8 @@ def load_library(path: str = LIB_PATH):
         "mag_cuda_matmul_f32": ([vp, vp, vp, vp, i64, i64, i64], C.c_int),
         "mag_cuda_broadcast2_f32": ([vp, C.c_int, vp, vp, vp, i64p, i64p, i64p], C.c_int),
         "mag_cuda_reduce_rows_f32": ([vp, C.c_int, vp, vp, i64, i64], C.c_int),
+        "mag_cuda_reduce_partial_f32": ([vp, vp, vp, i64p, i64p], C.c_int),
+        "mag_cuda_reduce_combine_f32": ([vp, C.c_int, vp, vp, C.c_int], C.c_int),
         "mag_cuda_softmax_rows_f32": ([vp, vp, vp, i64, i64], C.c_int),
         "mag_cuda_matmul_batched_f32": ([vp, vp, vp, vp, i64, i64, i64, i64], C.c_int),
         "mag_cuda_profile_start": ([vp], C.c_int),
@@ -156,6 +158,14 @@ def load_library(path: str = LIB_PATH):
         fn.restype = res
     _lib = L
     return L
+
+
+class ReducePart(C.Structure):
+    """mag_cuda_reduce_part: one shard's full-reduction record (24 bytes)."""
+    _fields_ = [("sum", C.c_double), ("min", C.c_float), ("max", C.c_float), ("count", C.c_uint64)]
+
+
+REDUCE_PART_BYTES = C.sizeof(ReducePart)
 
 
 class StoEntry(C.Structure):
@@ -340,6 +350,10 @@ class Device:
     def stream(self) -> int:
         return int(self.L.mag_cuda_stream(self.p) or 0)
 
+    @property
+    def ordinal(self) -> int:
+        return int(self.L.mag_cuda_device_ordinal(self.p))
+
     def sync(self):
         check(self.L.mag_cuda_synchronize(self.p), "synchronize")
 
@@ -386,6 +400,17 @@ class Device:
 
     def exec(self, r: Tensor):
         self.dev.eager_exec_fwd(self.p, r.ptr)
+
+    # ---- sharded full reductions (one record per shard, combined in shard order)
+    def reduce_partial(self, x: Tensor, part_ptr: int):
+        """Writes x's record (double sum, min, max, count) to device memory at part_ptr."""
+        d = (C.c_int64 * 6)(*[int(v) for v in x.t.shape])
+        s = (C.c_int64 * 6)(*[int(v) for v in x.t.strides])
+        check(self.L.mag_cuda_reduce_partial_f32(self.p, part_ptr, x.data_ptr, d, s), "reduce_partial")
+
+    def reduce_combine(self, name: str, r_ptr: int, parts_ptr: int, nparts: int):
+        """r[0] = SUM/MEAN/MIN/MAX over nparts records at parts_ptr, in record order."""
+        check(self.L.mag_cuda_reduce_combine_f32(self.p, OP[name], r_ptr, parts_ptr, nparts), "reduce_combine")
 
     # ---- .magnetron storage (mag_tensor_save / mag_tensor_load, magnetron/magnetron.c:2931-2977)
     def save(self, path: str, tensors):

@@ -40,6 +40,31 @@ WORKER = textwrap.dedent("""
     z = o.softmax_rows(o.matmul(h, w2, n, d_hid, d_out), n, d_out)
     if mode == "fail" and rank == 1:
         raise SystemExit(3)
+    if mode == "records":
+        # a sharded full SUM/MIN/MAX: one (double sum, min, max, count) record per
+        # rank, all-gathered in rank order, combined in that order
+        n = 1001
+        v = o.stream(0x5EED0D01).uniform(n, -1, 1)
+        start, cnt = dp.shard_rows(n, world, rank)
+        part = v[start:start + cnt]
+        rec = np.zeros(3, np.float64)
+        rec[0] = sum(float(e) for e in part)
+        rec[1:2].view(np.float32)[:] = [part.min(), part.max()]
+        rec[2:3].view(np.uint64)[0] = cnt
+        recs = dp.gather_records(torch.from_numpy(rec), world).numpy().reshape(world, 3)
+        total = 0.0
+        for r in range(world):
+            s_, c_ = dp.shard_rows(n, world, r)
+            assert recs[r, 2].view(np.uint64) == c_, "records out of rank order"
+            total += recs[r, 0]
+        mn = recs[:, 1].copy().view(np.float32).reshape(world, 2)[:, 0].min()
+        mx = recs[:, 1].copy().view(np.float32).reshape(world, 2)[:, 1].max()
+        s6 = pad6((n,))
+        assert abs(np.float32(total) - o.reduce("SUM", v, s6)) <= 1e-6
+        assert mn == o.reduce("MIN", v, s6) and mx == o.reduce("MAX", v, s6)
+        print("OK", flush=True)
+        dist.destroy_process_group()
+        raise SystemExit(0)
     try:
         full = dp.gather_rows(torch.from_numpy(z), rows, d_out, world, rank).numpy()
     except Exception as e:
@@ -97,3 +122,9 @@ def test_failed_rank_ends_the_collective_with_an_error():
     outs = _run("fail")
     assert outs[1][0] == 3
     assert outs[0][0] != 0  # rank 0 sees the peer gone (error or timeout), it does not hang
+
+
+def test_two_gloo_ranks_exchange_reduction_records_in_rank_order():
+    outs = _run("records")
+    for rc, out, err in outs:
+        assert rc == 0 and "OK" in out, err[-2000:]
