@@ -367,13 +367,15 @@ def _build_mlp(dev, rows, dims, inplace_gelu=True):
 
 
 @pytest.mark.parametrize("split", SPLITS)
-@pytest.mark.parametrize("inplace", [True, False])
-def test_fused_graph_matches_unfused_bitwise(inplace, split):
-    """Dense layers fused into the GEMM epilogue give the same bits as the op-by-op graph."""
+@pytest.mark.parametrize("inplace,rows,dims", [(True, 256, [512, 384, 256, 96]), (False, 256, [512, 384, 256, 96]),
+                                               (True, 4096, [512, 1024, 512, 96])])
+def test_fused_graph_matches_unfused_bitwise(inplace, rows, dims, split):
+    """Dense layers fused into the GEMM epilogue give the same bits as the op-by-op graph,
+    including the next product's operand split written by the epilogue (256 rows: split-K
+    products, the split runs after the part sum; 4096 rows: one part, the epilogue writes it)."""
     dev = device()
     _split(dev, split)
     o = oracle()
-    rows, dims = 256, [512, 384, 256, 96]
     X, Ws, Bs, root = _build_mlp(dev, rows, dims, inplace)
     s = o.stream(9100)
     X.write(s.uniform(rows * dims[0], -1, 1))
@@ -382,10 +384,14 @@ def test_fused_graph_matches_unfused_bitwise(inplace, split):
         B.write(s.uniform(rows * b, -0.1, 0.1))
     MB.check(dev.L.mag_cuda_set_matmul_mode(dev.p, 2), "tc")
     try:
+        n0 = dev.launches()
         dev.graph_exec(root)
         plain = root.read()
+        n1 = dev.launches()
         dev.graph_exec(root, fused=True)
         fused = root.read()
+        n2 = dev.launches()
+        assert n2 - n1 < n1 - n0  # fused: no separate ADD/GELU kernels
         x2 = s.uniform(rows * dims[0], -1, 1)  # replay with new input data
         X.write(x2)
         dev.graph_exec(root, fused=True)
@@ -420,6 +426,32 @@ def test_matmul_batched_tensor_core(split):
     for i in range(b):
         assert _normwise_ok(got[i * m * n:(i + 1) * m * n], x[i * m * k:(i + 1) * m * k],
                             y[i * k * n:(i + 1) * k * n], m, k, n), i
+
+
+def test_matmul_f16_magnitudes_differ_within_rows():
+    """Rows whose 256-element stretches lie up to 2^80 apart, a stretch 2^-130 below the rest
+    of its row, a zero stretch and a ragged K: the f16 split stays within 1e-5 of |X||Y|."""
+    dev = device()
+    _split(dev, MB.TC_SPLIT_F16)
+    o = oracle()
+    m, k, n = 512, 1000, 384
+    s = o.stream(7700)
+    x = s.uniform(m * k, -1.0, 1.0).reshape(m, k).astype(np.float64)
+    y = s.uniform(k * n, -1.0, 1.0).reshape(k, n)
+    g = np.arange(k) // 256
+    x *= 2.0 ** (((np.arange(m)[:, None] * 3 + g[None, :] * 20) % 81) - 40)
+    x[7, 256:512] = 0
+    x[9, :] *= 2.0 ** 60
+    x[9, 512:768] *= 2.0 ** -130
+    x, y = x.astype(np.float32).reshape(-1), y.astype(np.float32).reshape(-1)
+    MB.check(dev.L.mag_cuda_set_matmul_mode(dev.p, 2), "tc mode")
+    try:
+        got, _, _ = run_op(dev, "MATMUL", [x, y], [(m, k), (k, n)])
+    finally:
+        dev.L.mag_cuda_set_matmul_mode(dev.p, 0)
+    assert dev.L.mag_cuda_synchronize(dev.p) == 0
+    assert np.all(np.isfinite(got))
+    assert _normwise_ok(got, x, y, m, k, n)
 
 
 def test_matmul_f16_split_scaling_extremes():
