@@ -708,6 +708,9 @@ def run_case(args):
         elif args.case == "sum":
             fn = lambda: dev.L.mag_cuda_reduce_f32(dev.p, MB.OP["SUM"], r.data_ptr, x.data_ptr, dims, st)
             work = 4.0 * n / 1e9
+        elif args.case == "softmax256k":
+            fn = lambda: dev.L.mag_cuda_softmax_rows_f32(dev.p, r.data_ptr, x.data_ptr, n // 262144, 262144)
+            work = 8.0 * n / 1e9
         elif args.case == "softmax1k":
             fn = lambda: dev.L.mag_cuda_softmax_rows_f32(dev.p, r.data_ptr, x.data_ptr, n // 1024, 1024)
             work = 8.0 * n / 1e9
@@ -1022,7 +1025,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--case", default=None, choices=["gemm", "layer", "add", "sigmoid", "sum", "softmax", "softmax1k", "skinny", "tile", "bcast2",
+    ap.add_argument("--case", default=None, choices=["gemm", "layer", "add", "sigmoid", "sum", "softmax", "softmax1k", "softmax256k", "skinny", "tile", "bcast2",
                                                       "fill_uniform", "fill_normal", "fill_const", "storage", "image", "sharded"],
                     help="run one kernel family for a profiler instead of the benchmark")
     ap.add_argument("--size", type=int, default=None)

@@ -879,7 +879,7 @@ int mag_cuda_softmax_rows_f32(mag_compute_device_t* dvc, float* r, const float* 
     ext_out(d, r, (size_t)(rows * cols * 4));
     const size_t sb = mcu_softmax_rows_scratch_bytes(rows, cols);
     int rc = mcu_launch_softmax_rows(r, x, rows, cols, sb ? scratch_get(d, sb) : NULL, d->stream);
-    if (!rc) mcu_count_launches(sb ? 2 : 1);
+    if (!rc) mcu_count_launches(mcu_softmax_rows_kernels(rows, cols));
     return rc;
 }
 

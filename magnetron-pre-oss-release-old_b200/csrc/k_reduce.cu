@@ -280,6 +280,12 @@ __device__ __forceinline__ float4 neg_inf4() { return make_float4(-INFINITY, -IN
 __device__ __forceinline__ float max4(float4 v) { return fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)); }
 
 // e = exp(v - m) per component (reference lane/tail split by column), zero past the row end.
+// The row sum is kept in double; the four values (each in [0, 1]) are first added pairwise in
+// f32, which adds at most 2^-23 relative to the sum (about 1e-7) and saves three of every four
+// f32->f64 conversions and double adds, which otherwise bound the kernel's throughput.
+__device__ __forceinline__ double sum4(float4 e) {
+    return (double)__fadd_rn(__fadd_rn(e.x, e.y), __fadd_rn(e.z, e.w));
+}
 __device__ __forceinline__ float4 exp4(float4 v, float m, uint32_t c, uint32_t cols, uint32_t vec_end, double& s) {
     float4 e;
     if (c + 3 < vec_end) {  // all four are vector lanes
@@ -287,14 +293,14 @@ __device__ __forceinline__ float4 exp4(float4 v, float m, uint32_t c, uint32_t c
         e.y = sse_expf(fs(v.y, m));
         e.z = sse_expf(fs(v.z, m));
         e.w = sse_expf(fs(v.w, m));
-        s += (double)e.x + (double)e.y + (double)e.z + (double)e.w;
+        s += sum4(e);
         return e;
     }
     e.x = c < cols ? softmax_exp(fs(v.x, m), c, vec_end) : 0.0f;
     e.y = c + 1 < cols ? softmax_exp(fs(v.y, m), c + 1, vec_end) : 0.0f;
     e.z = c + 2 < cols ? softmax_exp(fs(v.z, m), c + 2, vec_end) : 0.0f;
     e.w = c + 3 < cols ? softmax_exp(fs(v.w, m), c + 3, vec_end) : 0.0f;
-    s += (double)e.x + (double)e.y + (double)e.z + (double)e.w;
+    s += sum4(e);
     return e;
 }
 
@@ -397,12 +403,13 @@ __global__ void __launch_bounds__(kSliceThreads, 1024 / kSliceThreads) softmax_r
     cluster.sync();  // peers may still read this CTA's slots
 }
 
-// Rows wider than 16 slices of 8192: two passes over x (12 B per element) instead of a
-// cluster that holds the whole row.  Pass 1 records each slice's max m_s and the double sum
-// of exp(x - m_s); pass 2 combines a row's slices in slice order (row max M, sum
-// S = sum_s S_s * exp(m_s - M) in f64), then writes exp(x - M) / S with the reference's
-// lane/tail exponential.  S differs from the one-pass sum only by the rounding of the
-// rescaled terms (about 1e-7 relative).
+// Rows wider than one CTA slice: two passes over x instead of a cluster that holds the whole
+// row.  Pass 1 records each slice's max m_s and the double sum of exp(x - m_s); pass 2
+// combines a row's slices in slice order (row max M, sum S = sum_s S_s * exp(m_s - M) in
+// f64), then writes exp(x - M) / S with the reference's lane/tail exponential.  S differs
+// from the one-pass sum only by the rounding of the rescaled terms (about 1e-7 relative).
+// The row combine runs once per row in its own small kernel between the passes (HBM sees
+// 12 B per element; running the passes over L2-sized chunks of rows measured slower).
 struct SliceStat {
     float m;
     float pad;
@@ -423,7 +430,8 @@ __global__ void __launch_bounds__(kStatThreads) softmax_slice_stats(SliceStat* _
     const bool vec = (cols % 4 == 0) && ((((uintptr_t)px) & 15) == 0);
     float4 v[kSliceVec];
 #pragma unroll
-    for (int i = 0; i < kSliceVec; ++i) v[i] = load4(px, c0 + (uint32_t)(threadIdx.x + kStatThreads * i) * 4, cols, vec);
+    for (int i = 0; i < kSliceVec; ++i)
+        v[i] = load4(px, c0 + (uint32_t)(threadIdx.x + kStatThreads * i) * 4, cols, vec);
     float m = -INFINITY;
 #pragma unroll
     for (int i = 0; i < kSliceVec; ++i) m = fmaxf(m, max4(v[i]));
@@ -438,24 +446,28 @@ __global__ void __launch_bounds__(kStatThreads) softmax_slice_stats(SliceStat* _
     if (threadIdx.x == 0) st[blockIdx.x] = SliceStat{m, 0.0f, s};
 }
 
+// One thread per row: the row's max and the reciprocal of its sum from the slice statistics,
+// in slice order, into the row's first SliceStat (m, and inv in `pad`).
+__global__ void __launch_bounds__(256) softmax_slice_combine(SliceStat* __restrict__ st, uint64_t rows,
+                                                              uint32_t nslices) {
+    const uint64_t row = (uint64_t)blockIdx.x * 256 + threadIdx.x;
+    if (row >= rows) return;
+    SliceStat* p = st + row * nslices;
+    float gm = -INFINITY;
+    for (uint32_t k = 0; k < nslices; ++k) gm = fmaxf(gm, p[k].m);
+    double gs = 0.0;
+    for (uint32_t k = 0; k < nslices; ++k)
+        if (p[k].m != -INFINITY) gs += p[k].s * exp((double)p[k].m - (double)gm);
+    p[0].m = gm;
+    p[0].pad = __frcp_rn((float)gs);
+}
+
 __global__ void __launch_bounds__(kStatThreads) softmax_slice_apply(float* __restrict__ r, const float* __restrict__ x,
                                                                     const SliceStat* __restrict__ st, uint32_t cols,
                                                                     uint32_t nslices) {
-    __shared__ float sh_m, sh_inv;
     const uint64_t row = blockIdx.x / nslices;
     const uint32_t c0 = (blockIdx.x % nslices) * (uint32_t)kStatSlice;
-    if (threadIdx.x == 0) {
-        const SliceStat* p = st + row * nslices;
-        float gm = -INFINITY;
-        for (uint32_t k = 0; k < nslices; ++k) gm = fmaxf(gm, p[k].m);
-        double gs = 0.0;
-        for (uint32_t k = 0; k < nslices; ++k)
-            if (p[k].m != -INFINITY) gs += p[k].s * exp((double)p[k].m - (double)gm);
-        sh_m = gm;
-        sh_inv = __frcp_rn((float)gs);
-    }
-    __syncthreads();
-    const float gm = sh_m, inv = sh_inv;
+    const float gm = st[row * nslices].m, inv = st[row * nslices].pad;
     const float* px = x + row * cols;
     float* pr = r + row * cols;
     const uint32_t vec_end = cols & ~3u;
@@ -565,19 +577,24 @@ extern "C" size_t mcu_softmax_rows_scratch_bytes(int64_t rows, int64_t cols) {
     return (size_t)rows * (size_t)((cols + kStatSlice - 1) / kStatSlice) * sizeof(SliceStat);
 }
 
+extern "C" int mcu_softmax_rows_kernels(int64_t rows, int64_t cols) {
+    if (rows <= 0 || cols <= 0) return 0;
+    return cols <= kClusterRowMax ? 1 : 3;
+}
+
 extern "C" int mcu_launch_softmax_rows(float* r, const float* x, int64_t rows, int64_t cols, void* scratch,
                                        cudaStream_t st) {
     if (rows <= 0 || cols <= 0) return (int)cudaSuccess;
     if (cols >= (1ll << 31) || rows >= (1ll << 31)) return (int)cudaErrorInvalidValue;
-    if (cols > kClusterRowMax && scratch) {
+    if (cols > kClusterRowMax) {
         const int64_t ns = (cols + kStatSlice - 1) / kStatSlice;
-        if (rows * ns < (1ll << 31)) {
-            SliceStat* stats = (SliceStat*)scratch;
-            softmax_slice_stats<<<(unsigned)(rows * ns), kStatThreads, 0, st>>>(stats, x, (uint32_t)cols, (uint32_t)ns);
-            softmax_slice_apply<<<(unsigned)(rows * ns), kStatThreads, 0, st>>>(r, x, stats, (uint32_t)cols,
-                                                                               (uint32_t)ns);
-            return (int)cudaGetLastError();
-        }
+        if (!scratch || rows * ns >= (1ll << 31)) return (int)cudaErrorInvalidValue;
+        SliceStat* stats = (SliceStat*)scratch;
+        const unsigned blocks = (unsigned)(rows * ns);
+        softmax_slice_stats<<<blocks, kStatThreads, 0, st>>>(stats, x, (uint32_t)cols, (uint32_t)ns);
+        softmax_slice_combine<<<(unsigned)((rows + 255) / 256), 256, 0, st>>>(stats, (uint64_t)rows, (uint32_t)ns);
+        softmax_slice_apply<<<blocks, kStatThreads, 0, st>>>(r, x, stats, (uint32_t)cols, (uint32_t)ns);
+        return (int)cudaGetLastError();
     }
     if (cols <= kWarpRowMax) {
         uint64_t g = ((uint64_t)rows * 32 + 255) / 256;
