@@ -230,7 +230,8 @@ def test_softmax_rows():
         got = _raw(dev, tr.data_ptr, rows * cols)
         want = o.softmax_rows(x, rows, cols)
         rel = np.abs(got - want) / np.maximum(np.abs(want), 1e-30)
-        assert rel.max() <= 1e-5, (rows, cols, rel.max())
+        # parity bar 1e-5; CUDA's expf against the reference's exp lanes measures <= 3.7e-7
+        assert rel.max() <= 1e-6, (rows, cols, rel.max())
 
 
 def test_broadcast2_small_exact():
