@@ -342,39 +342,55 @@ def run_ours(args):
     X.write(xh.numpy())
     dev.sync()
 
-    def step(zz=z, pp=P):
-        dev.graph_exec(zz, fused=True)
-        MB.check(dev.L.mag_cuda_softmax_rows_f32(dev.p, pp.data_ptr, zz.data_ptr, rows, D_OUT), "softmax")
-        if world > 1:
-            with torch.cuda.stream(stream):
-                src = torch.as_tensor(_CudaArray(pp.data_ptr, rows * D_OUT, dev.stream), device=f"cuda:{local}")
-                gathered["out"] = dp.gather_rows(src, GLOBAL_BATCH, D_OUT, world, rank)
-
-    # ---- end to end: two input buffers and two forward graphs, so step i+1's input upload
-    # (pinned host -> HBM on the backend's copy stream) and step i's output download overlap
-    # step i's kernels; every step's copies stay inside the timed region
+    # ---- two input buffers and two forward graphs (z, P) / (z2, P2), used alternately: step i's
+    # logits all-gather (N > 1) runs on its own stream and overlaps step i+1's kernels, and in the
+    # end-to-end run step i+1's input upload and step i's output download overlap step i
     X2 = dev.tensor((rows, D_IN))
+    X2.write(xh.numpy())
     z2 = forward(X2)
     P2 = dev.tensor((rows * D_OUT,))
     bufs = [(X, z, P), (X2, z2, P2)]
+    gstream = torch.cuda.Stream(device=f"cuda:{local}")
+    gdone = [None, None]  # per buffer: the event after its last all-gather
+
+    def step(i):
+        _, zc, pc = bufs[i % 2]
+        if gdone[i % 2] is not None:
+            stream.wait_event(gdone[i % 2])  # that buffer's previous gather has read it
+        dev.graph_exec(zc, fused=True)
+        MB.check(dev.L.mag_cuda_softmax_rows_f32(dev.p, pc.data_ptr, zc.data_ptr, rows, D_OUT), "softmax")
+        if world > 1:
+            ready = torch.cuda.Event()
+            ready.record(stream)
+            gstream.wait_event(ready)
+            with torch.cuda.stream(gstream):
+                src = torch.as_tensor(_CudaArray(pc.data_ptr, rows * D_OUT, dev.stream), device=f"cuda:{local}")
+                gathered[i % 2] = dp.gather_rows(src, GLOBAL_BATCH, D_OUT, world, rank)
+                ev = torch.cuda.Event()
+                ev.record(gstream)
+                gdone[i % 2] = ev
+
+    def join():  # the backend's stream waits for every gather issued so far
+        stream.wait_stream(gstream)
+
     out_h = [torch.empty(world * rows * D_OUT, dtype=torch.float32).pin_memory() for _ in range(2)]
     out_stream = torch.cuda.Stream(device=f"cuda:{local}")
 
     def e2e_run(steps):
         dev.upload_async(bufs[0][0], xh.data_ptr(), xh.numel() * 4)
         for i in range(steps):
-            xc, zc, pc = bufs[i % 2]
             if i + 1 < steps:
                 dev.upload_async(bufs[(i + 1) % 2][0], xh.data_ptr(), xh.numel() * 4)
-            step(zc, pc)
+            step(i)
             if rank == 0:
                 if world > 1:
-                    out_stream.wait_stream(stream)
+                    out_stream.wait_event(gdone[i % 2])
                     with torch.cuda.stream(out_stream):
-                        out_h[i % 2].copy_(gathered["out"], non_blocking=True)
-                        gathered["out"].record_stream(out_stream)
+                        out_h[i % 2].copy_(gathered[i % 2], non_blocking=True)
+                        gathered[i % 2].record_stream(out_stream)
                 else:
-                    dev.download_async(pc, out_h[i % 2].data_ptr(), rows * D_OUT * 4)
+                    dev.download_async(bufs[i % 2][2], out_h[i % 2].data_ptr(), rows * D_OUT * 4)
+        join()
         dev.copies_sync()
         out_stream.synchronize()
 
@@ -393,8 +409,9 @@ def run_ours(args):
 
     launches0 = dev.launches()
     dev.profile_start()  # graph captured on the first step carries per-op event nodes
-    for _ in range(args.warmup):
-        step()
+    for i in range(args.warmup):
+        step(i)
+    join()
     barrier()
     dev.profile_collect()
     dev.profile_start()  # reset the per-op totals; timing below only
@@ -405,9 +422,10 @@ def run_ours(args):
     launches_before = dev.launches()
     clocks.start()
     ev0.record(stream)
-    for _ in range(args.steps):
-        step()
+    for i in range(args.steps):
+        step(i)
         dev.profile_collect()  # reads this replay's op events (syncs the device stream)
+    join()
     ev1.record(stream)
     barrier()
     clk = clocks.stop()
