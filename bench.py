@@ -73,6 +73,7 @@ class ClockSampler:
     def __init__(self, index: int):
         self.index = index
         self.samples = []
+        self.stamps = []
         self.reasons = set()
         self.max_mhz = None
         self.stop_flag = threading.Event()
@@ -101,6 +102,7 @@ class ClockSampler:
         while not self.stop_flag.is_set():
             try:
                 self.samples.append(float(N.nvmlDeviceGetClockInfo(self.h, N.NVML_CLOCK_SM)))
+                self.stamps.append(time.perf_counter())
                 bits = N.nvmlDeviceGetCurrentClocksEventReasons(self.h)
                 for b, nm in self.names.items():
                     if bits & b:
@@ -109,6 +111,16 @@ class ClockSampler:
                 self.err = str(e)
                 return
             time.sleep(0.005)
+
+    def around(self, t0: float, t1: float):
+        """Median SM clock sampled in [t0, t1], else the sample nearest to that window."""
+        inside = [c for c, t in zip(self.samples, self.stamps) if t0 <= t <= t1]
+        if inside:
+            return statistics.median(inside)
+        if not self.samples:
+            return None
+        mid = 0.5 * (t0 + t1)
+        return min(zip(self.stamps, self.samples), key=lambda p: abs(p[0] - mid))[1]
 
     def stop(self):
         self.stop_flag.set()
@@ -869,21 +881,28 @@ def run_sweep_full(args):
             t.write(src[:m].numpy(), offset_elems=off)
         return t
 
+    clocks = ClockSampler(torch.cuda.current_device())
+    clocks.start()
+    window = [0.0, 0.0]
+
     def timeit(fn, reps):
         MB.check(fn(), "warm")
         dev.sync()
+        window[0] = time.perf_counter()
         e0.record(stream)
         for _ in range(reps):
             MB.check(fn(), "op")
         e1.record(stream)
         dev.sync()
         torch.cuda.synchronize()
+        window[1] = time.perf_counter()
         return e0.elapsed_time(e1) / reps
 
     def rec(group, name, ms, work, unit, peak):
         rate = work / (ms / 1e3)
+        mhz = clocks.around(window[0], window[1])
         rows_out.append({"group": group, "case": name, "ms": round(ms, 4), "rate": round(rate, 1), "unit": unit,
-                         "frac": round(rate / peak, 3) if peak else None})
+                         "frac": round(rate / peak, 3) if peak else None, "sm_mhz": mhz})
         print(json.dumps(rows_out[-1]), flush=True)
 
     def dims_strides(shape):
@@ -1028,9 +1047,10 @@ def run_sweep_full(args):
             for c in cpu:
                 c["rate"] = round(c["rate"], 4)
                 print(json.dumps({"cpu_reference_1thread": c}), flush=True)
+    clk = clocks.stop()
     if args.out:
         with open(args.out, "w") as f:
-            json.dump({"gpu": rows_out, "cpu_reference_1thread": cpu, "peaks": {"hbm_gbs": hbm, "split_tflops": tf, "split": SPLIT_NAME,
+            json.dump({"clocks": clk, "gpu": rows_out, "cpu_reference_1thread": cpu, "peaks": {"hbm_gbs": hbm, "split_tflops": tf, "split": SPLIT_NAME,
                                                                                  "source": pk_src},
                        "device": dev.name}, f, indent=1)
 

@@ -127,7 +127,8 @@ MAG_CUDA_EXPORT int mag_cuda_broadcast2_f32(mag_compute_device_t* dvc, int op, f
 /* Per-row SUM/MEAN/MIN/MAX of a rows x cols row-major matrix into r[rows]. */
 MAG_CUDA_EXPORT int mag_cuda_reduce_rows_f32(mag_compute_device_t* dvc, int op, float* r, const float* x,
                                              int64_t rows, int64_t cols);
-/* Normalised softmax of each row: exp(x - max) / sum. */
+/* Normalised softmax of each row: exp(x - max) / sum, the sum accumulated in double, exp from
+ * CUDA's expf (within 2 ulp; the reference has no row softmax, only the elementwise exp op). */
 MAG_CUDA_EXPORT int mag_cuda_softmax_rows_f32(mag_compute_device_t* dvc, float* r, const float* x, int64_t rows,
                                               int64_t cols);
 /* R[b] = X[b] Y[b] for b < batch, each M x K times K x N (tensor cores for large products,
