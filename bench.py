@@ -70,8 +70,9 @@ class ClockSampler:
     """SM clock and clock-event (throttle) reasons of one GPU, read through NVML
     every 5 ms while the timed region runs (read-only queries)."""
 
-    def __init__(self, index: int):
+    def __init__(self, index: int, interval: float = 0.005):
         self.index = index
+        self.interval = interval
         self.samples = []
         self.stamps = []
         self.reasons = set()
@@ -110,7 +111,7 @@ class ClockSampler:
             except Exception as e:
                 self.err = str(e)
                 return
-            time.sleep(0.005)
+            time.sleep(self.interval)
 
     def around(self, t0: float, t1: float):
         """Median SM clock sampled in [t0, t1], else the sample nearest to that window."""
@@ -881,7 +882,7 @@ def run_sweep_full(args):
             t.write(src[:m].numpy(), offset_elems=off)
         return t
 
-    clocks = ClockSampler(torch.cuda.current_device())
+    clocks = ClockSampler(torch.cuda.current_device(), interval=0.001)
     clocks.start()
     window = [0.0, 0.0]
 
@@ -965,6 +966,18 @@ def run_sweep_full(args):
         rec("reduce", f"full {op} 2^28", ms, 4.0 * n / 1e9, "GB/s", hbm)
     for t in (x, r):
         t.free()
+    # ---- seeded fills on the device (the PCG stream of a reference context, jumped per thread);
+    # before the matmul rows, whose power draw lowers the clocks of the integer-bound fills
+    n = 1 << 28
+    r = dev.tensor((n,))
+    g = MB.Pcg(0x5EED0002)
+    ms = timeit(lambda: dev.L.mag_cuda_fill_uniform_pcg_f32(dev.p, r.data_ptr, n, -1.0, 1.0, ctypes.byref(g.state),
+                                                           g.inc), 5)
+    rec("fill", "uniform PCG 2^28", ms, 4.0 * n / 1e9, "GB/s", hbm)
+    ms = timeit(lambda: dev.L.mag_cuda_fill_normal_pcg_f32(dev.p, r.data_ptr, n, 0.0, 1.0, ctypes.byref(g.state),
+                                                          g.inc), 5)
+    rec("fill", "normal PCG + Box-Muller 2^28", ms, 4.0 * n / 1e9, "GB/s", hbm)
+    r.free()
     # ---- config 4: matmul
     for m in (1024, 4096, 8192, 16384):
         a = filled(m * m, lambda c: c * (m ** -0.25))
@@ -991,17 +1004,6 @@ def run_sweep_full(args):
         2.0 * bt * mm ** 3 / 1e12, "TFLOP/s", tf)
     a.free()
     c_.free()
-    # ---- seeded fills on the device (the PCG stream of a reference context, jumped per thread)
-    n = 1 << 28
-    r = dev.tensor((n,))
-    g = MB.Pcg(0x5EED0002)
-    ms = timeit(lambda: dev.L.mag_cuda_fill_uniform_pcg_f32(dev.p, r.data_ptr, n, -1.0, 1.0, ctypes.byref(g.state),
-                                                           g.inc), 5)
-    rec("fill", "uniform PCG 2^28", ms, 4.0 * n / 1e9, "GB/s", hbm)
-    ms = timeit(lambda: dev.L.mag_cuda_fill_normal_pcg_f32(dev.p, r.data_ptr, n, 0.0, 1.0, ctypes.byref(g.state),
-                                                          g.inc), 5)
-    rec("fill", "normal PCG + Box-Muller 2^28", ms, 4.0 * n / 1e9, "GB/s", hbm)
-    r.free()
     # ---- reference CPU, single thread, on this host
     cpu = []
     if not args.no_cpu_baseline:

@@ -1112,7 +1112,7 @@ int mag_cuda_matmul_batched_f32(mag_compute_device_t* dvc, float* r, const float
         (double)batch * M * N * K >= 1.0e9) {
         void* scratch = scratch_get(d, mcu_matmul_tc_batched_scratch_bytes(batch, M, K, N));
         rc = mcu_launch_matmul_tc_batched(r, x, y, batch, M, K, N, scratch, d->d_status, d->stream, d->tc_f16);
-        if (!rc) mcu_count_launches(d->tc_f16 ? 4 : 3);
+        if (!rc) mcu_count_launches(mcu_matmul_tc_batched_kernels(batch, M, K, N, d->tc_f16));
     } else {
         rc = mcu_launch_matmul_exact(r, x, y, batch, M, K, N, N, 0, d->stream);
         if (!rc) mcu_count_launches(1);
@@ -1343,7 +1343,9 @@ static int exec_planned_matmul(mcu_device* d, mag_tensor_t* m, const mcu_plan_it
     }
     int rc = mcu_launch_matmul_tc_ex(fptr(out), fptr(x), fptr(y), M, K, N, scratch, d->d_status, d->stream, &ep,
                                      d->tc_f16);
-    if (!rc) mcu_count_launches(mcu_matmul_tc_kernels(M, K, N, d->tc_f16, it->a_split >= 0));
+    if (!rc)
+        mcu_count_launches(mcu_matmul_tc_kernels(M, K, N, d->tc_f16,
+                                                 (it->a_split >= 0 ? 1 : 0) | (it->kind == PLAN_FUSED ? 2 : 0)));
     return rc;
 }
 

@@ -303,12 +303,31 @@ __device__ __forceinline__ float gelu_lane(float x) {
     return __fmul_rn(0.5f, __fmul_rn(x, b));
 }
 
+// Work unit u -> tile t, part, and its K stages [kbeg, kend) (see the work-unit comment in gemm_3x).
+__device__ __forceinline__ void decode_unit(int u, int split_from, int kparts, int kpc, int nk, int& t, int& part,
+                                            int& kbeg, int& kend) {
+    if (u < split_from) {
+        t = u;
+        part = 0;
+        kbeg = 0;
+        kend = nk;
+    } else {
+        const int v = u - split_from;
+        const int j = v / kparts;
+        t = split_from + j;
+        part = v - j * kparts;
+        kbeg = part * kpc;
+        kend = min(nk, kbeg + kpc);
+    }
+}
+
 template <int BN, int STAGES, bool FUSED, bool F16, bool PAIR>
 __global__ void __maxnreg__(kLaunchRegs)
     gemm_3x(const __grid_constant__ CUtensorMap map_xhi, const __grid_constant__ CUtensorMap map_xlo,
                 const __grid_constant__ CUtensorMap map_yhi, const __grid_constant__ CUtensorMap map_ylo,
                 const __grid_constant__ CUtensorMap map_bias, float* __restrict__ r, int M, int N, int Kp, int64_t ldr, int* status, const Epi epi,
-                int seg_kb, int batch, int kparts, float* __restrict__ part_out) {
+                int seg_kb, int batch, int kparts, int kpc, int split_from, float* __restrict__ part_out,
+                float* __restrict__ tail_out) {
     using C = Cfg<BN, STAGES, PAIR>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -337,10 +356,12 @@ __global__ void __maxnreg__(kLaunchRegs)
     const int tiles = tiles_per_batch * batch;  // batch b's operands start at rows b*M (X) and b*N (Y)
     constexpr int KE = F16 ? BK16 : BK;          // K elements per ring stage
     const int nk = Kp / KE;
-    // split K (kparts > 1, one batch, no fused epilogue): work unit u is part u % kparts of tile
-    // u / kparts, K stages [part*kpc, part*kpc + kpc), written to part_out[part] for a fixed-order sum
-    const int kpc = (nk + kparts - 1) / kparts;
-    const int work = tiles * kparts;
+    // Work units: tiles [0, split_from) whole, one unit each; tiles [split_from, tiles) cut into
+    // kparts units of kpc K stages (kparts > 1, one batch, no fused epilogue).  split_from == 0:
+    // split K for products with few tiles, parts in part_out as [part][M][N]; split_from > 0: only
+    // the tiles of a last, partly filled wave are split, parts in tail_out as [tile][part][TM][BN].
+    // Either way the parts are summed afterwards in a fixed order.
+    const int work = split_from + (tiles - split_from) * kparts;
     Abort ab{abort_flag, status};
 
     if (threadIdx.x == 0) {
@@ -386,8 +407,8 @@ __global__ void __maxnreg__(kLaunchRegs)
             asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&map_ylo) : "memory");
             uint32_t it = 0;
             for (int u = unit; u < work; u += units) {
-                const int t = u / kparts, part = u - t * kparts;
-                const int kbeg = part * kpc, kend = min(nk, kbeg + kpc);
+                int t, part, kbeg, kend;
+                decode_unit(u, split_from, kparts, kpc, nk, t, part, kbeg, kend);
                 int mb, nb;
                 const int bt = t / tiles_per_batch;
                 tile_coords(t - bt * tiles_per_batch, num_m, num_n, mb, nb);
@@ -420,8 +441,8 @@ __global__ void __maxnreg__(kLaunchRegs)
             constexpr uint32_t idesc = idesc_3x(BN, F16, TM);
             uint32_t it = 0, gseg = 0;
             for (int u = unit; u < work; u += units) {
-                const int part = u % kparts;
-                const int kbeg = part * kpc, kend = min(nk, kbeg + kpc);
+                int t, part, kbeg, kend;
+                decode_unit(u, split_from, kparts, kpc, nk, t, part, kbeg, kend);
                 for (int kb0 = kbeg; kb0 < kend; kb0 += seg_kb, ++gseg) {
                     const uint32_t b = gseg & 1, bround = gseg >> 1;
                     if (!mbar_wait(&acc_empty[b], (bround & 1) ^ 1, ab, 2)) goto done;
@@ -463,9 +484,12 @@ __global__ void __maxnreg__(kLaunchRegs)
         const bool vec = ((ldr & 3) == 0) && ((((uintptr_t)r) & 15) == 0);
         uint32_t gseg = 0;
         for (int u = unit; u < work; u += units) {
-            const int t = u / kparts, part = u - t * kparts;
-            const int kbeg = part * kpc, kend = min(nk, kbeg + kpc);
-            float* const rb = kparts > 1 ? part_out + (int64_t)part * M * N : r;  // (kparts > 1: one batch)
+            int t, part, kbeg, kend;
+            decode_unit(u, split_from, kparts, kpc, nk, t, part, kbeg, kend);
+            // output: a whole tile goes to r; a split tile's part to part_out (every tile split,
+            // split_from == 0) or to tail_out (only the last wave's tiles split)
+            const bool tail = split_from > 0 && t >= split_from;
+            float* const rb = (kparts > 1 && split_from == 0) ? part_out + (int64_t)part * M * N : r;
             int mb, nb;
             const int bt = t / tiles_per_batch;
             tile_coords(t - bt * tiles_per_batch, num_m, num_n, mb, nb);
@@ -526,7 +550,10 @@ __global__ void __maxnreg__(kLaunchRegs)
             const int row = row0 + lane;
             const bool row_ok = row < M;
             const int rowc = row_ok ? row : row0;  // lanes past M compute but store nothing
-            float* out = rb + (int64_t)bt * M * ldr + (int64_t)rowc * ldr + colh;
+            float* out = tail ? tail_out + ((int64_t)((t - split_from) * kparts + part) * TM + (rowc - mb * TM)) * BN +
+                                    (colh - nb * BN)
+                              : rb + (int64_t)bt * M * ldr + (int64_t)rowc * ldr + colh;
+            const bool vec_u = tail || vec;  // the tail buffer's rows are BN floats, 16-byte aligned
             int ea = 0;
             if constexpr (F16) ea = epi.row_exp[(int64_t)bt * M + rowc];
 #pragma unroll
@@ -534,7 +561,7 @@ __global__ void __maxnreg__(kLaunchRegs)
                 float* v = sum + c * 32;
                 const int cb = colh + c * 32;
                 const bool full = cb + 32 <= N;
-                const bool fast = full && vec && (!F16 || ((((int64_t)bt * N) & 3) == 0));
+                const bool fast = full && vec_u && (!F16 || ((((int64_t)bt * N) & 3) == 0));
                 const bool staged = map_ok && full;
                 if (staged) {
                     if (c > 0 || !staged0) stage_bias(cb);
@@ -894,6 +921,42 @@ __global__ void __launch_bounds__(256) sum_parts(float* __restrict__ r, const fl
     }
 }
 
+// Last-wave split: r = part[0] + part[1] + ... (in that order) over the tiles [split_from, ...)
+// whose K range was cut into kparts units; parts laid out [tile][part][TM][BN].  One thread per
+// four consecutive columns of a tile row.
+template <int BN>
+__global__ void __launch_bounds__(256) sum_tail(float* __restrict__ r, const float* __restrict__ tail, int M, int N,
+                                                int TM, int num_m, int num_n, int split_from, int kparts) {
+    const int per_tile = TM * BN / 4;
+    const int64_t idx = (int64_t)blockIdx.x * 256 + threadIdx.x;
+    const int j = (int)(idx / per_tile);
+    const int local = (int)(idx - (int64_t)j * per_tile);
+    const int lr = local / (BN / 4), lc = (local - lr * (BN / 4)) * 4;
+    const int t = split_from + j, tpb = num_m * num_n;
+    const int bt = t / tpb;  // batch b's result starts at row b*M
+    int mb, nb;
+    tile_coords(t - bt * tpb, num_m, num_n, mb, nb);
+    const int row = mb * TM + lr, col = nb * BN + lc;
+    if (row >= M || col >= N) return;
+    r += (int64_t)bt * M * N;
+    const float* p = tail + ((int64_t)j * kparts * TM + lr) * BN + lc;
+    float4 a = __ldcs((const float4*)p);
+    for (int q = 1; q < kparts; ++q) {
+        const float4 b = __ldcs((const float4*)(p + (int64_t)q * TM * BN));
+        a.x = __fadd_rn(a.x, b.x); a.y = __fadd_rn(a.y, b.y);
+        a.z = __fadd_rn(a.z, b.z); a.w = __fadd_rn(a.w, b.w);
+    }
+    float* o = r + (int64_t)row * N + col;
+    if ((N & 3) == 0 && (((uintptr_t)r) & 15) == 0 && col + 4 <= N) {
+        *(float4*)o = a;
+    } else {
+        o[0] = a.x;
+        if (col + 1 < N) o[1] = a.y;
+        if (col + 2 < N) o[2] = a.z;
+        if (col + 3 < N) o[3] = a.w;
+    }
+}
+
 // Column maxima of Y[b][K][N] as f32 bits (|y| compares as an unsigned integer; NaN above inf):
 // a thread per column and 32-row chunk, eight independent loads in flight.
 __global__ void __launch_bounds__(256) col_absmax(const float* __restrict__ y, unsigned* __restrict__ cmax, int64_t K,
@@ -981,8 +1044,17 @@ int64_t round_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
 // exponents and column maxima.  Sized for the tf32 split, which needs the most.
 struct Layout {
     int64_t kp;
-    size_t xhi, xlo, yhi, ylo, rexp, cexp, cmax, parts, total;
+    size_t xhi, xlo, yhi, ylo, rexp, cexp, cmax, parts, tail, total;
     int kparts;  // split-K factor of an unfused single product (1: none)
+    int kpc;     // its ring stages per part
+};
+
+// The last wave of a persistent product of 1 to 8 waves: when the tiles left after the full
+// waves fill at most half of the CTAs (pairs), split each of them along K into parts (at least 4
+// ring stages each, at most 8 parts, parts x tiles <= CTAs), so that wave finishes in about
+// 1/parts of a tile time.
+struct TailPlan {
+    int parts = 1, kpc = 0, split_from = 0;
 };
 
 constexpr int kStagesPair = 6;  // 32 KB stages: A rows and half of Y's rows per CTA
@@ -1018,26 +1090,66 @@ int choose_parts(int64_t M, int64_t K, int64_t N, bool f16) {
     return (int)((nk + kpc - 1) / kpc);  // no empty part
 }
 
-Layout layout(int64_t M, int64_t K, int64_t N, bool f16) {
+TailPlan plan_tail(int64_t B, int64_t M, int64_t K, int64_t N, bool f16) {
+    TailPlan tp;
+    const bool pair = pair_for(M, f16);
+    const int64_t tm = pair ? 2 * BM : BM;
+    const int64_t tiles = B * ((M + tm - 1) / tm) * ((N + 255) / 256);
+    const int64_t units = pair ? sm_count() / 2 : sm_count();
+    const int64_t kp = (K + KPAD - 1) / KPAD * KPAD;
+    const int64_t nk = kp / (f16 ? BK16 : BK);
+    // (from 8 waves on, a mostly empty last wave costs under 1/16 of the product)
+    if (tiles <= units || tiles >= 8 * units) return tp;
+    const int64_t rem = tiles % units;
+    if (rem == 0 || 2 * rem > units) return tp;
+    int64_t parts = units / rem;
+    if (parts > 8) parts = 8;
+    if (parts > nk / 4) parts = nk / 4;
+    if (parts < 2) return tp;
+    const int64_t kpc = (nk + parts - 1) / parts;
+    parts = (nk + kpc - 1) / kpc;
+    if (parts < 2) return tp;
+    tp.parts = (int)parts;
+    tp.kpc = (int)kpc;
+    tp.split_from = (int)(tiles - rem);
+    return tp;
+}
+
+size_t tail_bytes(int64_t B, int64_t M, int64_t K, int64_t N, bool f16) {
+    const TailPlan tp = plan_tail(B, M, K, N, f16);
+    if (tp.parts < 2) return 0;
+    const int64_t tm = pair_for(M, f16) ? 2 * BM : BM;
+    const int64_t tiles = B * ((M + tm - 1) / tm) * ((N + 255) / 256);
+    return (size_t)((tiles - tp.split_from) * tp.parts * tm * 256 * 4);
+}
+
+// Scratch of B products of M x K times K x N (operands of all batches split into one array each).
+Layout layout(int64_t B, int64_t M, int64_t K, int64_t N, bool f16) {
     Layout l;
     l.kp = round_up(K < 1 ? 1 : K, KPAD);
     const int es = f16 ? 2 : 4;
-    size_t xs = (size_t)round_up(M * l.kp * es, 1024), ys = (size_t)round_up(N * l.kp * es, 1024);
+    const int64_t rows = B * M, cols = B * N;
+    size_t xs = (size_t)round_up(rows * l.kp * es, 1024), ys = (size_t)round_up(cols * l.kp * es, 1024);
     l.xhi = 0;
     l.xlo = xs;
     l.yhi = 2 * xs;
     l.ylo = 2 * xs + ys;
     l.rexp = 2 * xs + 2 * ys;
-    l.cexp = l.rexp + (size_t)round_up(M * 4, 256);
-    l.cmax = l.cexp + (size_t)round_up(N * 4, 256);
-    l.parts = l.cmax + (size_t)round_up(N * 4, 256);
-    l.kparts = choose_parts(M, K, N, f16);
-    l.total = l.parts + (l.kparts > 1 ? (size_t)round_up((int64_t)l.kparts * M * N * 4, 256) : 0);
+    l.cexp = l.rexp + (size_t)round_up(rows * 4, 256);
+    l.cmax = l.cexp + (size_t)round_up(cols * 4, 256);
+    l.parts = l.cmax + (size_t)round_up(cols * 4, 256);
+    l.kparts = B == 1 ? choose_parts(M, K, N, f16) : 1;
+    {
+        const int64_t nk = l.kp / (f16 ? BK16 : BK);
+        l.kpc = (int)((nk + l.kparts - 1) / l.kparts);
+    }
+    l.tail = l.parts + (l.kparts > 1 ? (size_t)round_up((int64_t)l.kparts * M * N * 4, 256) : 0);
+    l.total = l.tail + (l.kparts > 1 ? 0 : (size_t)round_up((int64_t)tail_bytes(B, M, K, N, f16), 256));
     return l;
 }
 
-size_t scratch_bytes(int64_t M, int64_t K, int64_t N) {
-    const size_t a = layout(M, K, N, false).total, b = layout(M, K, N, true).total;
+size_t scratch_bytes(int64_t B, int64_t M, int64_t K, int64_t N) {
+    const size_t a = layout(B, M, K, N, false).total, b = layout(B, M, K, N, true).total;
     return a > b ? a : b;
 }
 
@@ -1077,7 +1189,7 @@ bool make_bias_map(CUtensorMap* m, const float* bias, int64_t M, int64_t N) {
 template <bool FUSED, bool F16, bool PAIR>
 int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c, const CUtensorMap& d,
                 const CUtensorMap& bias, float* r, int64_t M, int64_t N, int64_t kp, int* status, const Epi& epi,
-                int64_t B, cudaStream_t st, int kparts, float* part_out) {
+                int64_t B, cudaStream_t st, int kparts, int kpc, int split_from, float* part_out, float* tail_out) {
     constexpr int STG = PAIR ? kStagesPair : kStages;
     using C = Cfg<kBN, STG, PAIR>;
     auto kern = gemm_3x<kBN, STG, FUSED, F16, PAIR>;
@@ -1085,11 +1197,13 @@ int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return (int)e;
     const int64_t tm = PAIR ? 2 * BM : BM;
-    const int64_t tiles = B * ((M + tm - 1) / tm) * ((N + kBN - 1) / kBN) * kparts;
+    const int64_t all = B * ((M + tm - 1) / tm) * ((N + kBN - 1) / kBN);
+    if (kparts <= 1) split_from = (int)all;
+    const int64_t tiles = split_from + (all - split_from) * kparts;  // work units
     if constexpr (!PAIR) {
         const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
         kern<<<grid, kThreads, smem, st>>>(a, b, c, d, bias, r, (int)M, (int)N, (int)kp, (int64_t)N, status, epi,
-                                           segment_kb(F16), (int)B, kparts, part_out);
+                                           segment_kb(F16), (int)B, kparts, kpc, split_from, part_out, tail_out);
         return (int)cudaGetLastError();
     } else {
         cudaLaunchConfig_t cfg = {};
@@ -1112,7 +1226,7 @@ int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c
         const int64_t clusters = tiles < max_clusters ? tiles : max_clusters;
         cfg.gridDim = dim3((unsigned)(2 * clusters));
         e = cudaLaunchKernelEx(&cfg, kern, a, b, c, d, bias, r, (int)M, (int)N, (int)kp, (int64_t)N, status, epi,
-                               segment_kb(F16), (int)B, kparts, part_out);
+                               segment_kb(F16), (int)B, kparts, kpc, split_from, part_out, tail_out);
         return (int)e;
     }
 }
@@ -1124,11 +1238,14 @@ extern "C" int mcu_matmul_tc_supported(void) {
     return encode_fn() != nullptr;
 }
 
-extern "C" size_t mcu_matmul_tc_scratch_bytes(int64_t M, int64_t K, int64_t N) { return scratch_bytes(M, K, N); }
+extern "C" size_t mcu_matmul_tc_scratch_bytes(int64_t M, int64_t K, int64_t N) { return scratch_bytes(1, M, K, N); }
 
-extern "C" int mcu_matmul_tc_kernels(int64_t M, int64_t K, int64_t N, int f16, int presplit) {
-    const int split = f16 ? 3 : (presplit ? 1 : 2);  // operand split kernels
-    return split + 1 + (choose_parts(M, K, N, f16 != 0) > 1 ? 1 : 0);
+extern "C" int mcu_matmul_tc_kernels(int64_t M, int64_t K, int64_t N, int f16, int flags) {
+    // flags: bit 0 = X arrives split by the previous layer (tf32), bit 1 = fused epilogue
+    const int split = f16 ? 3 : ((flags & 1) ? 1 : 2);  // operand split kernels
+    const bool parts = choose_parts(M, K, N, f16 != 0) > 1;
+    const bool tail = !parts && !(flags & 2) && plan_tail(1, M, K, N, f16 != 0).parts > 1;
+    return split + 1 + (parts || tail ? 1 : 0);
 }
 
 static int launch_tc(float* r, const float* x, const float* y, int64_t B, int64_t M, int64_t K, int64_t N,
@@ -1141,7 +1258,11 @@ extern "C" int mcu_launch_matmul_tc_ex(float* r, const float* x, const float* y,
 }
 
 extern "C" size_t mcu_matmul_tc_batched_scratch_bytes(int64_t B, int64_t M, int64_t K, int64_t N) {
-    return scratch_bytes(B * M, K, B * N);
+    return scratch_bytes(B, M, K, N);
+}
+
+extern "C" int mcu_matmul_tc_batched_kernels(int64_t B, int64_t M, int64_t K, int64_t N, int f16) {
+    return (f16 ? 3 : 2) + 1 + (plan_tail(B, M, K, N, f16 != 0).parts > 1 ? 1 : 0);
 }
 
 extern "C" int mcu_launch_matmul_tc_batched(float* r, const float* x, const float* y, int64_t B, int64_t M, int64_t K,
@@ -1154,7 +1275,7 @@ static int launch_tc(float* r, const float* x, const float* y, int64_t B, int64_
     if (B <= 0 || M <= 0 || N <= 0) return (int)cudaSuccess;
     if (B * M >= (1ll << 31) || B * N >= (1ll << 31) || K >= (1ll << 21) || !scratch) return (int)cudaErrorInvalidValue;
     if (B > 1 && ep) return (int)cudaErrorInvalidValue;
-    const Layout l = layout(B * M, K, B * N, f16 != 0);
+    const Layout l = layout(B, M, K, N, f16 != 0);
     char* base = (char*)scratch;
     void* xhi = base + l.xhi;
     void* xlo = base + l.xlo;
@@ -1221,17 +1342,45 @@ static int launch_tc(float* r, const float* x, const float* y, int64_t B, int64_
         CUtensorMap mb;
         memset(&mb, 0, sizeof(mb));
         epi.bias_map = ep->bias && make_bias_map(&mb, ep->bias, M, N);
-        if (pair) return launch_gemm<true, true, true>(mxh, mxl, myh, myl, mb, r, M, N, l.kp, status, epi, B, st, 1, nullptr);
-        return f16 ? launch_gemm<true, true, false>(mxh, mxl, myh, myl, mb, r, M, N, l.kp, status, epi, B, st, 1, nullptr)
-                   : launch_gemm<true, false, false>(mxh, mxl, myh, myl, mb, r, M, N, l.kp, status, epi, B, st, 1, nullptr);
+        if (pair)
+            return launch_gemm<true, true, true>(mxh, mxl, myh, myl, mb, r, M, N, l.kp, status, epi, B, st, 1, 0, 0,
+                                                 nullptr, nullptr);
+        return f16 ? launch_gemm<true, true, false>(mxh, mxl, myh, myl, mb, r, M, N, l.kp, status, epi, B, st, 1, 0, 0,
+                                                    nullptr, nullptr)
+                   : launch_gemm<true, false, false>(mxh, mxl, myh, myl, mb, r, M, N, l.kp, status, epi, B, st, 1, 0, 0,
+                                                     nullptr, nullptr);
     }
     Epi plain{};
     plain.row_exp = rexp;
     plain.col_exp = cexp;
-    int rc = pair ? launch_gemm<false, true, true>(mxh, mxl, myh, myl, mxh, r, M, N, l.kp, status, plain, B, st, kparts, part)
-         : f16 ? launch_gemm<false, true, false>(mxh, mxl, myh, myl, mxh, r, M, N, l.kp, status, plain, B, st, kparts, part)
-               : launch_gemm<false, false, false>(mxh, mxl, myh, myl, mxh, r, M, N, l.kp, status, plain, B, st, kparts, part);
-    if (rc || kparts == 1) return rc;
+    // an unfused single product whose last wave is mostly empty splits that wave's tiles along K
+    int gparts = kparts, gkpc = l.kpc, split_from = 0;
+    float* tail = nullptr;
+    if (kparts == 1 && !fused) {
+        const TailPlan tp = plan_tail(B, M, K, N, h);
+        if (tp.parts > 1) {
+            gparts = tp.parts;
+            gkpc = tp.kpc;
+            split_from = tp.split_from;
+            tail = (float*)(base + l.tail);
+        }
+    }
+    int rc = pair ? launch_gemm<false, true, true>(mxh, mxl, myh, myl, mxh, r, M, N, l.kp, status, plain, B, st, gparts,
+                                                   gkpc, split_from, part, tail)
+         : f16 ? launch_gemm<false, true, false>(mxh, mxl, myh, myl, mxh, r, M, N, l.kp, status, plain, B, st, gparts,
+                                                 gkpc, split_from, part, tail)
+               : launch_gemm<false, false, false>(mxh, mxl, myh, myl, mxh, r, M, N, l.kp, status, plain, B, st, gparts,
+                                                  gkpc, split_from, part, tail);
+    if (rc) return rc;
+    if (tail) {
+        const int tm = pair ? 2 * BM : BM;
+        const int num_m = (int)((M + tm - 1) / tm), num_n = (int)((N + kBN - 1) / kBN);
+        const int64_t ntail = B * num_m * num_n - split_from;
+        const int64_t blocks = ntail * tm * kBN / 4 / 256;
+        sum_tail<kBN><<<(unsigned)blocks, 256, 0, st>>>(r, tail, (int)M, (int)N, tm, num_m, num_n, split_from, gparts);
+        return (int)cudaGetLastError();
+    }
+    if (kparts == 1) return rc;
     // a fused layer whose product was split: its epilogue runs after the sum, in the same order
     Epi fe{};
     if (fused) {

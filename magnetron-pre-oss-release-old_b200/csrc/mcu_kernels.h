@@ -80,9 +80,10 @@ int mcu_skinny_noalloc_scratch(void** out);
  * f16 = 0: tf32 hi/lo split (kind::tf32), f16 = 1: scaled f16 hi/lo split (kind::f16).
  * scratch needs mcu_matmul_tc_scratch_bytes(M, K, N) bytes (either split). */
 size_t mcu_matmul_tc_scratch_bytes(int64_t M, int64_t K, int64_t N);
-/* Kernels one single (unbatched) product launches: operand splits, the GEMM, and the part
- * sum when K is split (presplit: X arrives split, tf32 only). */
-int mcu_matmul_tc_kernels(int64_t M, int64_t K, int64_t N, int f16, int presplit);
+/* Kernels one single (unbatched) product launches: operand splits, the GEMM, and the part sum
+ * when K is split (for few tiles, or for the tiles of a mostly empty last wave); flags bit 0:
+ * X arrives split by the previous layer's epilogue (tf32), bit 1: fused dense-layer epilogue. */
+int mcu_matmul_tc_kernels(int64_t M, int64_t K, int64_t N, int f16, int flags);
 int mcu_launch_matmul_tc(float* r, const float* x, const float* y, int64_t M, int64_t K, int64_t N,
                          void* scratch, int* status, cudaStream_t st, int f16);
 int mcu_matmul_tc_supported(void);
@@ -103,6 +104,7 @@ typedef struct mcu_tc_epilogue {
     int act;
 } mcu_tc_epilogue;
 size_t mcu_matmul_tc_batched_scratch_bytes(int64_t B, int64_t M, int64_t K, int64_t N);
+int mcu_matmul_tc_batched_kernels(int64_t B, int64_t M, int64_t K, int64_t N, int f16);
 int mcu_launch_matmul_tc_batched(float* r, const float* x, const float* y, int64_t B, int64_t M, int64_t K,
                                  int64_t N, void* scratch, int* status, cudaStream_t st, int f16);
 int mcu_launch_matmul_tc_ex(float* r, const float* x, const float* y, int64_t M, int64_t K, int64_t N,

@@ -312,7 +312,7 @@ def _split(dev, split):
 @pytest.mark.parametrize("split", SPLITS)
 @pytest.mark.parametrize("mkn", [(128, 32, 256), (300, 100, 700), (1000, 777, 300), (2048, 1024, 4096),
                                  (256, 4096, 1000), (4096, 4096, 4096), (1024, 1024, 1024), (64, 4096, 2048),
-                                 (40, 1024, 4096)])
+                                 (40, 1024, 4096), (4000, 2000, 4000)])
 def test_matmul_tensor_core_normwise(mkn, split):
     """tcgen05 path (tf32 or scaled f16 split) through the vtable; within 1e-5 of the exact
     product, norm-wise."""
@@ -330,6 +330,39 @@ def test_matmul_tensor_core_normwise(mkn, split):
         dev.L.mag_cuda_set_matmul_mode(dev.p, 0)
     assert dev.L.mag_cuda_synchronize(dev.p) == 0
     assert _normwise_ok(got, x, y, m, k, n)
+
+
+@pytest.mark.parametrize("split", SPLITS)
+def test_matmul_last_wave_split_deterministic(split):
+    """4096^3 has 256 tiles of 256 x 256 on 74 CTA pairs (512 of 128 x 256 on 148 CTAs for tf32):
+    the last, mostly empty wave's tiles are split along K and summed in a fixed order, so two
+    runs give the same bits and the product stays within 1e-5 of the exact one."""
+    dev = device()
+    _split(dev, split)
+    o = oracle()
+    m = k = n = 4096
+    s = o.stream(7350)
+    x = s.normal(m * k, 0.0, k ** -0.5)
+    y = s.normal(k * n, 0.0, k ** -0.5)
+    tx, ty, tr = dev.tensor((m, k)), dev.tensor((k, n)), dev.tensor((m, n))
+    tx.write(x)
+    ty.write(y)
+    MB.check(dev.L.mag_cuda_set_matmul_mode(dev.p, 2), "tc mode")
+    try:
+        n0 = dev.launches()
+        MB.check(dev.L.mag_cuda_matmul_f32(dev.p, tr.data_ptr, tx.data_ptr, ty.data_ptr, m, k, n), "mm")
+        first = tr.read()
+        n1 = dev.launches()
+        MB.check(dev.L.mag_cuda_matmul_f32(dev.p, tr.data_ptr, tx.data_ptr, ty.data_ptr, m, k, n), "mm")
+        second = tr.read()
+    finally:
+        dev.L.mag_cuda_set_matmul_mode(dev.p, 0)
+    assert dev.L.mag_cuda_synchronize(dev.p) == 0
+    assert n1 - n0 == (5 if split == MB.TC_SPLIT_F16 else 4)  # splits, GEMM, last-wave part sum
+    assert bits_equal(first, second).all()
+    rows = o.matmul_rows(x, y, 4000, 3, k, n)  # rows of the last wave's tiles
+    ref_err = np.abs(rows - first.reshape(m, n)[4000:4003].reshape(-1))
+    assert float(ref_err.max()) <= 1e-5 * float(np.abs(rows).max())
 
 
 @pytest.mark.parametrize("split", SPLITS)
