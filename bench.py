@@ -527,7 +527,7 @@ def sweep(dev, MB, torch, local):
     ms = timeit(lambda: dev.L.mag_cuda_reduce_f32(dev.p, MB.OP["SUM"], r.data_ptr, x.data_ptr, dims, st))
     out["sum_2^28_GBps"] = 4.0 * n / (ms / 1e3) / 1e9
     ms = timeit(lambda: dev.L.mag_cuda_softmax_rows_f32(dev.p, r.data_ptr, x.data_ptr, 4096, 32768))
-    out["softmax_rows_4096x32768_GBps"] = 8.0 * n / (ms / 1e3) / 1e9
+    out["softmax_rows_4096x32768_GBps"] = 8.0 * 4096 * 32768 / (ms / 1e3) / 1e9
     m = 4096
     ms = timeit(lambda: dev.L.mag_cuda_matmul_f32(dev.p, r.data_ptr, x.data_ptr, y.data_ptr, m, m, m), reps=2)
     out["matmul_4096^3_TFLOPs"] = 2.0 * m ** 3 / (ms / 1e3) / 1e12
