@@ -563,18 +563,10 @@ __global__ void __maxnreg__(kLaunchRegs)
                 const bool full = cb + 32 <= N;
                 const bool fast = full && vec_u && (!F16 || ((((int64_t)bt * N) & 3) == 0));
                 const bool staged = map_ok && full;
-                float4 bb[8];  // this lane's row of a staged bias chunk
                 if (staged) {
-                    if (c == 0 && !staged0) stage_bias(cb);
+                    if (c > 0 || !staged0) stage_bias(cb);
                     if (!mbar_wait(&bias_full[ew], bphase, ab, 5)) goto done;
                     bphase ^= 1;
-                    // row `lane` of the chunk (16-byte unit q at (q ^ (lane & 7)) under the 128B
-                    // swizzle) into registers; the slot then takes the next chunk while this one
-                    // goes through GELU and the stores
-#pragma unroll
-                    for (int q4 = 0; q4 < 8; ++q4) bb[q4] = *(const float4*)(bbuf + lane * 128 + ((q4 ^ (lane & 7)) << 4));
-                    __syncwarp();
-                    if (c + 1 < HC / 32 && cb + 64 <= N) stage_bias(cb + 32);
                 }
                 if (fast) {
                     // one float4 at a time through unscale, bias, GELU, split and store: short live
@@ -592,8 +584,9 @@ __global__ void __maxnreg__(kLaunchRegs)
                             a[3] = unscale(a[3], ea + e4.w);
                         }
                         if constexpr (FUSED) {
-                            if (staged || pb) {
-                                const float4 b4 = staged ? bb[j >> 2] : __ldcs((const float4*)(pb + j));
+                            if (staged || pb) {  // row `lane` of the staged chunk: 16-byte unit j/4, swizzled
+                                const float4 b4 = staged ? *(const float4*)(bbuf + lane * 128 + (((j >> 2) ^ (lane & 7)) << 4))
+                                                         : __ldcs((const float4*)(pb + j));
                                 a[0] = __fadd_rn(a[0], b4.x);
                                 a[1] = __fadd_rn(a[1], b4.y);
                                 a[2] = __fadd_rn(a[2], b4.z);
@@ -615,9 +608,11 @@ __global__ void __maxnreg__(kLaunchRegs)
                         }
                         if (row_ok) *(float4*)(out + c * 32 + j) = make_float4(a[0], a[1], a[2], a[3]);
                     }
+                    if (staged) __syncwarp();  // every lane has read the slot before it is refilled
                     continue;
                 }
-                if (!row_ok) continue;  // (a staged chunk is always on the fast path: full and vec)
+                if (staged) __syncwarp();  // (a staged chunk is always on the fast path: full and vec)
+                if (!row_ok) continue;
                 // ragged edge or unaligned result: element by element, bias from global memory
                 const float* pb = FUSED && epi.bias ? epi.bias + (int64_t)row * N + cb : nullptr;
                 const int* ce = F16 ? epi.col_exp + (int64_t)bt * N + cb : nullptr;
