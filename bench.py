@@ -710,12 +710,14 @@ def run_case(args):
         x.write(v)
         y.write(v)
         dims, st = MB.i64x6([n, 1, 1, 1, 1, 1]), MB.i64x6(MB.strides6([n, 1, 1, 1, 1, 1]))
-        if args.case in ("tile", "bcast2"):
+        if args.case in ("tile", "bcast2", "bcast2s"):
             if args.case == "tile":   # x rm [8,16,32,64,8,256] (+) y rm [1,16,1,64,1,256]
                 xs, ys = (256, 8, 64, 32, 16, 8), (256, 1, 64, 1, 16, 1)
                 rs = xs
-            else:                     # [8,16,1,64,1,256] (+) [1,16,32,1,128,256] -> 2^33 outputs
+            elif args.case == "bcast2":  # [8,16,1,64,1,256] (+) [1,16,32,1,128,256] -> 2^33 outputs
                 xs, ys, rs = (256, 1, 64, 1, 16, 8), (256, 128, 1, 32, 16, 1), (256, 128, 64, 32, 16, 8)
+            else:                     # profiling size: [1,16,1,4,1,256] (+) [1,16,32,1,128,256] -> 2^28
+                xs, ys, rs = (256, 1, 4, 1, 16, 1), (256, 128, 1, 32, 16, 1), (256, 128, 4, 32, 16, 1)
             for t in (x, y, r):
                 t.free()
             nx, ny, nr = int(np.prod(xs)), int(np.prod(ys)), int(np.prod(rs))
@@ -1065,7 +1067,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--case", default=None, choices=["gemm", "layer", "add", "sigmoid", "sum", "softmax", "softmax1k", "softmax256k", "skinny", "tile", "bcast2",
+    ap.add_argument("--case", default=None, choices=["gemm", "layer", "add", "sigmoid", "sum", "softmax", "softmax1k", "softmax256k", "skinny", "tile", "bcast2", "bcast2s",
                                                       "fill_uniform", "fill_normal", "fill_const", "storage", "image", "sharded"],
                     help="run one kernel family for a profiler instead of the benchmark")
     ap.add_argument("--size", type=int, default=None)

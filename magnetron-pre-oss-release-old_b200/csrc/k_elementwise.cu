@@ -321,7 +321,7 @@ struct RowWalk {
 };
 
 // Rows of at most 128 * STEPS columns, vectorised: a warp walks kRowChunk consecutive rows,
-// decomposing the first row's indices once and carrying them to the next rows, with two
+// decomposing the first row's indices once and carrying them to the next rows, with several
 // rows' loads in flight before their stores.
 template <int OP, int STEPS>
 __global__ void __launch_bounds__(kThreads, 2) binary_rows_chunked(float* __restrict__ r, const float* __restrict__ x,
@@ -372,21 +372,25 @@ __global__ void __launch_bounds__(kThreads, 2) binary_rows_chunked(float* __rest
         RowWalk w;
         w.start(row0, p);
         const uint32_t rows_here = min(kRowChunk, nrows - row0);
-        for (uint32_t rr = 0; rr < rows_here; rr += 2) {
-            float4 a0[STEPS], b0[STEPS], a1[STEPS], b1[STEPS];
-            const int64_t ro0 = w.ro;
-            load_x(w.xo, a0);
-            load_y(w.yo, b0);
-            w.next(p);
-            const bool two = rr + 1 < rows_here;
-            const int64_t ro1 = w.ro;
-            if (two) {
-                load_x(w.xo, a1);
-                load_y(w.yo, b1);
-                w.next(p);
+        // R rows' loads in flight before their stores: 4 for rows of at most 256 columns
+        // (the loads are L2 latency-bound there; 114 registers allow 2 CTAs per SM), else 2
+        constexpr int R = STEPS <= 2 ? 4 : 2;
+        for (uint32_t rr = 0; rr < rows_here; rr += R) {
+            float4 a[R][STEPS], b[R][STEPS];
+            int64_t ro[R];
+            const uint32_t nr = min((uint32_t)R, rows_here - rr);
+#pragma unroll
+            for (int k = 0; k < R; ++k) {
+                if ((uint32_t)k < nr) {
+                    ro[k] = w.ro;
+                    load_x(w.xo, a[k]);
+                    load_y(w.yo, b[k]);
+                    w.next(p);
+                }
             }
-            store_row(ro0, a0, b0);
-            if (two) store_row(ro1, a1, b1);
+#pragma unroll
+            for (int k = 0; k < R; ++k)
+                if ((uint32_t)k < nr) store_row(ro[k], a[k], b[k]);
         }
     }
 }
