@@ -67,18 +67,49 @@ __global__ void __launch_bounds__(kThreads) unary_vec4(float4* __restrict__ r, c
                                                        uint64_t n4, float xi) {
     uint64_t stride = (uint64_t)gridDim.x * kThreads;
     uint64_t i = (uint64_t)blockIdx.x * kThreads + threadIdx.x;
-    for (; i + 3 * stride < n4; i += 4 * stride) {
-        float4 v[4];
+    if constexpr (is_lane_op(OP)) {
+        // polynomial lanes: the next four loads are issued before this group is computed
+        if (i + 3 * stride < n4) {
+            float4 v[4];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) v[u] = __ldcs(x + i + u * stride);
+            for (int u = 0; u < 4; ++u) v[u] = __ldcs(x + i + u * stride);
+            for (;;) {
+                const uint64_t in = i + 4 * stride;
+                const bool more = in + 3 * stride < n4;
+                float4 w[4];
+                if (more) {
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            float4 o;
-            o.x = uapply<OP>(v[u].x, xi, true);
-            o.y = uapply<OP>(v[u].y, xi, true);
-            o.z = uapply<OP>(v[u].z, xi, true);
-            o.w = uapply<OP>(v[u].w, xi, true);
-            __stcs(r + i + u * stride, o);
+                    for (int u = 0; u < 4; ++u) w[u] = __ldcs(x + in + u * stride);
+                }
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    float4 o;
+                    o.x = uapply<OP>(v[u].x, xi, true);
+                    o.y = uapply<OP>(v[u].y, xi, true);
+                    o.z = uapply<OP>(v[u].z, xi, true);
+                    o.w = uapply<OP>(v[u].w, xi, true);
+                    __stcs(r + i + u * stride, o);
+                }
+                i = in;
+                if (!more) break;
+#pragma unroll
+                for (int u = 0; u < 4; ++u) v[u] = w[u];
+            }
+        }
+    } else {
+        for (; i + 3 * stride < n4; i += 4 * stride) {
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) v[u] = __ldcs(x + i + u * stride);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                float4 o;
+                o.x = uapply<OP>(v[u].x, xi, true);
+                o.y = uapply<OP>(v[u].y, xi, true);
+                o.z = uapply<OP>(v[u].z, xi, true);
+                o.w = uapply<OP>(v[u].w, xi, true);
+                __stcs(r + i + u * stride, o);
+            }
         }
     }
     for (; i < n4; i += stride) {
