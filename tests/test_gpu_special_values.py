@@ -90,3 +90,59 @@ def test_device_on_special_values(op):
             g, w = got[tails], want[tails]
             ok = same(g, w) | (np.isfinite(g) & np.isfinite(w) & (ulp_diff(g, w) <= 2))
             assert ok.all(), (op, shape, x[tails][~ok])
+
+
+def _pairs():
+    """Every ordered pair of special values, as two (n,) vectors."""
+    a, b = np.meshgrid(SPECIALS, SPECIALS, indexing="ij")
+    return a.reshape(-1).astype(np.float32), b.reshape(-1).astype(np.float32)
+
+
+BINARY = ["ADD", "SUB", "MUL", "DIV"]
+
+
+def test_oracle_binary_matches_reference_on_special_values():
+    from oracle import RefLib, REF_SO
+    if not os.path.exists(REF_SO):
+        pytest.skip("reference library not built (make -C oracle ref)")
+    o, R = oracle(), RefLib()
+    x, y = _pairs()
+    try:
+        for op in BINARY:
+            tx, ty = R.tensor_nd((x.size,)), R.tensor_nd((y.size,))
+            R.write(tx, x)
+            R.write(ty, y)
+            got = R.read(R.op(op, tx, ty))
+            want = o.binary(op, x, pad6((x.size,)), y, pad6((y.size,)))
+            assert same(got, want).all(), (op, x[~same(got, want)][:4], y[~same(got, want)][:4])
+    finally:
+        R.close()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("op", BINARY)
+def test_device_binary_on_special_values(op):
+    dev, o = device(), oracle()
+    x, y = _pairs()
+    got, _, _ = run_op(dev, op, [x, y], [(x.size,), (y.size,)])
+    want = o.binary(op, x, pad6((x.size,)), y, pad6((y.size,)))
+    assert same(got, want).all(), (op, x[~same(got, want)][:4], y[~same(got, want)][:4])
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("op", ["SUM", "MEAN", "MIN", "MAX"])
+def test_device_reductions_on_special_values(op):
+    """Full reductions over vectors holding infinities, NaN, signed zeros and subnormals: the
+    reference's double sums and fminf/fmaxf (which skip NaN, from +-inf) give the same value.
+    Values compare with ==: over zeros of both signs the reference's MIN/MAX keep whichever
+    zero glibc's argument order leaves, which a reduction tree cannot reproduce; the mixed
+    finite case is exact in double in any summation order."""
+    dev, o = device(), oracle()
+    cases = [SPECIALS, np.array([0.5, -0.25, 1.0, 88.5, -100.0, 0.0, -0.0, 3.0], np.float32),
+             np.array([np.inf, 1.0, -2.0], np.float32), np.array([np.nan, np.nan], np.float32),
+             np.array([np.nan, 1.0, np.nan], np.float32), np.array([-0.0, 0.0, -0.0], np.float32),
+             np.array([1e-40, -3e-40, 2e-45] * 300, np.float32)]
+    for v in cases:
+        got, _, _ = run_op(dev, op, [v], [(v.size,)])
+        want = np.float32(o.reduce(op, v, pad6((v.size,))))
+        assert got[0] == want or (np.isnan(got[0]) and np.isnan(want)), (op, v[:6], got[0], want)
