@@ -146,3 +146,48 @@ def test_device_reductions_on_special_values(op):
         got, _, _ = run_op(dev, op, [v], [(v.size,)])
         want = np.float32(o.reduce(op, v, pad6((v.size,))))
         assert got[0] == want or (np.isnan(got[0]) and np.isnan(want)), (op, v[:6], got[0], want)
+
+
+@pytest.mark.gpu
+def test_exact_matmul_on_special_values():
+    """The bit-exact MATMUL path (the reference's i-k-j loop, separately rounded multiply and add)
+    propagates infinities and NaN exactly as the oracle's restatement of it."""
+    import mag_b200 as MB
+    dev, o = device(), oracle()
+    m, k, n = 8, 11, 8
+    rng = np.random.default_rng(7)
+    x = rng.uniform(-1, 1, m * k).astype(np.float32)
+    y = rng.uniform(-1, 1, k * n).astype(np.float32)
+    x[[3, 17, 40, 41]] = [np.inf, -np.inf, np.nan, -0.0]
+    y[[5, 22, 60]] = [0.0, np.inf, 1e-40]
+    MB.check(dev.L.mag_cuda_set_matmul_mode(dev.p, 1), "exact")
+    try:
+        got, _, _ = run_op(dev, "MATMUL", [x, y], [(m, k), (k, n)])
+    finally:
+        dev.L.mag_cuda_set_matmul_mode(dev.p, 0)
+    want = o.matmul(x, y, m, k, n)
+    assert same(got, want).all(), np.where(~same(got, want))
+
+
+@pytest.mark.gpu
+def test_softmax_rows_with_masked_entries():
+    """Rows with -inf entries (masked positions) give exact zeros there and a normal softmax over
+    the rest; a row that is all -inf gives NaN, as exp(x - max) / sum does in the oracle."""
+    dev, o = device(), oracle()
+    for cols in (10, 1024, 8193):
+        rows = 4
+        x = np.random.default_rng(cols).uniform(-5, 5, rows * cols).astype(np.float32)
+        x[0:cols:3] = -np.inf               # row 0: every third entry masked
+        x[cols:2 * cols] = -np.inf          # row 1: fully masked
+        x[2 * cols + 1] = np.inf            # row 2: one +inf (max - max is NaN there)
+        tx, tr = dev.tensor((rows * cols,)), dev.tensor((rows * cols,))
+        tx.write(x)
+        import mag_b200 as MB
+        MB.check(dev.L.mag_cuda_softmax_rows_f32(dev.p, tr.data_ptr, tx.data_ptr, rows, cols), "softmax")
+        got = tr.read()
+        want = o.softmax_rows(x, rows, cols)
+        assert np.array_equal(np.isnan(got), np.isnan(want)), cols
+        fin = ~np.isnan(want)
+        assert np.all(got[fin][want[fin] == 0] == 0), cols
+        nz = fin & (want != 0)
+        assert np.all(np.abs(got[nz] - want[nz]) <= 1e-6 * np.abs(want[nz])), cols
