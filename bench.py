@@ -755,13 +755,16 @@ def run_case(args):
             fill = getattr(dev.L, f"mag_cuda_{args.case}_pcg_f32")
             fn = lambda: fill(dev.p, r.data_ptr, n, 0.0, 1.0, ctypes.byref(g.state), g.inc)
             work = 4.0 * n / 1e9
+        elif args.case == "batched":  # 64 products of 512 x 512 x 512
+            fn = lambda: dev.L.mag_cuda_matmul_batched_f32(dev.p, r.data_ptr, x.data_ptr, y.data_ptr, 64, 512, 512, 512)
+            work = 2.0 * 64 * 512 ** 3 / 1e12
         elif args.case == "skinny":  # M = 1, K = N = 4096
             fn = lambda: dev.L.mag_cuda_matmul_f32(dev.p, r.data_ptr, x.data_ptr, y.data_ptr, 1, 4096, 4096)
             work = 4.0 * (4096 + 4096 * 4096 + 4096) / 1e9
         else:
             fn = lambda: dev.L.mag_cuda_softmax_rows_f32(dev.p, r.data_ptr, x.data_ptr, n // 32768, 32768)
             work = 8.0 * n / 1e9
-        unit = "GB/s"
+        unit = "TFLOP/s" if args.case == "batched" else "GB/s"
     stream = torch.cuda.ExternalStream(dev.stream)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     MB.check(fn(), args.case)
@@ -1067,7 +1070,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--case", default=None, choices=["gemm", "layer", "add", "sigmoid", "sum", "softmax", "softmax1k", "softmax256k", "skinny", "tile", "bcast2", "bcast2s",
+    ap.add_argument("--case", default=None, choices=["gemm", "layer", "add", "sigmoid", "sum", "softmax", "softmax1k", "softmax256k", "skinny", "tile", "bcast2", "bcast2s", "batched",
                                                       "fill_uniform", "fill_normal", "fill_const", "storage", "image", "sharded"],
                     help="run one kernel family for a profiler instead of the benchmark")
     ap.add_argument("--size", type=int, default=None)
