@@ -972,8 +972,8 @@ __global__ void __launch_bounds__(256) col_absmax(const float* __restrict__ y, u
 }
 
 // Y[K][N] -> hi/lo transposed [N][Kp] f16 through a 64 (k) x 64 (n) shared tile, scaled per
-// column; each thread stores pairs of consecutive k as one 32-bit word.  col_exp[N] is
-// written by the first k-block.
+// column.  Each thread loads four float4 of Y's rows and stores eight consecutive k of one
+// column as one 16-byte word of hi and one of lo.  col_exp[N] is written by the first k-block.
 __global__ void __launch_bounds__(256) split_cols_t_f16(const float* __restrict__ y, const unsigned* __restrict__ cmax,
                                                         __half* __restrict__ hi, __half* __restrict__ lo,
                                                         int* __restrict__ col_exp, int64_t K, int64_t N, int64_t Kp) {
@@ -985,27 +985,52 @@ __global__ void __launch_bounds__(256) split_cols_t_f16(const float* __restrict_
     cmax += (int64_t)blockIdx.z * N;
     col_exp += (int64_t)blockIdx.z * N;
     const int64_t k0 = (int64_t)blockIdx.y * 64, n0 = (int64_t)blockIdx.x * 64;
-    const int tx = threadIdx.x & 63, ty = threadIdx.x >> 6;  // 64 x 4
     if (threadIdx.x < 64 && n0 + threadIdx.x < N) {
         const unsigned b = cmax[n0 + threadIdx.x];
         const int e = b > 0x7F800000u ? 0 : scale_exp(__uint_as_float(b));
         scl[threadIdx.x] = __int_as_float((127 + e) << 23);
         if (blockIdx.y == 0) col_exp[n0 + threadIdx.x] = e;
     }
-    for (int j = ty; j < 64; j += 4) {  // coalesced rows of Y
-        const int64_t k = k0 + j, n = n0 + tx;
-        tile[j][tx] = (k < K && n < N) ? y[k * N + n] : 0.0f;
+    // 64 rows of 16 float4: thread t takes float4 t & 15 of rows (t >> 4) + 16 i
+    const bool vec = (N % 4 == 0) && ((((uintptr_t)y) & 15) == 0);
+    const int c4 = (threadIdx.x & 15) * 4, r0 = threadIdx.x >> 4;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int j = r0 + 16 * i;
+        const int64_t k = k0 + j, n = n0 + c4;
+        float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (k < K) {
+            const float* py = y + k * N + n;
+            if (vec && n + 4 <= N) {
+                v = *(const float4*)py;
+            } else {
+                v.x = n < N ? py[0] : 0.0f;
+                v.y = n + 1 < N ? py[1] : 0.0f;
+                v.z = n + 2 < N ? py[2] : 0.0f;
+                v.w = n + 3 < N ? py[3] : 0.0f;
+            }
+        }
+        tile[j][c4] = v.x;
+        tile[j][c4 + 1] = v.y;
+        tile[j][c4 + 2] = v.z;
+        tile[j][c4 + 3] = v.w;
     }
     __syncthreads();
-    const int kk = (threadIdx.x & 31) * 2;  // two consecutive k per thread
-    for (int j = threadIdx.x >> 5; j < 64; j += 8) {
-        const int64_t n = n0 + j, k = k0 + kk;
-        if (n < N && k < Kp) {  // Kp is a multiple of 32: k and k + 1 are both inside
-            __half h0, l0, h1, l1;
-            split_f16(tile[kk][j], scl[j], h0, l0);
-            split_f16(tile[kk + 1][j], scl[j], h1, l1);
-            *(uint32_t*)(hi + n * Kp + k) = pack2(h0, h1);
-            *(uint32_t*)(lo + n * Kp + k) = pack2(l0, l1);
+    // 64 columns x 8 runs of 8 k: two per thread; a warp writes four columns' 128-byte runs
+#pragma unroll
+    for (int q2 = 0; q2 < 2; ++q2) {
+        const int item = threadIdx.x + 256 * q2;
+        const int j = item >> 3, kc = (item & 7) * 8;
+        const int64_t n = n0 + j, k = k0 + kc;
+        if (n < N && k < Kp) {  // Kp is a multiple of 32: k .. k + 7 are all inside
+            const float sc = scl[j];
+            __half h[8], l[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) split_f16(tile[kc + q][j], sc, h[q], l[q]);
+            *(uint4*)(hi + n * Kp + k) = make_uint4(pack2(h[0], h[1]), pack2(h[2], h[3]), pack2(h[4], h[5]),
+                                                    pack2(h[6], h[7]));
+            *(uint4*)(lo + n * Kp + k) = make_uint4(pack2(l[0], l[1]), pack2(l[2], l[3]), pack2(l[4], l[5]),
+                                                    pack2(l[6], l[7]));
         }
     }
 }
