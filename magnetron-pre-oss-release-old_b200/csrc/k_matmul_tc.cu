@@ -74,6 +74,16 @@ int sm_count() {
 // ------------------------------------------------------------ PTX wrappers
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
+__device__ __forceinline__ float4 lds4(uint32_t a) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(a) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void sts4(uint32_t a, float x, float y, float z, float w) {
+    asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(a), "f"(x), "f"(y), "f"(z), "f"(w) : "memory");
+}
+
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
 }
@@ -550,29 +560,132 @@ __global__ void __maxnreg__(kLaunchRegs)
             const int row = row0 + lane;
             const bool row_ok = row < M;
             const int rowc = row_ok ? row : row0;  // lanes past M compute but store nothing
+            int ea = 0;
+            if constexpr (F16) ea = epi.row_exp[(int64_t)bt * M + rowc];
+            if constexpr (FUSED) {
+                // Every 32-column chunk passes through this warp's 4 KB slot.  Phase A: lane = row
+                // writes its unscaled sums (plus the staged bias) in place, in the slot's 128-byte
+                // swizzle.  Phase B: a rolled loop walks the slot four rows at a time, eight lanes to
+                // a row, through the unstaged bias, GELU, the tf32 split and the stores, so each
+                // row's 128 bytes leave as one coalesced store and the per-element code exists once.
+                // (a fused product is one unsplit product: its tiles write r, batch 0)
+                const bool bvec = ((((uintptr_t)epi.bias) & 15) == 0) && (N & 3) == 0;
+                const int cc = (lane & 7) * 4;
+                const uint32_t sbuf = smem_u32(bbuf);
+#pragma unroll
+                for (int c = 0; c < HC / 32; ++c) {
+                    const int cb = colh + c * 32;
+                    if (cb >= N) break;
+                    const bool full = cb + 32 <= N;
+                    const bool staged = map_ok && full;
+                    if (staged) {
+                        if (c > 0 || !staged0) stage_bias(cb);
+                        if (!mbar_wait(&bias_full[ew], bphase, ab, 5)) goto done;
+                        bphase ^= 1;
+                    }
+                    const int* ce = F16 ? epi.col_exp + (int64_t)bt * N + cb : nullptr;
+#pragma unroll
+                    for (int j = 0; j < 32; j += 4) {
+                        const uint32_t slot = sbuf + lane * 128 + (((j >> 2) ^ (lane & 7)) << 4);
+                        float a[4] = {sum[c * 32 + j], sum[c * 32 + j + 1], sum[c * 32 + j + 2], sum[c * 32 + j + 3]};
+                        if constexpr (F16) {  // undo the operands' power-of-two scaling
+                            int e[4];
+#pragma unroll
+                            for (int u = 0; u < 4; ++u) e[u] = cb + j + u < N ? __ldg(ce + j + u) : 0;
+#pragma unroll
+                            for (int u = 0; u < 4; ++u) a[u] = unscale(a[u], ea + e[u]);
+                        }
+                        if (staged) {
+                            const float4 b4 = lds4(slot);
+                            a[0] = __fadd_rn(a[0], b4.x);
+                            a[1] = __fadd_rn(a[1], b4.y);
+                            a[2] = __fadd_rn(a[2], b4.z);
+                            a[3] = __fadd_rn(a[3], b4.w);
+                        }
+                        sts4(slot, a[0], a[1], a[2], a[3]);
+                    }
+                    __syncwarp();
+#pragma unroll 1
+                    for (int i = 0; i < 8; ++i) {
+                        const int rr = 4 * i + (lane >> 3);
+                        const int grow = row0 + rr;
+                        const int col = cb + cc;
+                        const float4 s4 = lds4(sbuf + rr * 128 + (((lane & 7) ^ (rr & 7)) << 4));
+                        if (grow >= M || col >= N) continue;
+                        const bool vq = vec && col + 4 <= N;
+                        const bool gbias = epi.bias && !staged;
+                        float a[4] = {s4.x, s4.y, s4.z, s4.w};
+                        if (gbias) {
+                            const float* q = epi.bias + (int64_t)grow * N + col;
+                            if (vq && bvec) {
+                                const float4 b4 = __ldcs((const float4*)q);
+                                a[0] = __fadd_rn(a[0], b4.x);
+                                a[1] = __fadd_rn(a[1], b4.y);
+                                a[2] = __fadd_rn(a[2], b4.z);
+                                a[3] = __fadd_rn(a[3], b4.w);
+                            } else {
+#pragma unroll
+                                for (int u = 0; u < 4; ++u)
+                                    if (col + u < N) a[u] = __fadd_rn(a[u], q[u]);
+                            }
+                        }
+                        if (epi.act == 1) {
+#pragma unroll
+                            for (int u = 0; u < 4; ++u) a[u] = gelu_lane(a[u]);
+                        }
+                        if constexpr (!F16) {  // the host admits a split output only for N % 32 == 0
+                            if (epi.out_hi) {
+                                float hh[4], ll[4];
+#pragma unroll
+                                for (int u = 0; u < 4; ++u) {
+                                    hh[u] = rna_tf32_dev(a[u]);
+                                    ll[u] = rna_tf32_dev(a[u] - hh[u]);
+                                }
+                                float* oh = epi.out_hi + (int64_t)grow * epi.kp_out + col;
+                                float* ol = epi.out_lo + (int64_t)grow * epi.kp_out + col;
+                                if (vq) {
+                                    *(float4*)oh = make_float4(hh[0], hh[1], hh[2], hh[3]);
+                                    *(float4*)ol = make_float4(ll[0], ll[1], ll[2], ll[3]);
+                                } else {
+#pragma unroll
+                                    for (int u = 0; u < 4; ++u) {
+                                        if (col + u < N) {
+                                            oh[u] = hh[u];
+                                            ol[u] = ll[u];
+                                        }
+                                    }
+                                }
+                            }
+                        }
+                        float* o = r + (int64_t)grow * ldr + col;
+                        if (vq) {
+                            *(float4*)o = make_float4(a[0], a[1], a[2], a[3]);
+                        } else {
+#pragma unroll
+                            for (int u = 0; u < 4; ++u)
+                                if (col + u < N) o[u] = a[u];
+                        }
+                    }
+                    // every lane is done with the slot before the next chunk's bias load refills it
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    __syncwarp();
+                }
+                continue;
+            }
             float* out = tail ? tail_out + ((int64_t)((t - split_from) * kparts + part) * TM + (rowc - mb * TM)) * BN +
                                     (colh - nb * BN)
                               : rb + (int64_t)bt * M * ldr + (int64_t)rowc * ldr + colh;
             const bool vec_u = tail || vec;  // the tail buffer's rows are BN floats, 16-byte aligned
-            int ea = 0;
-            if constexpr (F16) ea = epi.row_exp[(int64_t)bt * M + rowc];
 #pragma unroll
             for (int c = 0; c < HC / 32; ++c) {
                 float* v = sum + c * 32;
                 const int cb = colh + c * 32;
                 const bool full = cb + 32 <= N;
                 const bool fast = full && vec_u && (!F16 || ((((int64_t)bt * N) & 3) == 0));
-                const bool staged = map_ok && full;
-                if (staged) {
-                    if (c > 0 || !staged0) stage_bias(cb);
-                    if (!mbar_wait(&bias_full[ew], bphase, ab, 5)) goto done;
-                    bphase ^= 1;
-                }
                 if (fast) {
-                    // one float4 at a time through unscale, bias, GELU, split and store: short live
-                    // ranges keep the 128-column segment sum in registers without spills
+                    // one float4 at a time through unscale and store: short live ranges keep the
+                    // 128-column segment sum in registers without spills
                     const int* ce = F16 ? epi.col_exp + (int64_t)bt * N + cb : nullptr;
-                    const float* pb = FUSED && epi.bias && !staged ? epi.bias + (int64_t)rowc * N + cb : nullptr;
 #pragma unroll
                     for (int j = 0; j < 32; j += 4) {
                         float a[4] = {v[j], v[j + 1], v[j + 2], v[j + 3]};
@@ -583,55 +696,18 @@ __global__ void __maxnreg__(kLaunchRegs)
                             a[2] = unscale(a[2], ea + e4.z);
                             a[3] = unscale(a[3], ea + e4.w);
                         }
-                        if constexpr (FUSED) {
-                            if (staged || pb) {  // row `lane` of the staged chunk: 16-byte unit j/4, swizzled
-                                const float4 b4 = staged ? *(const float4*)(bbuf + lane * 128 + (((j >> 2) ^ (lane & 7)) << 4))
-                                                         : __ldcs((const float4*)(pb + j));
-                                a[0] = __fadd_rn(a[0], b4.x);
-                                a[1] = __fadd_rn(a[1], b4.y);
-                                a[2] = __fadd_rn(a[2], b4.z);
-                                a[3] = __fadd_rn(a[3], b4.w);
-                            }
-                            if (epi.act == 1) {
-#pragma unroll
-                                for (int u = 0; u < 4; ++u) a[u] = gelu_lane(a[u]);
-                            }
-                            if (!F16 && epi.out_hi && row_ok) {
-                                float4 hh, ll;
-                                hh.x = rna_tf32_dev(a[0]); ll.x = rna_tf32_dev(a[0] - hh.x);
-                                hh.y = rna_tf32_dev(a[1]); ll.y = rna_tf32_dev(a[1] - hh.y);
-                                hh.z = rna_tf32_dev(a[2]); ll.z = rna_tf32_dev(a[2] - hh.z);
-                                hh.w = rna_tf32_dev(a[3]); ll.w = rna_tf32_dev(a[3] - hh.w);
-                                *(float4*)(epi.out_hi + (int64_t)row * epi.kp_out + cb + j) = hh;
-                                *(float4*)(epi.out_lo + (int64_t)row * epi.kp_out + cb + j) = ll;
-                            }
-                        }
                         if (row_ok) *(float4*)(out + c * 32 + j) = make_float4(a[0], a[1], a[2], a[3]);
                     }
-                    if (staged) __syncwarp();  // every lane has read the slot before it is refilled
                     continue;
                 }
-                if (staged) __syncwarp();  // (a staged chunk is always on the fast path: full and vec)
                 if (!row_ok) continue;
-                // ragged edge or unaligned result: element by element, bias from global memory
-                const float* pb = FUSED && epi.bias ? epi.bias + (int64_t)row * N + cb : nullptr;
+                // ragged edge or unaligned result: element by element
                 const int* ce = F16 ? epi.col_exp + (int64_t)bt * N + cb : nullptr;
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
                     if (cb + j >= N) break;
                     float a = v[j];
                     if constexpr (F16) a = unscale(a, ea + ce[j]);
-                    if constexpr (FUSED) {
-                        if (pb) a = __fadd_rn(a, pb[j]);
-                        if (epi.act == 1) a = gelu_lane(a);
-                        if constexpr (!F16) {
-                            if (epi.out_hi && full) {
-                                const float hh = rna_tf32_dev(a);
-                                epi.out_hi[(int64_t)row * epi.kp_out + cb + j] = hh;
-                                epi.out_lo[(int64_t)row * epi.kp_out + cb + j] = rna_tf32_dev(a - hh);
-                            }
-                        }
-                    }
                     out[c * 32 + j] = a;
                 }
             }
