@@ -1033,40 +1033,53 @@ __global__ void __launch_bounds__(256) sum_tail(float* __restrict__ r, const flo
     }
 }
 
-// Column maxima of Y[b][K][N] as f32 bits (|y| compares as an unsigned integer; NaN above inf):
-// a thread per four consecutive columns (one float4 per row) and 32-row chunk, eight rows'
-// loads in flight, one atomicMax per column.
+// Column maxima of Y[b][K][N] as f32 bits (|y| compares as an unsigned integer; NaN above inf).
+// A block covers 128 columns x 128 rows: 32 lanes take four consecutive columns each (one
+// float4 per row, so a warp reads 512 contiguous bytes), 8 warps take every 8th row; the warps'
+// maxima meet in shared memory and one atomicMax per column leaves the block.
+constexpr int kColMaxRows = 128;
 __global__ void __launch_bounds__(256) col_absmax(const float* __restrict__ y, unsigned* __restrict__ cmax, int64_t K,
                                                   int64_t N) {
-    const int64_t n = ((int64_t)blockIdx.x * 256 + threadIdx.x) * 4;
-    if (n >= N) return;
+    __shared__ unsigned part[8][128];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int64_t n = (int64_t)blockIdx.x * 128 + lane * 4;
     y += (int64_t)blockIdx.z * K * N;
     cmax += (int64_t)blockIdx.z * N;
-    const int64_t k0 = (int64_t)blockIdx.y * 32, k1 = k0 + 32 < K ? k0 + 32 : K;
+    const int64_t k0 = (int64_t)blockIdx.y * kColMaxRows, k1 = k0 + kColMaxRows < K ? k0 + kColMaxRows : K;
     const bool vec = (N % 4 == 0) && ((((uintptr_t)y) & 15) == 0);
     unsigned m0 = 0, m1 = 0, m2 = 0, m3 = 0;
-    if (vec) {
-#pragma unroll 8
-        for (int64_t k = k0; k < k1; ++k) {
-            const float4 v = __ldg((const float4*)(y + k * N + n));
-            m0 = max(m0, __float_as_uint(v.x) & 0x7FFFFFFFu);
-            m1 = max(m1, __float_as_uint(v.y) & 0x7FFFFFFFu);
-            m2 = max(m2, __float_as_uint(v.z) & 0x7FFFFFFFu);
-            m3 = max(m3, __float_as_uint(v.w) & 0x7FFFFFFFu);
-        }
-    } else {
-        for (int64_t k = k0; k < k1; ++k) {
-            const float* p = y + k * N + n;
-            m0 = max(m0, __float_as_uint(__ldg(p)) & 0x7FFFFFFFu);
-            if (n + 1 < N) m1 = max(m1, __float_as_uint(__ldg(p + 1)) & 0x7FFFFFFFu);
-            if (n + 2 < N) m2 = max(m2, __float_as_uint(__ldg(p + 2)) & 0x7FFFFFFFu);
-            if (n + 3 < N) m3 = max(m3, __float_as_uint(__ldg(p + 3)) & 0x7FFFFFFFu);
+    if (n < N) {
+        if (vec) {
+#pragma unroll 4
+            for (int64_t k = k0 + w; k < k1; k += 8) {
+                const float4 v = __ldg((const float4*)(y + k * N + n));
+                m0 = max(m0, __float_as_uint(v.x) & 0x7FFFFFFFu);
+                m1 = max(m1, __float_as_uint(v.y) & 0x7FFFFFFFu);
+                m2 = max(m2, __float_as_uint(v.z) & 0x7FFFFFFFu);
+                m3 = max(m3, __float_as_uint(v.w) & 0x7FFFFFFFu);
+            }
+        } else {
+            for (int64_t k = k0 + w; k < k1; k += 8) {
+                const float* p = y + k * N + n;
+                m0 = max(m0, __float_as_uint(__ldg(p)) & 0x7FFFFFFFu);
+                if (n + 1 < N) m1 = max(m1, __float_as_uint(__ldg(p + 1)) & 0x7FFFFFFFu);
+                if (n + 2 < N) m2 = max(m2, __float_as_uint(__ldg(p + 2)) & 0x7FFFFFFFu);
+                if (n + 3 < N) m3 = max(m3, __float_as_uint(__ldg(p + 3)) & 0x7FFFFFFFu);
+            }
         }
     }
-    atomicMax(cmax + n, m0);
-    if (n + 1 < N) atomicMax(cmax + n + 1, m1);
-    if (n + 2 < N) atomicMax(cmax + n + 2, m2);
-    if (n + 3 < N) atomicMax(cmax + n + 3, m3);
+    part[w][lane * 4] = m0;
+    part[w][lane * 4 + 1] = m1;
+    part[w][lane * 4 + 2] = m2;
+    part[w][lane * 4 + 3] = m3;
+    __syncthreads();
+    if (threadIdx.x < 128) {
+        const int64_t c = (int64_t)blockIdx.x * 128 + threadIdx.x;
+        unsigned m = part[0][threadIdx.x];
+#pragma unroll
+        for (int i = 1; i < 8; ++i) m = max(m, part[i][threadIdx.x]);
+        if (c < N) atomicMax(cmax + c, m);
+    }
 }
 
 // Y[K][N] -> hi/lo transposed [N][Kp] f16 through a 64 (k) x 64 (n) shared tile, scaled per
@@ -1434,7 +1447,7 @@ static int launch_tc(float* r, const float* x, const float* y, int64_t B, int64_
     if (f16) {
         cudaError_t e = cudaMemsetAsync(cmax, 0, (size_t)(B * N) * 4, st);
         if (e != cudaSuccess) return (int)e;
-        dim3 gm((unsigned)((N + 1023) / 1024), (unsigned)((K + 31) / 32), (unsigned)B);
+        dim3 gm((unsigned)((N + 127) / 128), (unsigned)((K + kColMaxRows - 1) / kColMaxRows), (unsigned)B);
         col_absmax<<<gm, 256, 0, st>>>(y, cmax, K, N);
         dim3 grid((unsigned)((N + 63) / 64), (unsigned)((l.kp + 63) / 64), (unsigned)B);
         split_cols_t_f16<<<grid, 256, 0, st>>>(y, cmax, (__half*)yhi, (__half*)ylo, cexp, K, N, l.kp);
