@@ -132,7 +132,8 @@ MAG_CUDA_EXPORT int mag_cuda_reduce_rows_f32(mag_compute_device_t* dvc, int op, 
 MAG_CUDA_EXPORT int mag_cuda_softmax_rows_f32(mag_compute_device_t* dvc, float* r, const float* x, int64_t rows,
                                               int64_t cols);
 /* R[b] = X[b] Y[b] for b < batch, each M x K times K x N (tensor cores for large products,
- * the bit-exact CUDA-core kernel otherwise or under matmul mode 1). */
+ * the bit-exact CUDA-core kernel otherwise or under matmul mode 1).  Batches longer than 65535
+ * products run as consecutive slices of 65535. */
 MAG_CUDA_EXPORT int mag_cuda_matmul_batched_f32(mag_compute_device_t* dvc, float* r, const float* x,
                                                 const float* y, int64_t batch, int64_t M, int64_t K, int64_t N);
 

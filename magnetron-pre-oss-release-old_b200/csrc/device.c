@@ -1100,13 +1100,12 @@ int mag_cuda_img_draw_text(mag_compute_device_t* dvc, mag_tensor_t* t, int32_t x
     return rc;
 }
 
-int mag_cuda_matmul_batched_f32(mag_compute_device_t* dvc, float* r, const float* x, const float* y, int64_t batch,
-                                int64_t M, int64_t K, int64_t N) {
-    if (batch < 0 || M < 0 || K < 0 || N < 0) return MAG_CUDA_E_INVALID;
-    mcu_device* d = dev_of(dvc);
-    ext_in(d, x);
-    ext_in(d, y);
-    ext_out(d, r, (size_t)(batch * M * N * 4));
+/* The batched kernels index the batch with a grid dimension of at most 65535 blocks, so longer
+ * batches run as consecutive slices of that many products. */
+#define MCU_BATCH_SLICE 65535
+
+static int matmul_batched_slice(mcu_device* d, float* r, const float* x, const float* y, int64_t batch, int64_t M,
+                                int64_t K, int64_t N) {
     int rc;
     if (d->matmul_mode != 1 && mcu_matmul_tc_supported() && M >= 128 && N >= 64 && K >= 32 &&
         (double)batch * M * N * K >= 1.0e9) {
@@ -1116,6 +1115,21 @@ int mag_cuda_matmul_batched_f32(mag_compute_device_t* dvc, float* r, const float
     } else {
         rc = mcu_launch_matmul_exact(r, x, y, batch, M, K, N, N, 0, d->stream);
         if (!rc) mcu_count_launches(1);
+    }
+    return rc;
+}
+
+int mag_cuda_matmul_batched_f32(mag_compute_device_t* dvc, float* r, const float* x, const float* y, int64_t batch,
+                                int64_t M, int64_t K, int64_t N) {
+    if (batch < 0 || M < 0 || K < 0 || N < 0) return MAG_CUDA_E_INVALID;
+    mcu_device* d = dev_of(dvc);
+    ext_in(d, x);
+    ext_in(d, y);
+    ext_out(d, r, (size_t)(batch * M * N * 4));
+    int rc = 0;
+    for (int64_t b0 = 0; b0 < batch && !rc; b0 += MCU_BATCH_SLICE) {
+        const int64_t nb = batch - b0 < MCU_BATCH_SLICE ? batch - b0 : MCU_BATCH_SLICE;
+        rc = matmul_batched_slice(d, r + b0 * M * N, x + b0 * M * K, y + b0 * K * N, nb, M, K, N);
     }
     return rc;
 }

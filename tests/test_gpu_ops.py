@@ -465,6 +465,40 @@ def test_matmul_batched_tensor_core(split):
                             y[i * k * n:(i + 1) * k * n], m, k, n), i
 
 
+def test_matmul_batched_longer_than_a_grid_dimension():
+    """Batches of more than 65535 products run as consecutive slices (the batch is a grid
+    dimension of the kernels): the bit-exact path over the whole batch, and the tensor-core
+    path on the products either side of each slice boundary."""
+    dev = device()
+    o = oracle()
+    b, m, k, n = 65540, 3, 4, 5
+    s = o.stream(7300)
+    x = s.uniform(b * m * k, -1, 1)
+    y = s.uniform(b * k * n, -1, 1)
+    tx, ty, tr = dev.tensor((b * m * k,)), dev.tensor((b * k * n,)), dev.tensor((b * m * n,))
+    tx.write(x)
+    ty.write(y)
+    MB.check(dev.L.mag_cuda_matmul_batched_f32(dev.p, tr.data_ptr, tx.data_ptr, ty.data_ptr, b, m, k, n), "bmm")
+    assert dev.L.mag_cuda_synchronize(dev.p) == 0
+    assert bits_equal(_raw(dev, tr.data_ptr, b * m * n), o.matmul_batched(x, y, b, m, k, n)).all()
+    for t in (tx, ty, tr):
+        t.free()
+    b, m, k, n = 65537, 128, 32, 64  # 1.7e10 multiply-adds: the tensor-core path
+    tx, ty, tr = dev.tensor((b * m * k,)), dev.tensor((b * k * n,)), dev.tensor((b * m * n,))
+    g = MB.Pcg(0x5EED7301)
+    dev.fill_random_uniform(tx, -1.0, 1.0, g)
+    dev.fill_random_uniform(ty, -1.0, 1.0, g)
+    MB.check(dev.L.mag_cuda_matmul_batched_f32(dev.p, tr.data_ptr, tx.data_ptr, ty.data_ptr, b, m, k, n), "bmm")
+    assert dev.L.mag_cuda_synchronize(dev.p) == 0
+    for i in (0, 65533, 65534, 65535, 65536):
+        xi = _raw(dev, tx.data_ptr + 4 * i * m * k, m * k)
+        yi = _raw(dev, ty.data_ptr + 4 * i * k * n, k * n)
+        ri = _raw(dev, tr.data_ptr + 4 * i * m * n, m * n)
+        assert _normwise_ok(ri, xi, yi, m, k, n), i
+    for t in (tx, ty, tr):
+        t.free()
+
+
 def test_matmul_f16_magnitudes_differ_within_rows():
     """Rows whose 256-element stretches lie up to 2^80 apart, a stretch 2^-130 below the rest
     of its row, a zero stretch and a ragged K: the f16 split stays within 1e-5 of |X||Y|."""
