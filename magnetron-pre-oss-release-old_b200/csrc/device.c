@@ -389,7 +389,8 @@ enum { MM_EXACT, MM_SKINNY, MM_TC };
 
 static int matmul_path(mcu_device* d, int64_t M, int64_t K, int64_t N) {
     if (d->matmul_mode == 1) return MM_EXACT;
-    int tc_ok = mcu_matmul_tc_supported() && M >= 32 && N >= 64 && K >= 32;
+    int tc_ok = mcu_matmul_tc_supported() && M >= 32 && N >= 64 && K >= 32 && K <= MCU_TC_MAX_K &&
+                M < ((int64_t)1 << 31) && N < ((int64_t)1 << 31);
     if (d->matmul_mode == 2 && tc_ok) return MM_TC;
     if (M < 32 && K * N >= ((int64_t)1 << 20)) return MM_SKINNY; /* HBM-bound: Y is read once */
     if (tc_ok && (double)M * (double)N * (double)K >= 1.0e9) return MM_TC; /* split K fills the GPU */
@@ -501,7 +502,7 @@ static int exec_node(mcu_device* d, mag_tensor_t* r) {
                 if (!rc) mcu_count_launches(mcu_matmul_tc_kernels(M, K, N, d->tc_f16, 0));
             } else {
                 rc = mcu_launch_matmul_exact(fptr(r), px, py, 1, M, K, N, r_ld, accumulate, st);
-                if (!rc) mcu_count_launches(1);
+                if (!rc) mcu_count_launches(mcu_matmul_exact_kernels(1, M));
             }
             return rc;
         }
@@ -814,7 +815,7 @@ int mag_cuda_matmul_f32(mag_compute_device_t* dvc, float* r, const float* x, con
         if (!rc) mcu_count_launches(mcu_matmul_tc_kernels(M, K, N, d->tc_f16, 0));
     } else {
         rc = mcu_launch_matmul_exact(r, x, y, 1, M, K, N, N, 0, d->stream);
-        if (!rc) mcu_count_launches(1);
+        if (!rc) mcu_count_launches(mcu_matmul_exact_kernels(1, M));
     }
     return rc;
 }
@@ -1107,14 +1108,14 @@ int mag_cuda_img_draw_text(mag_compute_device_t* dvc, mag_tensor_t* t, int32_t x
 static int matmul_batched_slice(mcu_device* d, float* r, const float* x, const float* y, int64_t batch, int64_t M,
                                 int64_t K, int64_t N) {
     int rc;
-    if (d->matmul_mode != 1 && mcu_matmul_tc_supported() && M >= 128 && N >= 64 && K >= 32 &&
-        (double)batch * M * N * K >= 1.0e9) {
+    if (d->matmul_mode != 1 && mcu_matmul_tc_supported() && M >= 128 && N >= 64 && K >= 32 && K <= MCU_TC_MAX_K &&
+        batch * M < ((int64_t)1 << 31) && batch * N < ((int64_t)1 << 31) && (double)batch * M * N * K >= 1.0e9) {
         void* scratch = scratch_get(d, mcu_matmul_tc_batched_scratch_bytes(batch, M, K, N));
         rc = mcu_launch_matmul_tc_batched(r, x, y, batch, M, K, N, scratch, d->d_status, d->stream, d->tc_f16);
         if (!rc) mcu_count_launches(mcu_matmul_tc_batched_kernels(batch, M, K, N, d->tc_f16));
     } else {
         rc = mcu_launch_matmul_exact(r, x, y, batch, M, K, N, N, 0, d->stream);
-        if (!rc) mcu_count_launches(1);
+        if (!rc) mcu_count_launches(mcu_matmul_exact_kernels(batch, M));
     }
     return rc;
 }

@@ -228,9 +228,25 @@ int64_t skinny_kc(int64_t K, int64_t slices) {
 
 }  // namespace
 
+// Row tiles are a grid dimension (at most 65535 tiles of at least 16 rows): a single product with
+// more rows runs as consecutive slices of kExactRowSlice rows.
+constexpr int64_t kExactRowSlice = 65535 * 16;
+
+extern "C" int mcu_matmul_exact_kernels(int64_t batch, int64_t M) {
+    return batch == 1 && M > kExactRowSlice ? (int)((M + kExactRowSlice - 1) / kExactRowSlice) : 1;
+}
+
 extern "C" int mcu_launch_matmul_exact(float* r, const float* x, const float* y, int64_t batch, int64_t M,
                                        int64_t K, int64_t N, int64_t r_ld, int accumulate, cudaStream_t st) {
     if (batch <= 0 || M <= 0 || N <= 0) return (int)cudaSuccess;
+    if (batch == 1 && M > kExactRowSlice) {
+        for (int64_t m0 = 0; m0 < M; m0 += kExactRowSlice) {
+            const int64_t mr = M - m0 < kExactRowSlice ? M - m0 : kExactRowSlice;
+            const int rc = mcu_launch_matmul_exact(r + m0 * r_ld, x + m0 * K, y, 1, mr, K, N, r_ld, accumulate, st);
+            if (rc) return rc;
+        }
+        return (int)cudaSuccess;
+    }
     if (batch >= 65536 || (M + 15) / 16 >= 65536) return (int)cudaErrorInvalidValue;
     const int64_t target = 2 * (int64_t)sm_count();
     auto blocks = [&](int64_t bm, int64_t bn) { return batch * ((M + bm - 1) / bm) * ((N + bn - 1) / bn); };

@@ -1409,7 +1409,7 @@ extern "C" int mcu_launch_matmul_tc_batched(float* r, const float* x, const floa
 static int launch_tc(float* r, const float* x, const float* y, int64_t B, int64_t M, int64_t K, int64_t N,
                      void* scratch, int* status, cudaStream_t st, const mcu_tc_epilogue* ep, int f16) {
     if (B <= 0 || M <= 0 || N <= 0) return (int)cudaSuccess;
-    if (B * M >= (1ll << 31) || B * N >= (1ll << 31) || K >= (1ll << 21) || !scratch) return (int)cudaErrorInvalidValue;
+    if (B * M >= (1ll << 31) || B * N >= (1ll << 31) || K > MCU_TC_MAX_K || !scratch) return (int)cudaErrorInvalidValue;
     if (B > 1 && ep) return (int)cudaErrorInvalidValue;
     const Layout l = layout(B, M, K, N, f16 != 0);
     char* base = (char*)scratch;

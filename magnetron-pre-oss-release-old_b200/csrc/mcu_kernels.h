@@ -67,6 +67,11 @@ int mcu_launch_img_draw_text(float* img, int32_t w, int32_t h, const int32_t* gl
  * summed k = 0..K-1 in order with separately rounded multiply and add. */
 int mcu_launch_matmul_exact(float* r, const float* x, const float* y, int64_t batch, int64_t M, int64_t K,
                             int64_t N, int64_t r_ld, int accumulate, cudaStream_t st);
+/* Kernels one exact product launches: a single product of more than 1048560 rows runs in slices. */
+int mcu_matmul_exact_kernels(int64_t batch, int64_t M);
+/* Largest K the tensor-core product takes (its padded K indexes a grid dimension); beyond it the
+ * CUDA-core paths, which have no K limit, run the product. */
+#define MCU_TC_MAX_K (((int64_t)1 << 21) - 32)
 
 size_t mcu_matmul_skinny_scratch_bytes(int64_t M, int64_t K, int64_t N);
 int mcu_launch_matmul_skinny(float* r, const float* x, const float* y, int64_t M, int64_t K, int64_t N,

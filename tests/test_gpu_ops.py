@@ -499,6 +499,30 @@ def test_matmul_batched_longer_than_a_grid_dimension():
         t.free()
 
 
+def test_matmul_more_rows_than_a_grid_dimension():
+    """A product of 1048600 rows (more than 65535 row tiles of 16) on the bit-exact path runs
+    as row slices and equals the oracle bit for bit."""
+    dev, o = device(), oracle()
+    m, k, n = 1048600, 8, 8
+    s = o.stream(7400)
+    x = s.uniform(m * k, -1, 1)
+    y = s.uniform(k * n, -1, 1)
+    got, _, _ = run_op(dev, "MATMUL", [x, y], [(m, k), (k, n)])
+    assert bits_equal(got, o.matmul(x, y, m, k, n)).all()
+
+
+def test_matmul_k_beyond_the_tensor_core_limit():
+    """K = 2^21 is past the tensor-core product's limit: the product takes a CUDA-core path
+    and stays within the normwise tolerance."""
+    dev, o = device(), oracle()
+    m, k, n = 32, 1 << 21, 64
+    s = o.stream(7500)
+    x = s.uniform(m * k, -1, 1)
+    y = s.uniform(k * n, -1, 1)
+    got, _, _ = run_op(dev, "MATMUL", [x, y], [(m, k), (k, n)])
+    assert _normwise_ok(got, x, y, m, k, n)
+
+
 def test_matmul_f16_magnitudes_differ_within_rows():
     """Rows whose 256-element stretches lie up to 2^80 apart, a stretch 2^-130 below the rest
     of its row, a zero stretch and a ragged K: the f16 split stays within 1e-5 of |X||Y|."""
