@@ -405,11 +405,14 @@ def _build_mlp(dev, rows, dims, inplace_gelu=True):
 
 @pytest.mark.parametrize("split", SPLITS)
 @pytest.mark.parametrize("inplace,rows,dims", [(True, 256, [512, 384, 256, 96]), (False, 256, [512, 384, 256, 96]),
-                                               (True, 4096, [512, 1024, 512, 96])])
+                                               (True, 4096, [512, 1024, 512, 96]),
+                                               (True, 16384, [500, 300, 130, 70])])
 def test_fused_graph_matches_unfused_bitwise(inplace, rows, dims, split):
     """Dense layers fused into the GEMM epilogue give the same bits as the op-by-op graph,
     including the next product's operand split written by the epilogue (256 rows: split-K
-    products, the split runs after the part sum; 4096 rows: one part, the epilogue writes it)."""
+    products, the split runs after the part sum; 4096 rows: one part, the epilogue writes it;
+    16384 rows with ragged widths: one part, a partly filled last 32-column chunk (300, 70) and
+    rows that are not 16-byte aligned, with the bias read from global memory (130))."""
     dev = device()
     _split(dev, split)
     o = oracle()
