@@ -476,7 +476,7 @@ def run_ours(args):
         "gpu_launches": launches_timed,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": split_peak, "unit": "TFLOP/s",
                      "frac": achieved / split_peak if split_peak else None,
-                     "traffic": (0.929e9 + 0.121e9) * rows / 8192,
+                     "traffic": (0.946e9 + 0.120e9) * rows / 8192,
                      "traffic_note": "DRAM bytes per hidden-layer GEMM launch: ncu capture at 8192 rows "
                                      "(profiles/gemm_3xfp16_fused_layer_8192x4096.md) scaled by rows",
                      "kernel": "MATMUL op (per-op CUDA events inside the replayed graph)",
