@@ -673,13 +673,46 @@ def run_image(args):
     print(json.dumps(out), flush=True)
 
 
+def build_mlp2(dev, torch, batch=256, d_in=784, d_hid=256, d_out=10, seed=12):
+    """The two-layer MLP forward of the reference's MNIST-shaped example: X (batch x 784) U(0,1),
+    Glorot-uniform W1 (784 x 256) and W2 (256 x 10), a zero 1-D bias of 256 (tiling broadcast)
+    and a zero full-shape (batch x 10) bias, MATMUL -> ADD -> SIGMOID -> MATMUL -> ADD as one
+    recorded graph, then the normalised row softmax over the 10 logits.  Returns the forward
+    (graph replay + softmax, on the device's stream), the probability tensor and every tensor
+    to free."""
+    import mag_b200 as MB
+    g = torch.Generator().manual_seed(seed)
+    lim1, lim2 = (6.0 / (d_in + d_hid)) ** 0.5, (6.0 / (d_hid + d_out)) ** 0.5
+    X, W1, W2 = dev.tensor((batch, d_in)), dev.tensor((d_in, d_hid)), dev.tensor((d_hid, d_out))
+    B1, B2, P = dev.tensor((d_hid,)), dev.tensor((batch, d_out)), dev.tensor((batch * d_out,))
+    X.write(torch.rand(batch * d_in, generator=g).numpy())
+    W1.write(((torch.rand(d_in * d_hid, generator=g) * 2 - 1) * lim1).numpy())
+    W2.write(((torch.rand(d_hid * d_out, generator=g) * 2 - 1) * lim2).numpy())
+    dev.eager = False
+    try:
+        h = dev.op("SIGMOID", dev.op("ADD", dev.op("MATMUL", X, W1), B1), inplace=True)
+        z = dev.op("ADD", dev.op("MATMUL", h, W2), B2)
+    finally:
+        dev.eager = True
+
+    def fwd():
+        rc = dev.L.mag_cuda_graph_exec(dev.p, z.ptr)
+        return rc or dev.L.mag_cuda_softmax_rows_f32(dev.p, P.data_ptr, z.data_ptr, batch, d_out)
+    return fwd, P, [X, W1, W2, B1, B2, P]
+
+
 def run_case(args):
     """One kernel family, a few launches, for profilers: `--case gemm|add|sigmoid|sum|softmax`."""
     import torch
     import mag_b200 as MB
     dev = MB.Device()
     n = args.size
-    if args.case == "layer":
+    if args.case == "mlp2":
+        # the two-layer MLP forward, batch --size (default 256): graph replay + row softmax
+        rows = n
+        fn, _, _ = build_mlp2(dev, torch, batch=rows)
+        work, unit = float(rows), "samples/s"
+    elif args.case == "layer":
         # two dense layers of the MLP (rows = --size, 4096 features), fused graph:
         # layer 1 = GEMM + bias + GELU + operand split, layer 2 reads the split
         rows = n
@@ -1009,6 +1042,14 @@ def run_sweep_full(args):
         2.0 * bt * mm ** 3 / 1e12, "TFLOP/s", tf)
     a.free()
     c_.free()
+    # ---- config 1: two-layer MLP forward, batch 256 (launch-bound: graph replay of the five
+    # recorded ops, then the row softmax)
+    fwd, _, keep = build_mlp2(dev, torch)
+    ms = timeit(fwd, 200)
+    rec("mlp", "two-layer MLP fwd, batch 256 (784-256-10, sigmoid, row softmax; graph replay)", ms, 256.0,
+        "samples/s", None)
+    for t in keep:
+        t.free()
     # ---- reference CPU, single thread, on this host
     cpu = []
     if not args.no_cpu_baseline:
@@ -1050,6 +1091,28 @@ def run_sweep_full(args):
             R.write(tb, v[:m * m])
             dt = cpu_time(lambda: R.op("MATMUL", ta, tb), reps=1)
             cpu.append({"case": "MATMUL 1024^3", "rate": 2.0 * m ** 3 / dt / 1e12, "unit": "TFLOP/s"})
+            # the two-layer MLP forward through the reference's ops (SOFTMAX is its elementwise
+            # exp; the 256 x 10 row normalisation is left out of this CPU figure)
+            tx1, tw1, tw2 = R.tensor_nd((256, 784)), R.tensor_nd((784, 256)), R.tensor_nd((256, 10))
+            tb1, tb2 = R.tensor_nd((256,)), R.tensor_nd((256, 10))
+            R.write(tx1, np.abs(v[:256 * 784]))
+            R.write(tw1, v[:784 * 256] * 0.07)
+            R.write(tw2, v[:2560] * 0.15)
+            R.write(tb1, np.zeros(256, np.float32))
+            R.write(tb2, np.zeros(2560, np.float32))
+
+            def mlp2_ref():
+                a1 = R.op("MATMUL", tx1, tw1)
+                a2 = R.op("ADD", a1, tb1)
+                a3 = R.op("SIGMOID", a2)
+                a4 = R.op("MATMUL", a3, tw2)
+                a5 = R.op("ADD", a4, tb2)
+                out = R.op("SOFTMAX", a5)
+                for t in (a1, a2, a3, a4, a5):
+                    R.free(t)
+                return out
+            dt = cpu_time(mlp2_ref, reps=5)
+            cpu.append({"case": "two-layer MLP fwd, batch 256", "rate": 256.0 / dt, "unit": "samples/s"})
             R.close()
             for c in cpu:
                 c["rate"] = round(c["rate"], 4)
@@ -1071,7 +1134,7 @@ def main():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--case", default=None, choices=["gemm", "layer", "add", "sigmoid", "sum", "softmax", "softmax1k", "softmax256k", "skinny", "tile", "bcast2", "bcast2s", "batched",
-                                                      "fill_uniform", "fill_normal", "fill_const", "storage", "image", "sharded"],
+                                                      "fill_uniform", "fill_normal", "fill_const", "storage", "image", "sharded", "mlp2"],
                     help="run one kernel family for a profiler instead of the benchmark")
     ap.add_argument("--size", type=int, default=None)
     ap.add_argument("--sweep-full", action="store_true", help="measure every other BASELINE configuration")
@@ -1081,7 +1144,7 @@ def main():
         run_sweep_full(args)
         return
     if args.case:
-        args.size = args.size or (8192 if args.case in ("gemm", "layer") else 1 << 28)
+        args.size = args.size or (8192 if args.case in ("gemm", "layer") else 256 if args.case == "mlp2" else 1 << 28)
         {"storage": run_storage, "image": run_image, "sharded": run_sharded}.get(args.case, run_case)(args)
         return
     if args.warmup < 3:

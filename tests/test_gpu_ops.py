@@ -575,3 +575,45 @@ def test_matmul_f16_split_scaling_extremes():
     assert dev.L.mag_cuda_synchronize(dev.p) == 0
     assert np.all(got.reshape(m, n)[5] == 0) and np.all(got.reshape(m, n)[:, 9] == 0)
     assert _normwise_ok(got, x, y, m, k, n)
+
+
+def test_two_layer_mlp_forward_batch_256():
+    """The two-layer MLP of the reference's MNIST-shaped example at its batch of 256, recorded
+    as one graph (MATMUL -> ADD of a 1-D bias by tiling broadcast -> SIGMOID -> MATMUL -> ADD of
+    a full-shape bias) and replayed twice: the logits equal the oracle's chain of the same ops
+    bit for bit, and the normalised row softmax is within 1e-6 of the oracle's."""
+    dev, o = device(), oracle()
+    b, d, h, c = 256, 784, 256, 10
+    s = o.stream(0x5EED0001)
+    lim1, lim2 = (6.0 / (d + h)) ** 0.5, (6.0 / (h + c)) ** 0.5
+    x = s.uniform(b * d, 0.0, 1.0)
+    w1 = s.uniform(d * h, -lim1, lim1)
+    w2 = s.uniform(h * c, -lim2, lim2)
+    b1 = s.uniform(h, -0.1, 0.1)
+    b2 = s.uniform(b * c, -0.1, 0.1)
+    tx, tw1, tw2, tb1, tb2 = (dev.tensor((b, d)), dev.tensor((d, h)), dev.tensor((h, c)), dev.tensor((h,)),
+                              dev.tensor((b, c)))
+    for t, a in ((tx, x), (tw1, w1), (tw2, w2), (tb1, b1), (tb2, b2)):
+        t.write(a)
+    dev.eager = False
+    try:
+        hid = dev.op("SIGMOID", dev.op("ADD", dev.op("MATMUL", tx, tw1), tb1), inplace=True)
+        z = dev.op("ADD", dev.op("MATMUL", hid, tw2), tb2)
+    finally:
+        dev.eager = True
+    p = dev.tensor((b * c,))
+    a = o.matmul(x, w1, b, d, h)
+    a = o.binary("ADD", a, pad6((b, h)), b1, pad6((h,)))
+    a = o.unary("SIGMOID", a, pad6((b, h)))
+    a = o.matmul(a, w2, b, h, c)
+    logits = o.binary("ADD", a, pad6((b, c)), b2, pad6((b, c)))
+    want = o.softmax_rows(logits, b, c)
+    try:
+        for _ in range(2):
+            dev.graph_exec(z)
+            MB.check(dev.L.mag_cuda_softmax_rows_f32(dev.p, p.data_ptr, z.data_ptr, b, c), "softmax")
+            assert bits_equal(z.read(), logits).all()
+            got = p.read()
+            assert np.all(np.abs(got - want) <= 1e-6 * np.abs(want)), float(np.abs(got - want).max())
+    finally:
+        dev.graph_release(z)
