@@ -35,14 +35,27 @@ int sm_count() {
     return n;
 }
 
-// BM x BN output tile per CTA, TM x TN per thread, BK-deep shared stages.
-template <int BM, int BN, int TM, int TN, int BK>
+__device__ __forceinline__ void cp_async4(float* dst, const float* src, bool valid) {
+    // 4-byte asynchronous copy to shared memory; an invalid element is zero-filled (no bytes read)
+    const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(d), "l"(src), "r"(valid ? 4 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// BM x BN output tile per CTA, TM x TN per thread, BK-deep chunks of K in an S-stage ring filled
+// by cp.async: chunk c + S - 1 is in flight while chunk c is consumed, so small tiles (whose
+// per-chunk arithmetic is short) no longer wait a full memory latency per chunk.  Each thread
+// still adds its products in k order, separately rounded, over the valid k only.
+template <int BM, int BN, int TM, int TN, int BK, int S>
 __global__ void __launch_bounds__(kThreads) matmul_exact(float* __restrict__ r, const float* __restrict__ x,
                                                          const float* __restrict__ y, int64_t M, int64_t K,
                                                          int64_t N, int64_t r_ld, int accumulate) {
     static_assert((BM / TM) * (BN / TN) == kThreads, "thread tiling");
-    __shared__ float As[BK][BM + 1];
-    __shared__ float Bs[BK][BN];
+    static_assert(S >= 2, "a ring of at least two stages");
+    __shared__ float As[S][BK][BM + 1];
+    __shared__ float Bs[S][BK][BN];
     const int64_t b = blockIdx.z;
     x += b * M * K;
     y += b * K * N;
@@ -59,32 +72,49 @@ __global__ void __launch_bounds__(kThreads) matmul_exact(float* __restrict__ r, 
             int64_t gi = m0 + ty * TM + i, gj = n0 + tx * TN + j;
             acc[i][j] = (accumulate && gi < M && gj < N) ? r[gi * r_ld + gj] : 0.0f;
         }
-    for (int64_t k0 = 0; k0 < K; k0 += BK) {
+    const int64_t nk = (K + BK - 1) / BK;
+    auto issue = [&](int64_t c) {  // chunk c into stage c % S
+        const int st = (int)(c % S);
+        const int64_t k0 = c * BK;
         for (int t = threadIdx.x; t < BM * BK; t += kThreads) {
-            int mi = t / BK, ki = t % BK;
-            int64_t gm = m0 + mi, gk = k0 + ki;
-            As[ki][mi] = (gm < M && gk < K) ? x[gm * K + gk] : 0.0f;
+            const int mi = t / BK, ki = t % BK;
+            const int64_t gm = m0 + mi, gk = k0 + ki;
+            const bool ok = gm < M && gk < K;
+            cp_async4(&As[st][ki][mi], ok ? x + gm * K + gk : x, ok);
         }
         for (int t = threadIdx.x; t < BN * BK; t += kThreads) {
-            int ki = t / BN, ni = t % BN;
-            int64_t gk = k0 + ki, gn = n0 + ni;
-            Bs[ki][ni] = (gk < K && gn < N) ? y[gk * N + gn] : 0.0f;
+            const int ki = t / BN, ni = t % BN;
+            const int64_t gk = k0 + ki, gn = n0 + ni;
+            const bool ok = gk < K && gn < N;
+            cp_async4(&Bs[st][ki][ni], ok ? y + gk * N + gn : y, ok);
         }
-        __syncthreads();
+    };
+#pragma unroll
+    for (int c = 0; c < S - 1; ++c) {  // one commit group per chunk, empty past the last
+        if (c < nk) issue(c);
+        cp_async_commit();
+    }
+    for (int64_t c = 0; c < nk; ++c) {
+        cp_async_wait<S - 2>();  // this thread's copies of chunk c have landed
+        __syncthreads();         // everyone's have, and everyone is done with chunk c - 1's stage
+        if (c + S - 1 < nk) issue(c + S - 1);
+        cp_async_commit();
+        const int st = (int)(c % S);
+        const int64_t k0 = c * BK;
         const int kk_end = (int)((K - k0) < BK ? (K - k0) : BK);
         for (int kk = 0; kk < kk_end; ++kk) {
             float a[TM], bv[TN];
 #pragma unroll
-            for (int i = 0; i < TM; ++i) a[i] = As[kk][ty * TM + i];
+            for (int i = 0; i < TM; ++i) a[i] = As[st][kk][ty * TM + i];
 #pragma unroll
-            for (int j = 0; j < TN; ++j) bv[j] = Bs[kk][tx * TN + j];
+            for (int j = 0; j < TN; ++j) bv[j] = Bs[st][kk][tx * TN + j];
 #pragma unroll
             for (int i = 0; i < TM; ++i)
 #pragma unroll
                 for (int j = 0; j < TN; ++j) acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(a[i], bv[j]));
         }
-        __syncthreads();
     }
+    cp_async_wait<0>();
 #pragma unroll
     for (int i = 0; i < TM; ++i)
 #pragma unroll
@@ -94,11 +124,11 @@ __global__ void __launch_bounds__(kThreads) matmul_exact(float* __restrict__ r, 
         }
 }
 
-template <int BM, int BN, int TM, int TN>
+template <int BM, int BN, int TM, int TN, int BK, int S>
 cudaError_t launch_exact(float* r, const float* x, const float* y, int64_t batch, int64_t M, int64_t K, int64_t N,
                          int64_t r_ld, int accumulate, cudaStream_t st) {
     dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + BM - 1) / BM), (unsigned)batch);
-    matmul_exact<BM, BN, TM, TN, 16><<<grid, kThreads, 0, st>>>(r, x, y, M, K, N, r_ld, accumulate);
+    matmul_exact<BM, BN, TM, TN, BK, S><<<grid, kThreads, 0, st>>>(r, x, y, M, K, N, r_ld, accumulate);
     return cudaGetLastError();
 }
 
@@ -251,10 +281,10 @@ extern "C" int mcu_launch_matmul_exact(float* r, const float* x, const float* y,
     const int64_t target = 2 * (int64_t)sm_count();
     auto blocks = [&](int64_t bm, int64_t bn) { return batch * ((M + bm - 1) / bm) * ((N + bn - 1) / bn); };
     cudaError_t e;
-    if (blocks(128, 128) >= target) e = launch_exact<128, 128, 8, 8>(r, x, y, batch, M, K, N, r_ld, accumulate, st);
-    else if (blocks(64, 64) >= target) e = launch_exact<64, 64, 4, 4>(r, x, y, batch, M, K, N, r_ld, accumulate, st);
-    else if (blocks(32, 32) >= target / 2) e = launch_exact<32, 32, 2, 2>(r, x, y, batch, M, K, N, r_ld, accumulate, st);
-    else e = launch_exact<16, 16, 1, 1>(r, x, y, batch, M, K, N, r_ld, accumulate, st);
+    if (blocks(128, 128) >= target) e = launch_exact<128, 128, 8, 8, 16, 2>(r, x, y, batch, M, K, N, r_ld, accumulate, st);
+    else if (blocks(64, 64) >= target) e = launch_exact<64, 64, 4, 4, 16, 3>(r, x, y, batch, M, K, N, r_ld, accumulate, st);
+    else if (blocks(32, 32) >= target / 2) e = launch_exact<32, 32, 2, 2, 32, 4>(r, x, y, batch, M, K, N, r_ld, accumulate, st);
+    else e = launch_exact<16, 16, 1, 1, 64, 4>(r, x, y, batch, M, K, N, r_ld, accumulate, st);
     return (int)e;
 }
 
