@@ -101,8 +101,7 @@ __global__ void __launch_bounds__(kThreads) matmul_exact(float* __restrict__ r, 
         cp_async_commit();
         const int st = (int)(c % S);
         const int64_t k0 = c * BK;
-        const int kk_end = (int)((K - k0) < BK ? (K - k0) : BK);
-        for (int kk = 0; kk < kk_end; ++kk) {
+        auto step = [&](int kk) {
             float a[TM], bv[TN];
 #pragma unroll
             for (int i = 0; i < TM; ++i) a[i] = As[st][kk][ty * TM + i];
@@ -112,6 +111,13 @@ __global__ void __launch_bounds__(kThreads) matmul_exact(float* __restrict__ r, 
             for (int i = 0; i < TM; ++i)
 #pragma unroll
                 for (int j = 0; j < TN; ++j) acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(a[i], bv[j]));
+        };
+        if (K - k0 >= BK) {  // a full chunk: a fixed trip count lets the shared loads run ahead
+#pragma unroll 16
+            for (int kk = 0; kk < BK; ++kk) step(kk);
+        } else {
+            const int kk_end = (int)(K - k0);
+            for (int kk = 0; kk < kk_end; ++kk) step(kk);
         }
     }
     cp_async_wait<0>();
