@@ -35,11 +35,6 @@ int sm_count() {
     return n;
 }
 
-__device__ __forceinline__ void cp_async4(float* dst, const float* src, bool valid) {
-    // 4-byte asynchronous copy to shared memory; an invalid element is zero-filled (no bytes read)
-    const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(d), "l"(src), "r"(valid ? 4 : 0) : "memory");
-}
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
@@ -73,33 +68,60 @@ __global__ void __launch_bounds__(kThreads) matmul_exact(float* __restrict__ r, 
             acc[i][j] = (accumulate && gi < M && gj < N) ? r[gi * r_ld + gj] : 0.0f;
         }
     const int64_t nk = (K + BK - 1) / BK;
-    auto issue = [&](int64_t c) {  // chunk c into stage c % S
-        const int st = (int)(c % S);
+    // each thread's elements of a chunk: fixed rows/columns and k offsets, so per chunk only the
+    // k base moves (the address arithmetic had cost more instructions than the products)
+    constexpr int NA = BM * BK / kThreads, NB = BN * BK / kThreads;
+    static_assert(NA * kThreads == BM * BK && NB * kThreads == BN * BK, "whole chunks per thread");
+    constexpr uint32_t kStageA = BK * (BM + 1) * 4, kStageB = BK * BN * 4;
+    const float* xa[NA];
+    const float* yb[NB];
+    int kia[NA], kib[NB];
+    uint32_t sa[NA], sb[NB];
+#pragma unroll
+    for (int j = 0; j < NA; ++j) {
+        const int t = threadIdx.x + j * kThreads, mi = t / BK, ki = t % BK;
+        const bool ok = m0 + mi < M;
+        xa[j] = ok ? x + (m0 + mi) * K + ki : nullptr;
+        kia[j] = ki;
+        sa[j] = (uint32_t)__cvta_generic_to_shared(&As[0][ki][mi]);
+    }
+#pragma unroll
+    for (int j = 0; j < NB; ++j) {
+        const int t = threadIdx.x + j * kThreads, ki = t / BN, ni = t % BN;
+        const bool ok = n0 + ni < N;
+        yb[j] = ok ? y + (int64_t)ki * N + n0 + ni : nullptr;
+        kib[j] = ki;
+        sb[j] = (uint32_t)__cvta_generic_to_shared(&Bs[0][ki][ni]);
+    }
+    auto issue = [&](int64_t c, int st) {  // chunk c into stage st
         const int64_t k0 = c * BK;
-        for (int t = threadIdx.x; t < BM * BK; t += kThreads) {
-            const int mi = t / BK, ki = t % BK;
-            const int64_t gm = m0 + mi, gk = k0 + ki;
-            const bool ok = gm < M && gk < K;
-            cp_async4(&As[st][ki][mi], ok ? x + gm * K + gk : x, ok);
+#pragma unroll
+        for (int j = 0; j < NA; ++j) {
+            const bool ok = xa[j] && k0 + kia[j] < K;
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(sa[j] + st * kStageA),
+                         "l"(ok ? xa[j] + k0 : x), "r"(ok ? 4 : 0) : "memory");
         }
-        for (int t = threadIdx.x; t < BN * BK; t += kThreads) {
-            const int ki = t / BN, ni = t % BN;
-            const int64_t gk = k0 + ki, gn = n0 + ni;
-            const bool ok = gk < K && gn < N;
-            cp_async4(&Bs[st][ki][ni], ok ? y + gk * N + gn : y, ok);
+#pragma unroll
+        for (int j = 0; j < NB; ++j) {
+            const bool ok = yb[j] && k0 + kib[j] < K;
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(sb[j] + st * kStageB),
+                         "l"(ok ? yb[j] + k0 * N : y), "r"(ok ? 4 : 0) : "memory");
         }
     };
 #pragma unroll
     for (int c = 0; c < S - 1; ++c) {  // one commit group per chunk, empty past the last
-        if (c < nk) issue(c);
+        if (c < nk) issue(c, c);
         cp_async_commit();
     }
+    int st_use = 0, st_fill = S - 1;
     for (int64_t c = 0; c < nk; ++c) {
         cp_async_wait<S - 2>();  // this thread's copies of chunk c have landed
         __syncthreads();         // everyone's have, and everyone is done with chunk c - 1's stage
-        if (c + S - 1 < nk) issue(c + S - 1);
+        if (c + S - 1 < nk) issue(c + S - 1, st_fill);
         cp_async_commit();
-        const int st = (int)(c % S);
+        st_fill = st_fill == S - 1 ? 0 : st_fill + 1;
+        const int st = st_use;
+        st_use = st_use == S - 1 ? 0 : st_use + 1;
         const int64_t k0 = c * BK;
         auto step = [&](int kk) {
             float a[TM], bv[TN];
