@@ -43,11 +43,11 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 // by cp.async: chunk c + S - 1 is in flight while chunk c is consumed, so small tiles (whose
 // per-chunk arithmetic is short) no longer wait a full memory latency per chunk.  Each thread
 // still adds its products in k order, separately rounded, over the valid k only.
-template <int BM, int BN, int TM, int TN, int BK, int S>
-__global__ void __launch_bounds__(kThreads) matmul_exact(float* __restrict__ r, const float* __restrict__ x,
+template <int BM, int BN, int TM, int TN, int BK, int S, int THREADS = (BM / TM) * (BN / TN)>
+__global__ void __launch_bounds__(THREADS) matmul_exact(float* __restrict__ r, const float* __restrict__ x,
                                                          const float* __restrict__ y, int64_t M, int64_t K,
                                                          int64_t N, int64_t r_ld, int accumulate) {
-    static_assert((BM / TM) * (BN / TN) == kThreads, "thread tiling");
+    static_assert((BM / TM) * (BN / TN) == THREADS, "thread tiling");
     static_assert(S >= 2, "a ring of at least two stages");
     __shared__ float As[S][BK][BM + 1];
     __shared__ float Bs[S][BK][BN];
@@ -70,8 +70,8 @@ __global__ void __launch_bounds__(kThreads) matmul_exact(float* __restrict__ r, 
     const int64_t nk = (K + BK - 1) / BK;
     // each thread's elements of a chunk: fixed rows/columns and k offsets, so per chunk only the
     // k base moves (the address arithmetic had cost more instructions than the products)
-    constexpr int NA = BM * BK / kThreads, NB = BN * BK / kThreads;
-    static_assert(NA * kThreads == BM * BK && NB * kThreads == BN * BK, "whole chunks per thread");
+    constexpr int NA = BM * BK / THREADS, NB = BN * BK / THREADS;
+    static_assert(NA * THREADS == BM * BK && NB * THREADS == BN * BK, "whole chunks per thread");
     constexpr uint32_t kStageA = BK * (BM + 1) * 4, kStageB = BK * BN * 4;
     const float* xa[NA];
     const float* yb[NB];
@@ -79,7 +79,7 @@ __global__ void __launch_bounds__(kThreads) matmul_exact(float* __restrict__ r, 
     uint32_t sa[NA], sb[NB];
 #pragma unroll
     for (int j = 0; j < NA; ++j) {
-        const int t = threadIdx.x + j * kThreads, mi = t / BK, ki = t % BK;
+        const int t = threadIdx.x + j * THREADS, mi = t / BK, ki = t % BK;
         const bool ok = m0 + mi < M;
         xa[j] = ok ? x + (m0 + mi) * K + ki : nullptr;
         kia[j] = ki;
@@ -87,7 +87,7 @@ __global__ void __launch_bounds__(kThreads) matmul_exact(float* __restrict__ r, 
     }
 #pragma unroll
     for (int j = 0; j < NB; ++j) {
-        const int t = threadIdx.x + j * kThreads, ki = t / BN, ni = t % BN;
+        const int t = threadIdx.x + j * THREADS, ki = t / BN, ni = t % BN;
         const bool ok = n0 + ni < N;
         yb[j] = ok ? y + (int64_t)ki * N + n0 + ni : nullptr;
         kib[j] = ki;
@@ -156,7 +156,7 @@ template <int BM, int BN, int TM, int TN, int BK, int S>
 cudaError_t launch_exact(float* r, const float* x, const float* y, int64_t batch, int64_t M, int64_t K, int64_t N,
                          int64_t r_ld, int accumulate, cudaStream_t st) {
     dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + BM - 1) / BM), (unsigned)batch);
-    matmul_exact<BM, BN, TM, TN, BK, S><<<grid, kThreads, 0, st>>>(r, x, y, M, K, N, r_ld, accumulate);
+    matmul_exact<BM, BN, TM, TN, BK, S><<<grid, (BM / TM) * (BN / TN), 0, st>>>(r, x, y, M, K, N, r_ld, accumulate);
     return cudaGetLastError();
 }
 
@@ -312,7 +312,7 @@ extern "C" int mcu_launch_matmul_exact(float* r, const float* x, const float* y,
     if (blocks(128, 128) >= target) e = launch_exact<128, 128, 8, 8, 16, 2>(r, x, y, batch, M, K, N, r_ld, accumulate, st);
     else if (blocks(64, 64) >= target) e = launch_exact<64, 64, 4, 4, 16, 3>(r, x, y, batch, M, K, N, r_ld, accumulate, st);
     else if (blocks(32, 32) >= target / 2) e = launch_exact<32, 32, 2, 2, 32, 4>(r, x, y, batch, M, K, N, r_ld, accumulate, st);
-    else e = launch_exact<16, 16, 1, 1, 64, 4>(r, x, y, batch, M, K, N, r_ld, accumulate, st);
+    else e = launch_exact<16, 16, 2, 2, 64, 4>(r, x, y, batch, M, K, N, r_ld, accumulate, st);  // 64 threads
     return (int)e;
 }
 
