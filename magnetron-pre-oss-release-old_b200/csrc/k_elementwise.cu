@@ -351,13 +351,14 @@ struct RowWalk {
     }
 };
 
-// Rows of at most 128 * STEPS columns, vectorised: a warp walks kRowChunk consecutive rows,
+// Rows of at most 128 * STEPS columns, vectorised: a warp walks `chunk` consecutive rows
+// (kRowChunk, fewer when the tensor has few rows),
 // decomposing the first row's indices once and carrying them to the next rows, with several
 // rows' loads in flight before their stores.
 template <int OP, int STEPS>
 __global__ void __launch_bounds__(kThreads, 2) binary_rows_chunked(float* __restrict__ r, const float* __restrict__ x,
                                                                    const float* __restrict__ y, const RowParams p,
-                                                                   uint32_t nrows, uint32_t nchunks) {
+                                                                   uint32_t nrows, uint32_t nchunks, uint32_t chunk) {
     const int lane_id = threadIdx.x & 31;
     const uint32_t warp = (uint32_t)(((uint64_t)blockIdx.x * kThreads + threadIdx.x) >> 5);
     const uint32_t nwarps = (uint32_t)(((uint64_t)gridDim.x * kThreads) >> 5);
@@ -399,10 +400,10 @@ __global__ void __launch_bounds__(kThreads, 2) binary_rows_chunked(float* __rest
         }
     };
     for (uint32_t ch = warp; ch < nchunks; ch += nwarps) {
-        const uint32_t row0 = ch * kRowChunk;
+        const uint32_t row0 = ch * chunk;
         RowWalk w;
         w.start(row0, p);
-        const uint32_t rows_here = min(kRowChunk, nrows - row0);
+        const uint32_t rows_here = min(chunk, nrows - row0);
         // R rows' loads in flight before their stores: 4 for rows of at most 256 columns
         // (the loads are L2 latency-bound there; 114 registers allow 2 CTAs per SM), else 2
         constexpr int R = STEPS <= 2 ? 4 : 2;
@@ -462,13 +463,16 @@ cudaError_t launch_rows(float* r, const float* x, const float* y, const int64_t*
         for (int k = 1; k < 6; ++k) vec = vec && ys[k] % 4 == 0;
     }
     if (vec && p.steps <= 4 && dims[0] <= 512 && rows >= 4 * kRowChunk && rows < (1ull << 32)) {
-        const uint32_t nchunks = (uint32_t)((rows + kRowChunk - 1) / kRowChunk);
+        // kRowChunk rows per warp, fewer when that leaves fewer than four chunks per SM
+        uint32_t chunk = kRowChunk;
+        while (chunk > 1 && rows / chunk < 4ull * (uint64_t)sm_count()) chunk /= 2;
+        const uint32_t nchunks = (uint32_t)((rows + chunk - 1) / chunk);
         const unsigned g = grid_for((uint64_t)nchunks * 32, kThreads);
         switch (p.steps) {
-            case 1: binary_rows_chunked<OP, 1><<<g, kThreads, 0, st>>>(r, x, y, p, (uint32_t)rows, nchunks); break;
-            case 2: binary_rows_chunked<OP, 2><<<g, kThreads, 0, st>>>(r, x, y, p, (uint32_t)rows, nchunks); break;
-            case 3: binary_rows_chunked<OP, 3><<<g, kThreads, 0, st>>>(r, x, y, p, (uint32_t)rows, nchunks); break;
-            default: binary_rows_chunked<OP, 4><<<g, kThreads, 0, st>>>(r, x, y, p, (uint32_t)rows, nchunks); break;
+            case 1: binary_rows_chunked<OP, 1><<<g, kThreads, 0, st>>>(r, x, y, p, (uint32_t)rows, nchunks, chunk); break;
+            case 2: binary_rows_chunked<OP, 2><<<g, kThreads, 0, st>>>(r, x, y, p, (uint32_t)rows, nchunks, chunk); break;
+            case 3: binary_rows_chunked<OP, 3><<<g, kThreads, 0, st>>>(r, x, y, p, (uint32_t)rows, nchunks, chunk); break;
+            default: binary_rows_chunked<OP, 4><<<g, kThreads, 0, st>>>(r, x, y, p, (uint32_t)rows, nchunks, chunk); break;
         }
         return cudaGetLastError();
     }
