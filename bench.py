@@ -677,9 +677,9 @@ def build_mlp2(dev, torch, batch=256, d_in=784, d_hid=256, d_out=10, seed=12):
     """The two-layer MLP forward of the reference's MNIST-shaped example: X (batch x 784) U(0,1),
     Glorot-uniform W1 (784 x 256) and W2 (256 x 10), a zero 1-D bias of 256 (tiling broadcast)
     and a zero full-shape (batch x 10) bias, MATMUL -> ADD -> SIGMOID -> MATMUL -> ADD as one
-    recorded graph, then the normalised row softmax over the 10 logits.  Returns the forward
-    (graph replay + softmax, on the device's stream), the probability tensor and every tensor
-    to free."""
+    recorded graph run by the fused executor (each bias and the SIGMOID in its product's
+    epilogue), then the normalised row softmax over the 10 logits.  Returns the forward (graph
+    replay + softmax, on the device's stream), the probability tensor and every tensor to free."""
     import mag_b200 as MB
     g = torch.Generator().manual_seed(seed)
     lim1, lim2 = (6.0 / (d_in + d_hid)) ** 0.5, (6.0 / (d_hid + d_out)) ** 0.5
@@ -696,7 +696,7 @@ def build_mlp2(dev, torch, batch=256, d_in=784, d_hid=256, d_out=10, seed=12):
         dev.eager = True
 
     def fwd():
-        rc = dev.L.mag_cuda_graph_exec(dev.p, z.ptr)
+        rc = dev.L.mag_cuda_graph_exec_fused(dev.p, z.ptr)
         return rc or dev.L.mag_cuda_softmax_rows_f32(dev.p, P.data_ptr, z.data_ptr, batch, d_out)
     return fwd, P, [X, W1, W2, B1, B2, P]
 

@@ -80,9 +80,12 @@ MAG_CUDA_EXPORT size_t mag_cuda_memory_in_use(mag_compute_device_t* dvc);
 MAG_CUDA_EXPORT int mag_cuda_graph_exec(mag_compute_device_t* dvc, mag_tensor_t* root);
 /* As mag_cuda_graph_exec, and fuses dense layers, MATMUL -> ADD(same-shape bias)
  * [-> GELU], into one tensor-core GEMM per layer (bias, GELU and the next
- * layer's operand split in its epilogue).  After the call the root and every
- * tensor outside such chains hold their values; the MATMUL and ADD results
- * inside a fused chain are not written. */
+ * layer's operand split in its epilogue).  Products below the tensor-core
+ * threshold fuse MATMUL -> ADD(same-shape bias, or one broadcast along dim 0)
+ * [-> GELU or SIGMOID] into the bit-exact kernel's store, with the same bits as
+ * the separate ops (activations only when dim 0 is a multiple of 4).  After the
+ * call the root and every tensor outside such chains hold their values; the
+ * MATMUL and ADD results inside a fused chain are not written. */
 MAG_CUDA_EXPORT int mag_cuda_graph_exec_fused(mag_compute_device_t* dvc, mag_tensor_t* root);
 /* Drops the cached graphs of root (call before freeing the graph's tensors). */
 MAG_CUDA_EXPORT int mag_cuda_graph_release(mag_compute_device_t* dvc, mag_tensor_t* root);

@@ -1239,6 +1239,8 @@ typedef struct mcu_plan_item {
     int act;                /* fused: 0 none, 1 GELU */
     int a_split;            /* -1, or activation split buffer holding A's hi/lo */
     int out_split;          /* -1, or activation split buffer receiving out's hi/lo */
+    int exact;              /* fused on the bit-exact CUDA-core product (else the tensor-core one) */
+    int64_t bias_mod;       /* exact: 0 full-shape bias, else the length of a bias broadcast along dim 0 */
 } mcu_plan_item;
 
 static int same_shape_canonical(const mag_tensor_t* a, const mag_tensor_t* b) {
@@ -1247,7 +1249,7 @@ static int same_shape_canonical(const mag_tensor_t* a, const mag_tensor_t* b) {
     return is_canonical(a) && is_canonical(b);
 }
 
-static int tc_matmul_ok(mcu_device* d, const mag_tensor_t* m) {
+static int matmul_on_path(mcu_device* d, const mag_tensor_t* m, int path) {
     if (m->op != MAG_ABI_OP_MATMUL) return 0;
     const mag_tensor_t* x = m->op_inputs[0];
     const mag_tensor_t* y = m->op_inputs[1];
@@ -1255,7 +1257,19 @@ static int tc_matmul_ok(mcu_device* d, const mag_tensor_t* m) {
     const int64_t M = x->shape[0], K = x->shape[1], N = y->shape[1];
     if (m->storage.base == x->storage.base || m->storage.base == y->storage.base) return 0;
     if (m->shape[1] != N || (size_t)(M * N * 4) != m->storage.size) return 0;
-    return matmul_path(d, M, K, N) == MM_TC;
+    if (path == MM_EXACT && M > 1048560) return 0; /* the fused exact product runs unsliced */
+    return matmul_path(d, M, K, N) == path;
+}
+
+static int tc_matmul_ok(mcu_device* d, const mag_tensor_t* m) { return matmul_on_path(d, m, MM_TC); }
+
+/* A bias the elementwise ADD broadcasts along dim 0 of the product: a canonical tensor of
+ * shape (shape[0] of the product, 1, 1, 1, 1, 1), read at the flat index mod its length. */
+static int row_bias(const mag_tensor_t* b, const mag_tensor_t* m) {
+    if (!is_canonical(b) || b->shape[0] != m->shape[0]) return 0;
+    for (int k = 1; k < 6; ++k)
+        if (b->shape[k] != 1) return 0;
+    return 1;
 }
 
 static size_t find_index(mag_tensor_t** nodes, size_t n, const mag_tensor_t* t) {
@@ -1285,23 +1299,32 @@ static size_t plan_fusion(mcu_device* d, mag_tensor_t** nodes, size_t n, mag_ten
     size_t split_bytes = 0;
     for (size_t i = 0; i < n; ++i) {
         mag_tensor_t* m = nodes[i];
-        if (plan[i].kind != PLAN_NORMAL || !tc_matmul_ok(d, m) || m == root || users[i] != 1) continue;
+        if (plan[i].kind != PLAN_NORMAL || m == root || users[i] != 1) continue;
+        const int tc = tc_matmul_ok(d, m);
+        const int exact = !tc && matmul_on_path(d, m, MM_EXACT);
+        if (!tc && !exact) continue;
         size_t ia = user_of[i];
         mag_tensor_t* a = nodes[ia];
         if (a->op != MAG_ABI_OP_ADD || a->op_inputs[0] != m || a->op_inputs[1] == m) continue;
         mag_tensor_t* b = a->op_inputs[1];
-        if (!same_shape_canonical(a, m) || !same_shape_canonical(b, m) || a->storage.size != m->storage.size) continue;
+        if (!same_shape_canonical(a, m) || a->storage.size != m->storage.size) continue;
+        const int full = same_shape_canonical(b, m);
+        if (!full && !(exact && row_bias(b, m))) continue;
         plan[i].kind = PLAN_FUSED;
         plan[i].bias = b;
         plan[i].out = a;
+        plan[i].exact = exact;
+        plan[i].bias_mod = full ? 0 : b->shape[0];
         plan[ia].kind = PLAN_SKIP;
         size_t last = ia;
         if (a != root && users[ia] == 1) {
             size_t ig = user_of[ia];
             mag_tensor_t* g = nodes[ig];
-            if (g->op == MAG_ABI_OP_GELU && g->op_inputs[0] == a && same_shape_canonical(g, m) &&
-                g->storage.size == m->storage.size && m->shape[0] % 4 == 0) {
-                plan[i].act = 1;
+            /* every element on the activation's vector-lane formula: dim 0 a multiple of 4 */
+            const int act = g->op == MAG_ABI_OP_GELU ? 1 : (exact && g->op == MAG_ABI_OP_SIGMOID ? 2 : 0);
+            if (act && g->op_inputs[0] == a && same_shape_canonical(g, m) && g->storage.size == m->storage.size &&
+                m->shape[0] % 4 == 0) {
+                plan[i].act = act;
                 plan[i].out = g;
                 plan[ig].kind = PLAN_SKIP;
                 last = ig;
@@ -1310,7 +1333,7 @@ static size_t plan_fusion(mcu_device* d, mag_tensor_t** nodes, size_t n, mag_ten
         /* the next MATMUL reads this layer's output: hand it the split operand */
         mag_tensor_t* out = plan[i].out;
         const int64_t N = m->shape[1];
-        if (!d->tc_f16 && out != root && users[last] == 1 && N % 32 == 0) { /* the f16 split scales whole rows itself */
+        if (tc && !d->tc_f16 && out != root && users[last] == 1 && N % 32 == 0) { /* the f16 split scales whole rows itself */
             size_t in2 = user_of[last];
             mag_tensor_t* m2 = nodes[in2];
             if (m2->op_inputs[0] == out && m2->op_inputs[1] != out && tc_matmul_ok(d, m2)) {
@@ -1338,6 +1361,12 @@ static int exec_planned_matmul(mcu_device* d, mag_tensor_t* m, const mcu_plan_it
     materialize(d, y->storage.base);
     if (it->bias) materialize(d, it->bias->storage.base);
     result_written(d, out->storage.base, (size_t)(M * N * 4) == out->storage.size);
+    if (it->exact) {
+        int rc = mcu_launch_matmul_exact_ep(fptr(out), fptr(x), fptr(y), M, K, N, it->bias ? fptr(it->bias) : NULL,
+                                            it->bias_mod, it->act, d->stream);
+        if (!rc) mcu_count_launches(1);
+        return rc;
+    }
     mcu_tc_epilogue ep;
     memset(&ep, 0, sizeof(ep));
     const size_t half = split_bytes / 2;

@@ -19,6 +19,7 @@
 #include <cuda_runtime.h>
 #include <cstdint>
 #include "mcu_kernels.h"
+#include "mcu_math.cuh"
 
 namespace {
 
@@ -46,7 +47,8 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 template <int BM, int BN, int TM, int TN, int BK, int S, int THREADS = (BM / TM) * (BN / TN)>
 __global__ void __launch_bounds__(THREADS) matmul_exact(float* __restrict__ r, const float* __restrict__ x,
                                                          const float* __restrict__ y, int64_t M, int64_t K,
-                                                         int64_t N, int64_t r_ld, int accumulate) {
+                                                         int64_t N, int64_t r_ld, int accumulate,
+                                                         const float* __restrict__ bias, int64_t bias_mod, int act) {
     static_assert((BM / TM) * (BN / TN) == THREADS, "thread tiling");
     static_assert(S >= 2, "a ring of at least two stages");
     __shared__ float As[S][BK][BM + 1];
@@ -148,15 +150,29 @@ __global__ void __launch_bounds__(THREADS) matmul_exact(float* __restrict__ r, c
 #pragma unroll
         for (int j = 0; j < TN; ++j) {
             int64_t gi = m0 + ty * TM + i, gj = n0 + tx * TN + j;
-            if (gi < M && gj < N) r[gi * r_ld + gj] = acc[i][j];
+            if (gi < M && gj < N) {
+                // a fused dense layer: the bias as the elementwise ADD indexes it (flat index,
+                // or flat index mod the length of a bias broadcast along dim 0), then the
+                // activation's vector-lane formula
+                float v = acc[i][j];
+                if (bias) {
+                    const int64_t f = gi * N + gj;
+                    v = __fadd_rn(v, bias[bias_mod ? f % bias_mod : f]);
+                }
+                if (act == 1) v = mcu::lane_op<mcu::OP_GELU>(v);
+                else if (act == 2) v = mcu::lane_op<mcu::OP_SIGMOID>(v);
+                r[gi * r_ld + gj] = v;
+            }
         }
 }
 
 template <int BM, int BN, int TM, int TN, int BK, int S>
 cudaError_t launch_exact(float* r, const float* x, const float* y, int64_t batch, int64_t M, int64_t K, int64_t N,
-                         int64_t r_ld, int accumulate, cudaStream_t st) {
+                         int64_t r_ld, int accumulate, cudaStream_t st, const float* bias = nullptr,
+                         int64_t bias_mod = 0, int act = 0) {
     dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + BM - 1) / BM), (unsigned)batch);
-    matmul_exact<BM, BN, TM, TN, BK, S><<<grid, (BM / TM) * (BN / TN), 0, st>>>(r, x, y, M, K, N, r_ld, accumulate);
+    matmul_exact<BM, BN, TM, TN, BK, S><<<grid, (BM / TM) * (BN / TN), 0, st>>>(r, x, y, M, K, N, r_ld, accumulate,
+                                                                               bias, bias_mod, act);
     return cudaGetLastError();
 }
 
@@ -284,6 +300,20 @@ int64_t skinny_kc(int64_t K, int64_t slices) {
     return (kc + 15) / 16 * 16;
 }
 
+cudaError_t exact_tiles(float* r, const float* x, const float* y, int64_t batch, int64_t M, int64_t K, int64_t N,
+                        int64_t r_ld, int accumulate, cudaStream_t st, const float* bias, int64_t bias_mod, int act) {
+    const int64_t target = 2 * (int64_t)sm_count();
+    auto blocks = [&](int64_t bm, int64_t bn) { return batch * ((M + bm - 1) / bm) * ((N + bn - 1) / bn); };
+    if (blocks(128, 128) >= target)
+        return launch_exact<128, 128, 8, 8, 16, 2>(r, x, y, batch, M, K, N, r_ld, accumulate, st, bias, bias_mod, act);
+    if (blocks(64, 64) >= target)
+        return launch_exact<64, 64, 4, 4, 16, 3>(r, x, y, batch, M, K, N, r_ld, accumulate, st, bias, bias_mod, act);
+    if (blocks(32, 32) >= target / 2)
+        return launch_exact<32, 32, 2, 2, 32, 4>(r, x, y, batch, M, K, N, r_ld, accumulate, st, bias, bias_mod, act);
+    // 64 threads of 2 x 2 outputs
+    return launch_exact<16, 16, 2, 2, 64, 4>(r, x, y, batch, M, K, N, r_ld, accumulate, st, bias, bias_mod, act);
+}
+
 }  // namespace
 
 // Row tiles are a grid dimension (at most 65535 tiles of at least 16 rows): a single product with
@@ -306,14 +336,14 @@ extern "C" int mcu_launch_matmul_exact(float* r, const float* x, const float* y,
         return (int)cudaSuccess;
     }
     if (batch >= 65536 || (M + 15) / 16 >= 65536) return (int)cudaErrorInvalidValue;
-    const int64_t target = 2 * (int64_t)sm_count();
-    auto blocks = [&](int64_t bm, int64_t bn) { return batch * ((M + bm - 1) / bm) * ((N + bn - 1) / bn); };
-    cudaError_t e;
-    if (blocks(128, 128) >= target) e = launch_exact<128, 128, 8, 8, 16, 2>(r, x, y, batch, M, K, N, r_ld, accumulate, st);
-    else if (blocks(64, 64) >= target) e = launch_exact<64, 64, 4, 4, 16, 3>(r, x, y, batch, M, K, N, r_ld, accumulate, st);
-    else if (blocks(32, 32) >= target / 2) e = launch_exact<32, 32, 2, 2, 32, 4>(r, x, y, batch, M, K, N, r_ld, accumulate, st);
-    else e = launch_exact<16, 16, 2, 2, 64, 4>(r, x, y, batch, M, K, N, r_ld, accumulate, st);  // 64 threads
-    return (int)e;
+    return (int)exact_tiles(r, x, y, batch, M, K, N, r_ld, accumulate, st, nullptr, 0, 0);
+}
+
+extern "C" int mcu_launch_matmul_exact_ep(float* r, const float* x, const float* y, int64_t M, int64_t K, int64_t N,
+                                          const float* bias, int64_t bias_mod, int act, cudaStream_t st) {
+    if (M <= 0 || N <= 0) return (int)cudaSuccess;
+    if (M > kExactRowSlice || bias_mod < 0 || act < 0 || act > 2) return (int)cudaErrorInvalidValue;
+    return (int)exact_tiles(r, x, y, 1, M, K, N, N, 0, st, bias, bias_mod, act);
 }
 
 extern "C" size_t mcu_matmul_skinny_scratch_bytes(int64_t M, int64_t K, int64_t N) {

@@ -67,6 +67,12 @@ int mcu_launch_img_draw_text(float* img, int32_t w, int32_t h, const int32_t* gl
  * summed k = 0..K-1 in order with separately rounded multiply and add. */
 int mcu_launch_matmul_exact(float* r, const float* x, const float* y, int64_t batch, int64_t M, int64_t K,
                             int64_t N, int64_t r_ld, int accumulate, cudaStream_t st);
+/* A single bit-exact product with a fused dense-layer epilogue: r = act(xy + bias), the bias
+ * read at the flat result index (bias_mod = 0) or at that index mod bias_mod (a bias broadcast
+ * along dim 0), act 0 none, 1 GELU, 2 SIGMOID (their vector-lane formulas).  At most 1048560
+ * rows. */
+int mcu_launch_matmul_exact_ep(float* r, const float* x, const float* y, int64_t M, int64_t K, int64_t N,
+                               const float* bias, int64_t bias_mod, int act, cudaStream_t st);
 /* Kernels one exact product launches: a single product of more than 1048560 rows runs in slices. */
 int mcu_matmul_exact_kernels(int64_t batch, int64_t M);
 /* Largest K the tensor-core product takes (its padded K indexes a grid dimension); beyond it the

@@ -609,11 +609,44 @@ def test_two_layer_mlp_forward_batch_256():
     logits = o.binary("ADD", a, pad6((b, c)), b2, pad6((b, c)))
     want = o.softmax_rows(logits, b, c)
     try:
-        for _ in range(2):
-            dev.graph_exec(z)
+        for fused in (False, True, False, True):  # fused: bias and SIGMOID in the products' epilogues
+            n0 = dev.launches()
+            dev.graph_exec(z, fused=fused)
+            if fused:
+                assert dev.launches() - n0 == 2
             MB.check(dev.L.mag_cuda_softmax_rows_f32(dev.p, p.data_ptr, z.data_ptr, b, c), "softmax")
             assert bits_equal(z.read(), logits).all()
             got = p.read()
             assert np.all(np.abs(got - want) <= 1e-6 * np.abs(want)), float(np.abs(got - want).max())
     finally:
         dev.graph_release(z)
+
+
+@pytest.mark.parametrize("m,k,n,row_bias,act", [(102, 300, 70, True, "SIGMOID"), (96, 200, 50, False, "GELU"),
+                                                (96, 200, 50, True, "SIGMOID"), (40, 33, 17, False, None)])
+def test_fused_exact_layer_matches_unfused_bitwise(m, k, n, row_bias, act):
+    """Products below the tensor-core threshold fuse the following ADD (a full-shape bias, or one
+    broadcast along dim 0) and, when dim 0 is a multiple of 4, GELU or SIGMOID into the bit-exact
+    kernel's store: the same bits as the op-by-op graph (dim 0 = 102 keeps SIGMOID separate)."""
+    dev, o = device(), oracle()
+    s = o.stream(9300 + m + k)
+    tx, tw = dev.tensor((m, k)), dev.tensor((k, n))
+    tb = dev.tensor((m,)) if row_bias else dev.tensor((m, n))
+    tx.write(s.uniform(m * k, -1, 1))
+    tw.write(s.uniform(k * n, -0.3, 0.3))
+    tb.write(s.uniform(m if row_bias else m * n, -0.5, 0.5))
+    dev.eager = False
+    try:
+        h = dev.op("ADD", dev.op("MATMUL", tx, tw), tb)
+        if act:
+            h = dev.op(act, h, inplace=True)
+    finally:
+        dev.eager = True
+    try:
+        dev.graph_exec(h)
+        plain = h.read()
+        dev.graph_exec(h, fused=True)
+        fused = h.read()
+    finally:
+        dev.graph_release(h)
+    assert bits_equal(fused, plain).all()
