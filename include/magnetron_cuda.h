@@ -63,7 +63,10 @@ MAG_CUDA_EXPORT int mag_cuda_device_ordinal(mag_compute_device_t* dvc);
 #define MAG_CUDA_TC_SPLIT_F16 1
 MAG_CUDA_EXPORT int mag_cuda_set_tc_split(mag_compute_device_t* dvc, int split);
 MAG_CUDA_EXPORT void* mag_cuda_stream(mag_compute_device_t* dvc);          /* cudaStream_t */
-MAG_CUDA_EXPORT int mag_cuda_synchronize(mag_compute_device_t* dvc);       /* waits, reports async errors */
+/* Waits for the device's stream and reports asynchronous errors: a CUDA error code, or
+ * MAG_CUDA_E_DEVICE_WAIT when a kernel gave up a bounded wait since the last report (the
+ * status word is then cleared). */
+MAG_CUDA_EXPORT int mag_cuda_synchronize(mag_compute_device_t* dvc);
 MAG_CUDA_EXPORT int mag_cuda_last_error(mag_compute_device_t* dvc);        /* sticky error of the eager path */
 /* MATMUL algorithm: 0 = automatic (default, or MAG_CUDA_MATMUL=exact|tc), 1 = the
  * bit-exact CUDA-core kernel, 2 = the 3xTF32 tensor-core kernel where the shape allows. */
@@ -237,9 +240,12 @@ MAG_CUDA_EXPORT int mag_cuda_img_draw_text(mag_compute_device_t* dvc, mag_tensor
  * inside a stream capture or a host path that must stay off the allocator.  Its
  * partial sums go to one fixed 16 MiB array in this library's device image,
  * which every GPU that loads the library keeps until the process exits.  Calls
- * needing more (slices x M x N x 4 bytes; M=8, K=N=4096 needs 8 MiB) return
- * MAG_CUDA_E_SCRATCH_LIMIT.  The first call on a device looks up the array's
- * device address, so make it before any stream capture.  All calls on a device
+ * needing more (slices x M x N x 4 bytes) return MAG_CUDA_E_SCRATCH_LIMIT.  On a
+ * 148-SM B200 an M x 4096 x 4096 product takes 128 slices, 2 MiB per row of M:
+ * M = 1..8 fits (M = 8 fills the array exactly) and M = 9..16 is rejected at that
+ * size.  The first call on a device looks up the array's device address, so make
+ * it before any stream capture; the address is kept for the life of the process,
+ * so the entry point does not survive cudaDeviceReset.  All calls on a device
  * share the array: calls whose kernels overlap on the GPU race. */
 MAG_CUDA_EXPORT int mag_cuda_matmul_skinny_f32_noalloc(mag_compute_device_t* dvc, float* r, const float* x,
                                                        const float* y, int64_t M, int64_t K, int64_t N);

@@ -722,7 +722,10 @@ int mag_cuda_synchronize(mag_compute_device_t* dvc) {
     int st = 0;
     e = cudaMemcpy(&st, d->d_status, sizeof(int), cudaMemcpyDeviceToHost);
     if (e != cudaSuccess) return (int)e;
-    return st ? MAG_CUDA_E_DEVICE_WAIT : 0;
+    if (!st) return 0;
+    /* reported once: the word is cleared, so later work on this device is judged on its own */
+    e = cudaMemset(d->d_status, 0, sizeof(int));
+    return e != cudaSuccess ? (int)e : MAG_CUDA_E_DEVICE_WAIT;
 }
 
 int mag_cuda_exec_node(mag_compute_device_t* dvc, mag_tensor_t* node) {
@@ -1202,10 +1205,23 @@ static uint64_t mix(uint64_t h, uint64_t v) {
     return h;
 }
 
-static uint64_t graph_signature(mag_tensor_t** nodes, size_t n) {
+static int is_compute(const mag_tensor_t* t) {
+    return t->op != MAG_ABI_OP_NOP && t->op != MAG_ABI_OP_VIEW && t->op != MAG_ABI_OP_TRANSPOSE &&
+           t->op != MAG_ABI_OP_PERMUTE;
+}
+
+/* A leaf whose whole buffer holds zeros that nothing has overwritten since (fresh storage, or
+ * set to zero through the storage callback). */
+static int leaf_is_zero(mcu_device* d, const mag_tensor_t* t) {
+    mcu_block* b = tab_find(d, t->storage.base);
+    return b && b->known_zero && (size_t)(t->numel * 4) <= b->size;
+}
+
+static uint64_t graph_signature(mcu_device* d, mag_tensor_t** nodes, size_t n) {
     uint64_t h = 0x1234567ull;
     for (size_t i = 0; i < n; ++i) {
         mag_tensor_t* t = nodes[i];
+        if (!is_compute(t)) h = mix(h, (uint64_t)leaf_is_zero(d, t)); /* zero biases are planned as such */
         h = mix(h, (uintptr_t)t);
         h = mix(h, (uint64_t)t->op);
         h = mix(h, (uint64_t)t->storage.base);
@@ -1216,10 +1232,6 @@ static uint64_t graph_signature(mag_tensor_t** nodes, size_t n) {
     return h;
 }
 
-static int is_compute(const mag_tensor_t* t) {
-    return t->op != MAG_ABI_OP_NOP && t->op != MAG_ABI_OP_VIEW && t->op != MAG_ABI_OP_TRANSPOSE &&
-           t->op != MAG_ABI_OP_PERMUTE;
-}
 
 /* ---- fusion planner for deferred graphs ----
  * Recognises dense layers, MATMUL -> ADD(same-shape bias) [-> GELU], whose
@@ -1241,6 +1253,7 @@ typedef struct mcu_plan_item {
     int out_split;          /* -1, or activation split buffer receiving out's hi/lo */
     int exact;              /* fused on the bit-exact CUDA-core product (else the tensor-core one) */
     int64_t bias_mod;       /* exact: 0 full-shape bias, else the length of a bias broadcast along dim 0 */
+    int bias_zero;          /* tensor-core: the bias is a leaf known to hold zeros (no bias read) */
 } mcu_plan_item;
 
 static int same_shape_canonical(const mag_tensor_t* a, const mag_tensor_t* b) {
@@ -1283,7 +1296,7 @@ static size_t plan_fusion(mcu_device* d, mag_tensor_t** nodes, size_t n, mag_ten
     int* users = (int*)calloc(n, sizeof(int));
     size_t* user_of = (size_t*)malloc(n * sizeof(size_t));
     for (size_t i = 0; i < n; ++i) {
-        plan[i] = (mcu_plan_item){PLAN_NORMAL, NULL, NULL, 0, -1, -1};
+        plan[i] = (mcu_plan_item){PLAN_NORMAL, NULL, NULL, 0, -1, -1, 0, 0, 0};
         user_of[i] = n;
     }
     for (size_t i = 0; i < n; ++i)
@@ -1315,6 +1328,9 @@ static size_t plan_fusion(mcu_device* d, mag_tensor_t** nodes, size_t n, mag_ten
         plan[i].out = a;
         plan[i].exact = exact;
         plan[i].bias_mod = full ? 0 : b->shape[0];
+        /* a leaf bias that nothing has written since it was zeroed (the core's fresh tensors):
+         * the epilogue adds +0.0f instead of reading it; the graph's key holds that state */
+        plan[i].bias_zero = tc && full && !is_compute(b) && leaf_is_zero(d, b);
         plan[ia].kind = PLAN_SKIP;
         size_t last = ia;
         if (a != root && users[ia] == 1) {
@@ -1376,7 +1392,8 @@ static int exec_planned_matmul(mcu_device* d, mag_tensor_t* m, const mcu_plan_it
         ep.a_lo = (const float*)(b + half);
     }
     if (it->kind == PLAN_FUSED) {
-        ep.bias = it->bias ? fptr(it->bias) : NULL;
+        ep.bias = it->bias && !it->bias_zero ? fptr(it->bias) : NULL;
+        ep.bias_zero = it->bias_zero;
         ep.act = it->act;
         if (it->out_split >= 0) {
             char* b = scratch + split_off + (size_t)it->out_split * split_bytes;
@@ -1393,18 +1410,23 @@ static int exec_planned_matmul(mcu_device* d, mag_tensor_t* m, const mcu_plan_it
     return rc;
 }
 
+static void harvest_graph_events(mcu_device* d, mcu_graph* g, int wait);
+
 static int graph_exec_impl(mag_compute_device_t* dvc, mag_tensor_t* root, int fuse) {
     if (!dvc || !root) return MAG_CUDA_E_INVALID;
     mcu_device* d = dev_of(dvc);
     size_t n = 0;
     mag_tensor_t** nodes = topo_order(root, &n);
     /* the matmul path and split kind are baked into a captured graph: part of its key */
-    uint64_t sig = graph_signature(nodes, n) ^ ((uint64_t)(1 + d->tc_f16 + 2 * d->matmul_mode) * 0x9E3779B97F4A7C15ull);
+    uint64_t sig = graph_signature(d, nodes, n) ^ ((uint64_t)(1 + d->tc_f16 + 2 * d->matmul_mode) * 0x9E3779B97F4A7C15ull);
     mcu_graph* g = d->graphs;
     while (g && (g->root != root || g->fused != fuse)) g = g->next;
     for (size_t i = 0; i < n; ++i) io_wait(d, tab_find(d, nodes[i]->storage.base)); /* outside any capture */
     if (g && g->sig == sig) {
         free(nodes);
+        /* profiling: the previous replay's op events are read before this replay records over them
+         * (waiting for that replay alone, so work queued after it keeps running) */
+        if (g->ran && d->profiling) harvest_graph_events(d, g, 1);
         g->ran = g->n_ev > 0;
         mcu_count_launches((int)g->n_kernels);
         return (int)cudaGraphLaunch(g->exec, d->stream);
@@ -1417,7 +1439,7 @@ static int graph_exec_impl(mag_compute_device_t* dvc, mag_tensor_t* root, int fu
         graph_free(g);
     }
     mcu_plan_item* plan = (mcu_plan_item*)calloc(n ? n : 1, sizeof(mcu_plan_item));
-    for (size_t i = 0; i < n; ++i) plan[i] = (mcu_plan_item){PLAN_NORMAL, NULL, NULL, 0, -1, -1};
+    for (size_t i = 0; i < n; ++i) plan[i] = (mcu_plan_item){PLAN_NORMAL, NULL, NULL, 0, -1, -1, 0, 0, 0};
     size_t split_bytes = fuse ? plan_fusion(d, nodes, n, root, plan) : 0;
     /* leaves are materialised outside the capture so replays never clear data the caller wrote later */
     size_t scratch = 0;
@@ -1532,6 +1554,20 @@ static const char* const k_op_names[MAG_ABI_OP__COUNT] = {
     "SILU_DV", "TANH", "TANH_DV", "RELU", "RELU_DV", "GELU", "GELU_DV", "ADD", "SUB", "MUL", "DIV", "ADDS",
     "SUBS", "MULS", "DIVS", "MATMUL"};
 
+/* Adds the op event times of g's last replay to the per-op totals (wait: first wait for that
+ * replay's last event; the stream need not be idle). */
+static void harvest_graph_events(mcu_device* d, mcu_graph* g, int wait) {
+    if (wait && g->n_ev) cudaEventSynchronize(g->ev_b[g->n_ev - 1]);
+    for (size_t i = 0; i < g->n_ev; ++i) {
+        float ms = 0.0f;
+        if (cudaEventElapsedTime(&ms, g->ev_a[i], g->ev_b[i]) == cudaSuccess) {
+            d->prof_us[g->ev_op[i]] += ms * 1e3;
+            d->prof_cnt[g->ev_op[i]]++;
+        }
+    }
+    g->ran = 0;
+}
+
 int mag_cuda_profile_start(mag_compute_device_t* dvc) {
     mcu_device* d = dev_of(dvc);
     d->profiling = 1;
@@ -1554,17 +1590,8 @@ int mag_cuda_profile_collect(mag_compute_device_t* dvc) {
         cudaEventDestroy(d->prof[i].b);
     }
     d->prof_n = 0;
-    for (mcu_graph* g = d->graphs; g; g = g->next) {
-        if (!g->ran) continue;
-        for (size_t i = 0; i < g->n_ev; ++i) {
-            float ms = 0.0f;
-            if (cudaEventElapsedTime(&ms, g->ev_a[i], g->ev_b[i]) == cudaSuccess) {
-                d->prof_us[g->ev_op[i]] += ms * 1e3;
-                d->prof_cnt[g->ev_op[i]]++;
-            }
-        }
-        g->ran = 0;
-    }
+    for (mcu_graph* g = d->graphs; g; g = g->next)
+        if (g->ran) harvest_graph_events(d, g, 0);
     cudaGetLastError();
     return 0;
 }
@@ -1588,7 +1615,18 @@ int mag_cuda_profile_stop(mag_compute_device_t* dvc, const char* csv_path) {
     if (!f) return MAG_CUDA_E_INVALID;
     if (csv_path) fprintf(f, "Operation,Executions,Usage,AVG Time,Total Time\n");
     else printf("%16s %16s %16s %16s %16s\n", "Operation", "Executions", "Usage (%)", "AVG Time (us)", "Total Time (us)");
-    for (int op = 0; op < MAG_ABI_OP__COUNT; ++op) {
+    /* rows by total time, longest first, ties in op order (the core's qsort by elapsed time,
+     * magnetron/magnetron.c:1037-1043, :1085) */
+    int order[MAG_ABI_OP__COUNT];
+    for (int i = 0; i < MAG_ABI_OP__COUNT; ++i) order[i] = i;
+    for (int i = 1; i < MAG_ABI_OP__COUNT; ++i) {
+        const int v = order[i];
+        int j = i;
+        for (; j > 0 && d->prof_us[order[j - 1]] < d->prof_us[v]; --j) order[j] = order[j - 1];
+        order[j] = v;
+    }
+    for (int k = 0; k < MAG_ABI_OP__COUNT; ++k) {
+        const int op = order[k];
         if (!d->prof_cnt[op]) continue;
         double perc = (double)d->prof_cnt[op] / (double)all * 100.0;
         double avg = d->prof_us[op] / (double)d->prof_cnt[op];

@@ -17,6 +17,7 @@
 // uses FMA and a different summation order, so it is accurate to f32
 // rounding (well inside 1e-5 relative) but not bit-identical.
 #include <cuda_runtime.h>
+#include <atomic>
 #include <cstdint>
 #include "mcu_kernels.h"
 #include "mcu_math.cuh"
@@ -397,7 +398,10 @@ constexpr int kMaxDevices = 64;
 static __device__ __align__(256) float g_skinny_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
 
 namespace {
-void* g_noalloc_addr[kMaxDevices];
+// Looked up once per device and kept for the life of the process (a cudaDeviceReset would make
+// the address stale; the entry point does not support one).  Atomic: host threads may race on
+// the first call.
+std::atomic<void*> g_noalloc_addr[kMaxDevices];
 }  // namespace
 
 extern "C" size_t mcu_skinny_noalloc_limit(void) { return kNoAllocScratchBytes; }
@@ -411,12 +415,12 @@ extern "C" int mcu_skinny_noalloc_scratch(void** out) {
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return (int)e;
     if (dev < 0 || dev >= kMaxDevices) return (int)cudaErrorInvalidDevice;
-    if (!g_noalloc_addr[dev]) {
-        void* p = nullptr;
+    void* p = g_noalloc_addr[dev].load(std::memory_order_acquire);
+    if (!p) {
         e = cudaGetSymbolAddress(&p, g_skinny_noalloc_scratch);
         if (e != cudaSuccess) return (int)e;
-        g_noalloc_addr[dev] = p;
+        g_noalloc_addr[dev].store(p, std::memory_order_release);  // every thread finds the same address
     }
-    *out = g_noalloc_addr[dev];
+    *out = p;
     return (int)cudaSuccess;
 }

@@ -299,6 +299,16 @@ struct Epi {
     const int* row_exp; // f16 split: power-of-two exponents of X's rows ([B*M]) and Y's columns ([B*N])
     const int* col_exp;
     int bias_map;       // the bias is also described by map_bias (32 x 32 boxes): staged through shared memory
+    int bias_zero;      // no bias read: the bias is known to be zero, and x + 0.0f (-0 -> +0) stands for it
+    // f16 split: floor-element counts of X's rows ([B*M]) and of Y's 32-column chunks
+    // ([B*ceil(N/32)]), and where outputs that fail the floor check are listed (floor_check)
+    const int* row_floor;
+    const int* col_floor32;
+    int2* chk_list;     // (global row, column) of each listed output, up to chk_cap
+    int* chk_count;     // [0] outputs listed (may pass chk_cap), [1] rows listed
+    int* chk_rflag;     // [B*M] a row has a listed output
+    int* chk_rows;      // [B*M] those rows
+    int chk_cap;
 };
 
 __device__ __forceinline__ float rna_tf32_dev(float x) {
@@ -312,6 +322,28 @@ __device__ __forceinline__ float gelu_lane(float x) {
     // elementwise GELU kernel (lane_op<OP_GELU>), so fused and unfused layers agree bit for bit
     return mcu::lane_op<mcu::OP_GELU>(x);
 }
+
+// The floor of the f16 split.  For a scaled element s = x * 2^e (row maximum in [2^14, 2^15)),
+// hi + lo represents s within 2^-22 |s| while lo is a normal f16, i.e. for |s| >= 2^-3; below
+// that ("floor elements") lo is subnormal and the error is at most 2^-25, absolute, in scaled
+// units.  So an output's error beyond the 2^-22-relative terms is at most
+//     2^-25 (nF_i 2^-e_i max_k|y_kj| + nG_j 2^-f_j max_k|x_ik|) <= 2^-10 2^-(e_i+f_j) (nF_i + nG_j)
+// (nF_i, nG_j: floor elements of row i of X and column j of Y; the maxima are below 2^(15-e)),
+// which is at most 2^-20 of the output whenever its scaled sum |acc| = 2^(e_i+f_j) |C_ij| is at
+// least 2^10 (nF_i + nG_j).  Outputs below that are listed and recomputed exactly (fix_outputs):
+// in ordinary data a handful per product, for a row whose large entries meet zeros in Y (all
+// its products then carried by elements far below its maximum) the whole row.  nG_j is bounded
+// by the count of its 32-column chunk, so all checks of an output use the same bound.
+__device__ __forceinline__ float floor_threshold(int n) { return n > 0 ? 1024.0f * (float)n : 0.0f; }
+
+__device__ __noinline__ void list_output(int2* list, int* count, int* rflag, int* rows, int cap, int64_t grow,
+                                        int64_t col) {
+    const int i = atomicAdd(count, 1);
+    if (i < cap) list[i] = make_int2((int)grow, (int)col);
+    if (atomicExch(rflag + grow, 1) == 0) rows[atomicAdd(count + 1, 1)] = (int)grow;
+}
+#define LIST_OUTPUT(epi, grow, col) \
+    list_output((epi).chk_list, (epi).chk_count, (epi).chk_rflag, (epi).chk_rows, (epi).chk_cap, (grow), (col))
 
 // Work unit u -> tile t, part, and its K stages [kbeg, kend) (see the work-unit comment in gemm_3x).
 __device__ __forceinline__ void decode_unit(int u, int split_from, int kparts, int kpc, int nk, int& t, int& part,
@@ -336,8 +368,8 @@ __global__ void __maxnreg__(kLaunchRegs)
     gemm_3x(const __grid_constant__ CUtensorMap map_xhi, const __grid_constant__ CUtensorMap map_xlo,
                 const __grid_constant__ CUtensorMap map_yhi, const __grid_constant__ CUtensorMap map_ylo,
                 const __grid_constant__ CUtensorMap map_bias, float* __restrict__ r, int M, int N, int Kp, int64_t ldr, int* status, const Epi epi,
-                int seg_kb, int batch, int kparts, int kpc, int split_from, float* __restrict__ part_out,
-                float* __restrict__ tail_out) {
+                int seg_kb, int first_kb, int batch, int kparts, int kpc, int split_from, float* __restrict__ part_out,
+                float* __restrict__ tail_out, int stall) {
     using C = Cfg<BN, STAGES, PAIR>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -426,7 +458,10 @@ __global__ void __maxnreg__(kLaunchRegs)
                 const int yrow = bt * N + nb * BN + (int)rank * (BN / 2) * (PAIR ? 1 : 0);
                 for (int kb = kbeg; kb < kend; ++kb, ++it) {
                     const uint32_t s = it % STAGES, round = it / STAGES;
-                    if (!mbar_wait(&empty[s], (round & 1) ^ 1, ab, 1)) goto done;
+                    // stall (a test of the bounded waits): the first wait is for a phase that
+                    // nothing completes, so it expires before any copy or MMA is issued
+                    const uint32_t want = ((round & 1) ^ 1) ^ (stall && it == 0 ? 1u : 0u);
+                    if (!mbar_wait(&empty[s], want, ab, 1)) goto done;
                     uint8_t* st = ring + s * C::STAGE_BYTES;
                     if constexpr (PAIR) {
                         // both CTAs' loads complete on the leader's full barrier, which expects both
@@ -453,12 +488,12 @@ __global__ void __maxnreg__(kLaunchRegs)
             for (int u = unit; u < work; u += units) {
                 int t, part, kbeg, kend;
                 decode_unit(u, split_from, kparts, kpc, nk, t, part, kbeg, kend);
-                for (int kb0 = kbeg; kb0 < kend; kb0 += seg_kb, ++gseg) {
+                for (int kb0 = kbeg, sl = first_kb; kb0 < kend; kb0 += sl, sl = seg_kb, ++gseg) {
                     const uint32_t b = gseg & 1, bround = gseg >> 1;
                     if (!mbar_wait(&acc_empty[b], (bround & 1) ^ 1, ab, 2)) goto done;
                     tc_fence_after();
                     const uint32_t d = tmem_base + b * BN;
-                    const int kb1 = min(kb0 + seg_kb, kend);
+                    const int kb1 = min(kb0 + sl, kend);
                     for (int kb = kb0; kb < kb1; ++kb, ++it) {
                         const uint32_t s = it % STAGES, round = it / STAGES;
                         if (!mbar_wait(&full[s], round & 1, ab, 3)) goto done;
@@ -528,9 +563,9 @@ __global__ void __maxnreg__(kLaunchRegs)
             bool staged0 = false;
             // segment sums are added in registers with round-to-nearest
             float sum[HC];
-            for (int kb0 = kbeg; kb0 < kend; kb0 += seg_kb, ++gseg) {
+            for (int kb0 = kbeg, sl = first_kb; kb0 < kend; kb0 += sl, sl = seg_kb, ++gseg) {
                 const uint32_t b = gseg & 1, bround = gseg >> 1;
-                if (map_ok && !staged0 && kb0 + seg_kb >= kend && colh + 32 <= N) {
+                if (map_ok && !staged0 && kb0 + sl >= kend && colh + 32 <= N) {
                     stage_bias(colh);  // the first chunk loads while the last segment accumulates
                     staged0 = true;
                 }
@@ -584,10 +619,21 @@ __global__ void __maxnreg__(kLaunchRegs)
                         bphase ^= 1;
                     }
                     const int* ce = F16 ? epi.col_exp + (int64_t)bt * N + cb : nullptr;
+                    float thr = 0.0f;  // floor check of this lane's row (threshold on the scaled sums)
+                    if constexpr (F16)
+                        thr = row_ok ? floor_threshold(__ldg(epi.row_floor + row) + __ldg(epi.col_floor32 + cb / 32)) : 0.0f;
 #pragma unroll
                     for (int j = 0; j < 32; j += 4) {
                         const uint32_t slot = sbuf + lane * 128 + (((j >> 2) ^ (lane & 7)) << 4);
                         float a[4] = {sum[c * 32 + j], sum[c * 32 + j + 1], sum[c * 32 + j + 2], sum[c * 32 + j + 3]};
+                        if constexpr (F16) {
+                            const bool lo4 = fabsf(a[0]) < thr || fabsf(a[1]) < thr || fabsf(a[2]) < thr || fabsf(a[3]) < thr;
+                            if (__any_sync(0xffffffffu, lo4)) {  // rare: listed for the exact recomputation
+#pragma unroll
+                                for (int u = 0; u < 4; ++u)
+                                    if (fabsf(a[u]) < thr && cb + j + u < N) LIST_OUTPUT(epi, row, cb + j + u);
+                            }
+                        }
                         if constexpr (F16) {  // undo the operands' power-of-two scaling
                             int e[4];
 #pragma unroll
@@ -615,6 +661,10 @@ __global__ void __maxnreg__(kLaunchRegs)
                         const bool vq = vec && col + 4 <= N;
                         const bool gbias = epi.bias && !staged;
                         float a[4] = {s4.x, s4.y, s4.z, s4.w};
+                        if (epi.bias_zero) {
+#pragma unroll
+                            for (int u = 0; u < 4; ++u) a[u] = __fadd_rn(a[u], 0.0f);
+                        }
                         if (gbias) {
                             const float* q = epi.bias + (int64_t)grow * N + col;
                             if (vq && bvec) {
@@ -676,11 +726,24 @@ __global__ void __maxnreg__(kLaunchRegs)
                                     (colh - nb * BN)
                               : rb + (int64_t)bt * M * ldr + (int64_t)rowc * ldr + colh;
             const bool vec_u = tail || vec;  // the tail buffer's rows are BN floats, 16-byte aligned
+            // whole-tile outputs get the floor check here; split tiles' parts after their sum
+            const bool check = F16 && !tail && !(kparts > 1 && split_from == 0);
 #pragma unroll
             for (int c = 0; c < HC / 32; ++c) {
                 float* v = sum + c * 32;
                 const int cb = colh + c * 32;
                 const bool full = cb + 32 <= N;
+                if (F16 && check && cb < N && row_ok) {
+                    const float thr = floor_threshold(__ldg(epi.row_floor + (int64_t)bt * M + row) +
+                                                      __ldg(epi.col_floor32 + (int64_t)bt * ((N + 31) / 32) + cb / 32));
+                    uint32_t low = 0;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) low |= (fabsf(v[j]) < thr ? 1u : 0u) << j;
+                    for (uint32_t m = low; m; m &= m - 1) {
+                        const int j = __ffs(m) - 1;
+                        if (cb + j < N) LIST_OUTPUT(epi, (int64_t)bt * M + row, cb + j);
+                    }
+                }
                 const bool fast = full && vec_u && (!F16 || ((((int64_t)bt * N) & 3) == 0));
                 if (fast) {
                     // one float4 at a time through unscale and store: short live ranges keep the
@@ -808,17 +871,20 @@ __device__ __forceinline__ uint32_t pack2(__half a, __half b) {
     return (uint32_t)__half_as_ushort(a) | ((uint32_t)__half_as_ushort(b) << 16);
 }
 
-__device__ __forceinline__ void split_f16(float v, float scale, __half& hi, __half& lo) {
-    const float s = __fmul_rn(v, scale);  // exact: a power of two
+// Returns whether v is a floor element (below).
+__device__ __forceinline__ bool split_f16(float v, float scale, __half& hi, __half& lo) {
+    const float s = __fmul_rn(v, scale);  // exact: a power of two (unless it underflows)
     hi = __float2half_rn(s);
     lo = __float2half_rn(__fsub_rn(s, __half2float(hi)));  // the difference is exact in f32
+    return v != 0.0f && fabsf(s) < 0.125f;
 }
+
 
 // X[M][K] -> hi/lo [M][Kp] f16 and row_exp[M]: one warp per row, the row read twice
 // (the second read hits L2).
 __global__ void __launch_bounds__(256) split_rows_f16(const float* __restrict__ x, __half* __restrict__ hi,
                                                       __half* __restrict__ lo, int* __restrict__ row_exp, int64_t M,
-                                                      int64_t K, int64_t Kp) {
+                                                      int64_t K, int64_t Kp, int* __restrict__ row_floor) {
     const int64_t m = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (m >= M) return;
@@ -841,6 +907,7 @@ __global__ void __launch_bounds__(256) split_rows_f16(const float* __restrict__ 
     if (lane == 0) row_exp[m] = e;
     __half* hr = hi + m * Kp;
     __half* lr = lo + m * Kp;
+    int nf = 0;
     for (int64_t k = lane * 4; k < Kp; k += 128) {
         float v[4];
         if (vec && k + 4 <= K) {
@@ -852,10 +919,12 @@ __global__ void __launch_bounds__(256) split_rows_f16(const float* __restrict__ 
         }
         __half h[4], l[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) split_f16(v[j], scale, h[j], l[j]);
+        for (int j = 0; j < 4; ++j) nf += split_f16(v[j], scale, h[j], l[j]);
         *(uint2*)(hr + k) = make_uint2(pack2(h[0], h[1]), pack2(h[2], h[3]));
         *(uint2*)(lr + k) = make_uint2(pack2(l[0], l[1]), pack2(l[2], l[3]));
     }
+    nf = __reduce_add_sync(0xffffffffu, nf);
+    if (lane == 0) row_floor[m] = nf;
 }
 
 // The same split for rows of up to 128*V elements (V <= 8): one warp per row, the row in
@@ -863,7 +932,7 @@ __global__ void __launch_bounds__(256) split_rows_f16(const float* __restrict__ 
 template <int V>
 __global__ void __launch_bounds__(256) split_rows_f16_warp(const float* __restrict__ x, __half* __restrict__ hi,
                                                            __half* __restrict__ lo, int* __restrict__ row_exp,
-                                                           int64_t M, int64_t K, int64_t Kp) {
+                                                           int64_t M, int64_t K, int64_t Kp, int* __restrict__ row_floor) {
     const int64_t m = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (m >= M) return;
@@ -891,18 +960,21 @@ __global__ void __launch_bounds__(256) split_rows_f16_warp(const float* __restri
     if (lane == 0) row_exp[m] = e;
     __half* hr = hi + m * Kp;
     __half* lr = lo + m * Kp;
+    int nf = 0;
 #pragma unroll
     for (int i = 0; i < V; ++i) {
         const int64_t k = ((int64_t)i * 32 + lane) * 4;
         if (k >= Kp) break;
         __half h[4], l[4];
-        split_f16(v[i].x, scale, h[0], l[0]);
-        split_f16(v[i].y, scale, h[1], l[1]);
-        split_f16(v[i].z, scale, h[2], l[2]);
-        split_f16(v[i].w, scale, h[3], l[3]);
+        nf += split_f16(v[i].x, scale, h[0], l[0]);
+        nf += split_f16(v[i].y, scale, h[1], l[1]);
+        nf += split_f16(v[i].z, scale, h[2], l[2]);
+        nf += split_f16(v[i].w, scale, h[3], l[3]);
         *(uint2*)(hr + k) = make_uint2(pack2(h[0], h[1]), pack2(h[2], h[3]));
         *(uint2*)(lr + k) = make_uint2(pack2(l[0], l[1]), pack2(l[2], l[3]));
     }
+    nf = __reduce_add_sync(0xffffffffu, nf);
+    if (lane == 0) row_floor[m] = nf;
 }
 
 // The same split for rows of up to 1024*V elements: one 256-thread CTA per row keeps the row
@@ -910,8 +982,9 @@ __global__ void __launch_bounds__(256) split_rows_f16_warp(const float* __restri
 template <int V>
 __global__ void __launch_bounds__(256) split_rows_f16_block(const float* __restrict__ x, __half* __restrict__ hi,
                                                             __half* __restrict__ lo, int* __restrict__ row_exp,
-                                                            int64_t K, int64_t Kp) {
+                                                            int64_t K, int64_t Kp, int* __restrict__ row_floor) {
     __shared__ float wmax[8];
+    __shared__ int wfloor[8];
     const int64_t m = blockIdx.x;
     const float* xr = x + m * K;
     const bool vec = (K % 4 == 0) && ((((uintptr_t)x) & 15) == 0);
@@ -942,23 +1015,42 @@ __global__ void __launch_bounds__(256) split_rows_f16_block(const float* __restr
     if (threadIdx.x == 0) row_exp[m] = e;
     __half* hr = hi + m * Kp;
     __half* lr = lo + m * Kp;
+    int nf = 0;
 #pragma unroll
     for (int i = 0; i < V; ++i) {
         const int64_t k = ((int64_t)i * 256 + threadIdx.x) * 4;
         if (k >= Kp) break;
         __half h[4], l[4];
-        split_f16(v[i].x, scale, h[0], l[0]);
-        split_f16(v[i].y, scale, h[1], l[1]);
-        split_f16(v[i].z, scale, h[2], l[2]);
-        split_f16(v[i].w, scale, h[3], l[3]);
+        nf += split_f16(v[i].x, scale, h[0], l[0]);
+        nf += split_f16(v[i].y, scale, h[1], l[1]);
+        nf += split_f16(v[i].z, scale, h[2], l[2]);
+        nf += split_f16(v[i].w, scale, h[3], l[3]);
         *(uint2*)(hr + k) = make_uint2(pack2(h[0], h[1]), pack2(h[2], h[3]));
         *(uint2*)(lr + k) = make_uint2(pack2(l[0], l[1]), pack2(l[2], l[3]));
+    }
+    nf = __reduce_add_sync(0xffffffffu, nf);
+    if ((threadIdx.x & 31) == 0) wfloor[threadIdx.x >> 5] = nf;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int t = 0;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) t += wfloor[w];
+        row_floor[m] = t;
     }
 }
 
 // Split-K: r = part[0] + part[1] + ... in that order (f32 adds, so the result does not
 // depend on which parts finished first), then a fused layer's bias, GELU and tf32 operand
 // split exactly as the GEMM epilogue (and the separate ADD and GELU ops) apply them.
+// Floor check of a finished (unscaled) output at flat index i of an [M][N] result, batch 0 (the
+// same bound as the GEMM epilogue's, in unscaled units).  M * N < 2^31 for the products that
+// reach it (split along K: fewer tiles than CTAs; last-wave tails: under 8 waves of tiles).
+__device__ __forceinline__ void check_output(const Epi& epi, float c, int64_t row, int64_t col, int64_t N) {
+    const int n = epi.row_floor[row] + epi.col_floor32[col >> 5];
+    if (n > 0 && fabsf(c) < unscale(floor_threshold(n), epi.row_exp[row] + epi.col_exp[col]))
+        LIST_OUTPUT(epi, row, col);
+}
+
 __global__ void __launch_bounds__(256) sum_parts(float* __restrict__ r, const float* __restrict__ part, int64_t M,
                                                  int64_t N, int parts, const Epi epi) {
     const int64_t n = M * N;
@@ -970,10 +1062,24 @@ __global__ void __launch_bounds__(256) sum_parts(float* __restrict__ r, const fl
                 a.x = __fadd_rn(a.x, b.x); a.y = __fadd_rn(a.y, b.y);
                 a.z = __fadd_rn(a.z, b.z); a.w = __fadd_rn(a.w, b.w);
             }
+            if (epi.chk_count) {
+                const uint32_t e0 = (uint32_t)(4 * i), row = e0 / (uint32_t)N;
+                uint32_t col = e0 - row * (uint32_t)N;
+                const float v[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const uint32_t rr = col < (uint32_t)N ? row : row + 1, cc = col < (uint32_t)N ? col : col - (uint32_t)N;
+                    check_output(epi, v[u], rr, cc, N);
+                    ++col;
+                }
+            }
             if (epi.bias) {
                 const float4 b = ((const float4*)epi.bias)[i];
                 a.x = __fadd_rn(a.x, b.x); a.y = __fadd_rn(a.y, b.y);
                 a.z = __fadd_rn(a.z, b.z); a.w = __fadd_rn(a.w, b.w);
+            } else if (epi.bias_zero) {
+                a.x = __fadd_rn(a.x, 0.0f); a.y = __fadd_rn(a.y, 0.0f);
+                a.z = __fadd_rn(a.z, 0.0f); a.w = __fadd_rn(a.w, 0.0f);
             }
             if (epi.act == 1) {
                 a.x = gelu_lane(a.x); a.y = gelu_lane(a.y); a.z = gelu_lane(a.z); a.w = gelu_lane(a.w);
@@ -985,11 +1091,16 @@ __global__ void __launch_bounds__(256) sum_parts(float* __restrict__ r, const fl
     for (int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x; i < n; i += (int64_t)gridDim.x * 256) {
         float a = __ldcs(part + i);
         for (int p = 1; p < parts; ++p) a = __fadd_rn(a, __ldcs(part + (int64_t)p * n + i));
+        if (epi.chk_count) {
+            const uint32_t row = (uint32_t)i / (uint32_t)N;
+            check_output(epi, a, row, (uint32_t)i - row * (uint32_t)N, N);
+        }
         if (epi.bias) a = __fadd_rn(a, epi.bias[i]);
+        else if (epi.bias_zero) a = __fadd_rn(a, 0.0f);
         if (epi.act == 1) a = gelu_lane(a);
         r[i] = a;
         if (epi.out_hi) {
-            const int64_t row = i / N, col = i - row * N;
+            const int64_t row = (uint32_t)i / (uint32_t)N, col = i - row * N;  // M * N < 2^31
             const float hh = rna_tf32_dev(a);
             epi.out_hi[row * epi.kp_out + col] = hh;
             epi.out_lo[row * epi.kp_out + col] = rna_tf32_dev(a - hh);
@@ -1002,7 +1113,8 @@ __global__ void __launch_bounds__(256) sum_parts(float* __restrict__ r, const fl
 // four consecutive columns of a tile row.
 template <int BN>
 __global__ void __launch_bounds__(256) sum_tail(float* __restrict__ r, const float* __restrict__ tail, int M, int N,
-                                                int TM, int num_m, int num_n, int split_from, int kparts) {
+                                                int TM, int num_m, int num_n, int split_from, int kparts,
+                                                const Epi chk) {
     const int per_tile = TM * BN / 4;
     const int64_t idx = (int64_t)blockIdx.x * 256 + threadIdx.x;
     const int j = (int)(idx / per_tile);
@@ -1021,6 +1133,17 @@ __global__ void __launch_bounds__(256) sum_tail(float* __restrict__ r, const flo
         const float4 b = __ldcs((const float4*)(p + (int64_t)q * TM * BN));
         a.x = __fadd_rn(a.x, b.x); a.y = __fadd_rn(a.y, b.y);
         a.z = __fadd_rn(a.z, b.z); a.w = __fadd_rn(a.w, b.w);
+    }
+    if (chk.chk_count) {  // f16 split: the floor check of the split tiles' outputs
+        const float v[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            if (col + u >= N) break;
+            const int64_t grow = (int64_t)bt * M + row, gcol = (int64_t)bt * N + col + u;
+            const int nf = chk.row_floor[grow] + chk.col_floor32[(int64_t)bt * ((N + 31) / 32) + ((col + u) >> 5)];
+            if (nf > 0 && fabsf(v[u]) < unscale(floor_threshold(nf), chk.row_exp[grow] + chk.col_exp[gcol]))
+                LIST_OUTPUT(chk, grow, col + u);
+        }
     }
     float* o = r + (int64_t)row * N + col;
     if ((N & 3) == 0 && (((uintptr_t)r) & 15) == 0 && col + 4 <= N) {
@@ -1087,7 +1210,8 @@ __global__ void __launch_bounds__(256) col_absmax(const float* __restrict__ y, u
 // column as one 16-byte word of hi and one of lo.  col_exp[N] is written by the first k-block.
 __global__ void __launch_bounds__(256) split_cols_t_f16(const float* __restrict__ y, const unsigned* __restrict__ cmax,
                                                         __half* __restrict__ hi, __half* __restrict__ lo,
-                                                        int* __restrict__ col_exp, int64_t K, int64_t N, int64_t Kp) {
+                                                        int* __restrict__ col_exp, int64_t K, int64_t N, int64_t Kp,
+                                                        int* __restrict__ col_floor32) {
     __shared__ float tile[64][65];
     __shared__ float scl[64];
     y += (int64_t)blockIdx.z * K * N;
@@ -1136,12 +1260,56 @@ __global__ void __launch_bounds__(256) split_cols_t_f16(const float* __restrict_
         if (n < N && k < Kp) {  // Kp is a multiple of 32: k .. k + 7 are all inside
             const float sc = scl[j];
             __half h[8], l[8];
+            int nf = 0;
 #pragma unroll
-            for (int q = 0; q < 8; ++q) split_f16(tile[kc + q][j], sc, h[q], l[q]);
+            for (int q = 0; q < 8; ++q) nf += split_f16(tile[kc + q][j], sc, h[q], l[q]);
+            // floor elements, counted per 32-column chunk (zeroed before the split; partial
+            // counts of every k-block add up)
+            if (nf) atomicAdd(col_floor32 + (int64_t)blockIdx.z * ((N + 31) / 32) + n / 32, nf);
             *(uint4*)(hi + n * Kp + k) = make_uint4(pack2(h[0], h[1]), pack2(h[2], h[3]), pack2(h[4], h[5]),
                                                     pack2(h[6], h[7]));
             *(uint4*)(lo + n * Kp + k) = make_uint4(pack2(l[0], l[1]), pack2(l[2], l[3]), pack2(l[4], l[5]),
                                                     pack2(l[6], l[7]));
+        }
+    }
+}
+
+// The outputs listed by the floor check, recomputed exactly: one warp per output, the lanes'
+// products of f32 (exact in double) summed in double over k = lane, lane + 32, ..., then across
+// lanes in a fixed tree, rounded once; a fused layer's bias and GELU follow, as in the epilogue.
+// When more outputs were listed than the list holds, every output of the listed rows is
+// recomputed.  Either way the result depends only on the inputs.
+__global__ void __launch_bounds__(256) fix_outputs(const float* __restrict__ x, const float* __restrict__ y,
+                                                   float* __restrict__ r, int64_t M, int64_t K, int64_t N,
+                                                   const Epi epi) {
+    const int listed = epi.chk_count[0];
+    const bool by_rows = listed > epi.chk_cap;
+    const int64_t items = by_rows ? (int64_t)epi.chk_count[1] * N : (int64_t)listed;
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t)gridDim.x * 8;
+    for (int64_t it = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); it < items; it += warps) {
+        int64_t gi, j;
+        if (by_rows) {
+            gi = epi.chk_rows[it / N];
+            j = it - (it / N) * N;
+        } else {
+            const int2 p = epi.chk_list[it];
+            gi = p.x;
+            j = p.y;
+        }
+        const int64_t bt = gi / M;
+        const float* xr = x + gi * K;
+        const float* yc = y + bt * K * N + j;
+        double acc = 0.0;
+        for (int64_t k = lane; k < K; k += 32) acc += (double)__ldg(xr + k) * (double)__ldg(yc + k * N);
+#pragma unroll
+        for (int o = 16; o; o >>= 1) acc += __shfl_down_sync(0xffffffffu, acc, o);
+        if (lane == 0) {
+            float c = (float)acc;
+            if (epi.bias) c = __fadd_rn(c, epi.bias[gi * N + j]);
+            else if (epi.bias_zero) c = __fadd_rn(c, 0.0f);
+            if (epi.act == 1) c = gelu_lane(c);
+            r[gi * N + j] = c;
         }
     }
 }
@@ -1178,9 +1346,13 @@ int64_t round_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
 
 // Scratch of one product: split operands, and for the f16 split the row/column
 // exponents and column maxima.  Sized for the tf32 split, which needs the most.
+constexpr int kCheckCap = 1 << 16;  // outputs the floor check lists individually
+
 struct Layout {
     int64_t kp;
     size_t xhi, xlo, yhi, ylo, rexp, cexp, cmax, parts, tail, total;
+    // f16 split's floor check: [cmax | cfloor32 | counters | chk_rflag] is cleared by one memset
+    size_t cfloor32, counters, chk_rflag, clear_bytes, rfloor, chk_rows, chk_list;
     int kparts;  // split-K factor of an unfused single product (1: none)
     int kpc;     // its ring stages per part
 };
@@ -1273,7 +1445,14 @@ Layout layout(int64_t B, int64_t M, int64_t K, int64_t N, bool f16) {
     l.rexp = 2 * xs + 2 * ys;
     l.cexp = l.rexp + (size_t)round_up(rows * 4, 256);
     l.cmax = l.cexp + (size_t)round_up(cols * 4, 256);
-    l.parts = l.cmax + (size_t)round_up(cols * 4, 256);
+    l.cfloor32 = l.cmax + (size_t)round_up(cols * 4, 256);
+    l.counters = l.cfloor32 + (size_t)round_up(B * ((N + 31) / 32) * 4, 256);
+    l.chk_rflag = l.counters + 256;
+    l.clear_bytes = l.chk_rflag + (size_t)round_up(rows * 4, 256) - l.cmax;
+    l.rfloor = l.chk_rflag + (size_t)round_up(rows * 4, 256);
+    l.chk_rows = l.rfloor + (size_t)round_up(rows * 4, 256);
+    l.chk_list = l.chk_rows + (size_t)round_up(rows * 4, 256);
+    l.parts = l.chk_list + (size_t)kCheckCap * 8;
     l.kparts = B == 1 ? choose_parts(M, K, N, f16) : 1;
     {
         const int64_t nk = l.kp / (f16 ? BK16 : BK);
@@ -1309,6 +1488,21 @@ int segment_kb(bool f16) {
     return seg <= 0 ? (1 << 30) : (seg + ke - 1) / ke;
 }
 
+// K of a tile's first segment (MAG_CUDA_TC_SEGMENT_FIRST; default: the segment length), in ring
+// stages.  The epilogue's stores of one tile overlap the MMAs of the next tile's first two
+// segments, so a long first segment hides them while short later segments keep the truncation
+// of the tensor-core accumulator small.
+int segment_first_kb(bool f16) {
+    static int k = -2;
+    if (k == -2) {
+        const char* e = getenv("MAG_CUDA_TC_SEGMENT_FIRST");
+        k = (e && *e) ? atoi(e) : -1;
+    }
+    if (k == -1) return segment_kb(f16);
+    const int ke = f16 ? BK16 : BK;
+    return k <= 0 ? (1 << 30) : (k + ke - 1) / ke;
+}
+
 // 2-D map over the fused epilogue's row-major [M][N] f32 bias, box 32 x 32, 128-byte swizzle.
 bool make_bias_map(CUtensorMap* m, const float* bias, int64_t M, int64_t N) {
     auto fn = encode_fn();
@@ -1320,6 +1514,13 @@ bool make_bias_map(CUtensorMap* m, const float* bias, int64_t M, int64_t N) {
     return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void*)bias, dims, strides, box, estr,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// MAG_CUDA_TC_TEST_STALL=1 makes the GEMM's first wait one that never completes (read at each
+// launch): a test of the bounded waits and the status word without any fault.
+int test_stall() {
+    const char* e = getenv("MAG_CUDA_TC_TEST_STALL");
+    return e && e[0] == '1';
 }
 
 template <bool FUSED, bool F16, bool PAIR>
@@ -1339,7 +1540,8 @@ int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c
     if constexpr (!PAIR) {
         const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
         kern<<<grid, kThreads, smem, st>>>(a, b, c, d, bias, r, (int)M, (int)N, (int)kp, (int64_t)N, status, epi,
-                                           segment_kb(F16), (int)B, kparts, kpc, split_from, part_out, tail_out);
+                                           segment_kb(F16), segment_first_kb(F16), (int)B, kparts, kpc, split_from,
+                                           part_out, tail_out, test_stall());
         return (int)cudaGetLastError();
     } else {
         cudaLaunchConfig_t cfg = {};
@@ -1362,7 +1564,8 @@ int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c
         const int64_t clusters = tiles < max_clusters ? tiles : max_clusters;
         cfg.gridDim = dim3((unsigned)(2 * clusters));
         e = cudaLaunchKernelEx(&cfg, kern, a, b, c, d, bias, r, (int)M, (int)N, (int)kp, (int64_t)N, status, epi,
-                               segment_kb(F16), (int)B, kparts, kpc, split_from, part_out, tail_out);
+                               segment_kb(F16), segment_first_kb(F16), (int)B, kparts, kpc, split_from, part_out,
+                               tail_out, test_stall());
         return (int)e;
     }
 }
@@ -1381,7 +1584,7 @@ extern "C" int mcu_matmul_tc_kernels(int64_t M, int64_t K, int64_t N, int f16, i
     const int split = f16 ? 3 : ((flags & 1) ? 1 : 2);  // operand split kernels
     const bool parts = choose_parts(M, K, N, f16 != 0) > 1;
     const bool tail = !parts && !(flags & 2) && plan_tail(1, M, K, N, f16 != 0).parts > 1;
-    return split + 1 + (parts || tail ? 1 : 0);
+    return split + 1 + (parts || tail ? 1 : 0) + (f16 ? 1 : 0);  // f16: the floor check's recomputation
 }
 
 static int launch_tc(float* r, const float* x, const float* y, int64_t B, int64_t M, int64_t K, int64_t N,
@@ -1398,7 +1601,7 @@ extern "C" size_t mcu_matmul_tc_batched_scratch_bytes(int64_t B, int64_t M, int6
 }
 
 extern "C" int mcu_matmul_tc_batched_kernels(int64_t B, int64_t M, int64_t K, int64_t N, int f16) {
-    return (f16 ? 3 : 2) + 1 + (plan_tail(B, M, K, N, f16 != 0).parts > 1 ? 1 : 0);
+    return (f16 ? 4 : 2) + 1 + (plan_tail(B, M, K, N, f16 != 0).parts > 1 ? 1 : 0);
 }
 
 extern "C" int mcu_launch_matmul_tc_batched(float* r, const float* x, const float* y, int64_t B, int64_t M, int64_t K,
@@ -1423,21 +1626,26 @@ static int launch_tc(float* r, const float* x, const float* y, int64_t B, int64_
     // the tf32 split can take X already split by the previous layer's epilogue; the f16
     // split scales whole rows, so it always splits X itself
     const bool presplit = !f16 && ep && ep->a_hi && ep->a_lo;
+    int* rfloor = (int*)(base + l.rfloor);
+    int* cfloor32 = (int*)(base + l.cfloor32);
     if (presplit) {
         xhi = (void*)ep->a_hi;
         xlo = (void*)ep->a_lo;
     } else if (f16) {
+        // column maxima, floor counts of column chunks, the check's counters and row flags start at zero
+        cudaError_t e = cudaMemsetAsync(cmax, 0, l.clear_bytes, st);
+        if (e != cudaSuccess) return (int)e;
         __half *h16 = (__half*)xhi, *l16 = (__half*)xlo;
         const unsigned rows = (unsigned)(B * M);
         const unsigned wrows = (rows + 7) / 8;
-        if (l.kp <= 128) split_rows_f16_warp<1><<<wrows, 256, 0, st>>>(x, h16, l16, rexp, B * M, K, l.kp);
-        else if (l.kp <= 256) split_rows_f16_warp<2><<<wrows, 256, 0, st>>>(x, h16, l16, rexp, B * M, K, l.kp);
-        else if (l.kp <= 512) split_rows_f16_warp<4><<<wrows, 256, 0, st>>>(x, h16, l16, rexp, B * M, K, l.kp);
-        else if (l.kp <= 1024) split_rows_f16_warp<8><<<wrows, 256, 0, st>>>(x, h16, l16, rexp, B * M, K, l.kp);
-        else if (l.kp <= 2048) split_rows_f16_block<2><<<rows, 256, 0, st>>>(x, h16, l16, rexp, K, l.kp);
-        else if (l.kp <= 4096) split_rows_f16_block<4><<<rows, 256, 0, st>>>(x, h16, l16, rexp, K, l.kp);
-        else if (l.kp <= 8192) split_rows_f16_block<8><<<rows, 256, 0, st>>>(x, h16, l16, rexp, K, l.kp);
-        else split_rows_f16<<<(unsigned)((B * M + 7) / 8), 256, 0, st>>>(x, h16, l16, rexp, B * M, K, l.kp);
+        if (l.kp <= 128) split_rows_f16_warp<1><<<wrows, 256, 0, st>>>(x, h16, l16, rexp, B * M, K, l.kp, rfloor);
+        else if (l.kp <= 256) split_rows_f16_warp<2><<<wrows, 256, 0, st>>>(x, h16, l16, rexp, B * M, K, l.kp, rfloor);
+        else if (l.kp <= 512) split_rows_f16_warp<4><<<wrows, 256, 0, st>>>(x, h16, l16, rexp, B * M, K, l.kp, rfloor);
+        else if (l.kp <= 1024) split_rows_f16_warp<8><<<wrows, 256, 0, st>>>(x, h16, l16, rexp, B * M, K, l.kp, rfloor);
+        else if (l.kp <= 2048) split_rows_f16_block<2><<<rows, 256, 0, st>>>(x, h16, l16, rexp, K, l.kp, rfloor);
+        else if (l.kp <= 4096) split_rows_f16_block<4><<<rows, 256, 0, st>>>(x, h16, l16, rexp, K, l.kp, rfloor);
+        else if (l.kp <= 8192) split_rows_f16_block<8><<<rows, 256, 0, st>>>(x, h16, l16, rexp, K, l.kp, rfloor);
+        else split_rows_f16<<<(unsigned)((B * M + 7) / 8), 256, 0, st>>>(x, h16, l16, rexp, B * M, K, l.kp, rfloor);
     } else {
         int64_t n = B * M * (l.kp / 4);  // X of all batches is one (B*M) x K row-major matrix
         int64_t g = (n + 255) / 256;
@@ -1445,12 +1653,10 @@ static int launch_tc(float* r, const float* x, const float* y, int64_t B, int64_
         split_rows<<<(unsigned)g, 256, 0, st>>>(x, (float*)xhi, (float*)xlo, B * M, K, l.kp);
     }
     if (f16) {
-        cudaError_t e = cudaMemsetAsync(cmax, 0, (size_t)(B * N) * 4, st);
-        if (e != cudaSuccess) return (int)e;
         dim3 gm((unsigned)((N + 127) / 128), (unsigned)((K + kColMaxRows - 1) / kColMaxRows), (unsigned)B);
         col_absmax<<<gm, 256, 0, st>>>(y, cmax, K, N);
         dim3 grid((unsigned)((N + 63) / 64), (unsigned)((l.kp + 63) / 64), (unsigned)B);
-        split_cols_t_f16<<<grid, 256, 0, st>>>(y, cmax, (__half*)yhi, (__half*)ylo, cexp, K, N, l.kp);
+        split_cols_t_f16<<<grid, 256, 0, st>>>(y, cmax, (__half*)yhi, (__half*)ylo, cexp, K, N, l.kp, cfloor32);
     } else {
         dim3 grid((unsigned)((N + 31) / 32), (unsigned)(l.kp / 32), (unsigned)B);
         split_cols_t<<<grid, 256, 0, st>>>(y, (float*)yhi, (float*)ylo, K, N, l.kp);
@@ -1462,15 +1668,38 @@ static int launch_tc(float* r, const float* x, const float* y, int64_t B, int64_
     if (!make_map(&mxh, xhi, B * M, l.kp, BM, h) || !make_map(&mxl, xlo, B * M, l.kp, BM, h) ||
         !make_map(&myh, yhi, B * N, l.kp, yrows, h) || !make_map(&myl, ylo, B * N, l.kp, yrows, h))
         return (int)cudaErrorInvalidValue;
-    Epi epi{};
-    epi.row_exp = rexp;
-    epi.col_exp = cexp;
-    const bool fused = ep && (ep->bias || ep->act || (ep->out_hi && !f16));
+    Epi chk{};  // the f16 split's floor check (no fields for tf32)
+    chk.row_exp = rexp;
+    chk.col_exp = cexp;
+    if (f16) {
+        chk.row_floor = rfloor;
+        chk.col_floor32 = cfloor32;
+        chk.chk_list = (int2*)(base + l.chk_list);
+        chk.chk_count = (int*)(base + l.counters);
+        chk.chk_rflag = (int*)(base + l.chk_rflag);
+        chk.chk_rows = (int*)(base + l.chk_rows);
+        chk.chk_cap = kCheckCap;
+    }
+    Epi epi = chk;
+    const bool fused = ep && (ep->bias || ep->bias_zero || ep->act || (ep->out_hi && !f16));
     const int kparts = B == 1 ? l.kparts : 1;
     float* part = kparts > 1 ? (float*)(base + l.parts) : nullptr;
+    // f16 split: the listed outputs recomputed exactly, after every other kernel of the product
+    auto fix = [&]() -> int {
+        if (!f16) return (int)cudaSuccess;
+        Epi fe = chk;
+        if (fused) {
+            fe.bias = ep->bias;
+            fe.bias_zero = ep->bias_zero;
+            fe.act = ep->act;
+        }
+        fix_outputs<<<(unsigned)(2 * sm_count()), 256, 0, st>>>(x, y, r, M, K, N, fe);
+        return (int)cudaGetLastError();
+    };
     if (fused && kparts == 1) {
         if (!f16 && ep->out_hi && (N % 32 != 0 || ep->kp_out != round_up(N, KPAD))) return (int)cudaErrorInvalidValue;
         epi.bias = ep->bias;
+        epi.bias_zero = ep->bias ? 0 : ep->bias_zero;
         epi.out_hi = f16 ? nullptr : ep->out_hi;
         epi.out_lo = f16 ? nullptr : ep->out_lo;
         epi.kp_out = ep->kp_out;
@@ -1478,17 +1707,18 @@ static int launch_tc(float* r, const float* x, const float* y, int64_t B, int64_
         CUtensorMap mb;
         memset(&mb, 0, sizeof(mb));
         epi.bias_map = ep->bias && make_bias_map(&mb, ep->bias, M, N);
+        int rc;
         if (pair)
-            return launch_gemm<true, true, true>(mxh, mxl, myh, myl, mb, r, M, N, l.kp, status, epi, B, st, 1, 0, 0,
-                                                 nullptr, nullptr);
-        return f16 ? launch_gemm<true, true, false>(mxh, mxl, myh, myl, mb, r, M, N, l.kp, status, epi, B, st, 1, 0, 0,
-                                                    nullptr, nullptr)
-                   : launch_gemm<true, false, false>(mxh, mxl, myh, myl, mb, r, M, N, l.kp, status, epi, B, st, 1, 0, 0,
-                                                     nullptr, nullptr);
+            rc = launch_gemm<true, true, true>(mxh, mxl, myh, myl, mb, r, M, N, l.kp, status, epi, B, st, 1, 0, 0,
+                                               nullptr, nullptr);
+        else
+            rc = f16 ? launch_gemm<true, true, false>(mxh, mxl, myh, myl, mb, r, M, N, l.kp, status, epi, B, st, 1, 0,
+                                                      0, nullptr, nullptr)
+                     : launch_gemm<true, false, false>(mxh, mxl, myh, myl, mb, r, M, N, l.kp, status, epi, B, st, 1, 0,
+                                                       0, nullptr, nullptr);
+        return rc ? rc : fix();
     }
-    Epi plain{};
-    plain.row_exp = rexp;
-    plain.col_exp = cexp;
+    Epi plain = chk;
     // an unfused single product whose last wave is mostly empty splits that wave's tiles along K
     int gparts = kparts, gkpc = l.kpc, split_from = 0;
     float* tail = nullptr;
@@ -1513,15 +1743,18 @@ static int launch_tc(float* r, const float* x, const float* y, int64_t B, int64_
         const int num_m = (int)((M + tm - 1) / tm), num_n = (int)((N + kBN - 1) / kBN);
         const int64_t ntail = B * num_m * num_n - split_from;
         const int64_t blocks = ntail * tm * kBN / 4 / 256;
-        sum_tail<kBN><<<(unsigned)blocks, 256, 0, st>>>(r, tail, (int)M, (int)N, tm, num_m, num_n, split_from, gparts);
-        return (int)cudaGetLastError();
+        sum_tail<kBN><<<(unsigned)blocks, 256, 0, st>>>(r, tail, (int)M, (int)N, tm, num_m, num_n, split_from, gparts,
+                                                         chk);
+        rc = (int)cudaGetLastError();
+        return rc ? rc : fix();
     }
-    if (kparts == 1) return rc;
+    if (kparts == 1) return fix();
     // a fused layer whose product was split: its epilogue runs after the sum, in the same order
-    Epi fe{};
+    Epi fe = chk;
     if (fused) {
         if (!f16 && ep->out_hi && (N % 32 != 0 || ep->kp_out != round_up(N, KPAD))) return (int)cudaErrorInvalidValue;
         fe.bias = ep->bias;
+        fe.bias_zero = ep->bias ? 0 : ep->bias_zero;
         fe.act = ep->act;
         fe.out_hi = f16 ? nullptr : ep->out_hi;
         fe.out_lo = f16 ? nullptr : ep->out_lo;
@@ -1531,7 +1764,8 @@ static int launch_tc(float* r, const float* x, const float* y, int64_t B, int64_
     int64_t g = (n + 255) / 256;
     if (g > 8 * sm_count()) g = 8 * sm_count();
     sum_parts<<<(unsigned)(g ? g : 1), 256, 0, st>>>(r, part, M, N, kparts, fe);
-    return (int)cudaGetLastError();
+    rc = (int)cudaGetLastError();
+    return rc ? rc : fix();
 }
 
 extern "C" int mcu_launch_matmul_tc(float* r, const float* x, const float* y, int64_t M, int64_t K, int64_t N,

@@ -113,6 +113,7 @@ typedef struct mcu_tc_epilogue {
     float* out_lo;
     int64_t kp_out;
     int act;
+    int bias_zero; /* the bias is known to be zero: add +0.0f (which maps -0 to +0) and read nothing */
 } mcu_tc_epilogue;
 size_t mcu_matmul_tc_batched_scratch_bytes(int64_t B, int64_t M, int64_t K, int64_t N);
 int mcu_matmul_tc_batched_kernels(int64_t B, int64_t M, int64_t K, int64_t N, int f16);

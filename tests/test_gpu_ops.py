@@ -358,7 +358,8 @@ def test_matmul_last_wave_split_deterministic(split):
     finally:
         dev.L.mag_cuda_set_matmul_mode(dev.p, 0)
     assert dev.L.mag_cuda_synchronize(dev.p) == 0
-    assert n1 - n0 == (5 if split == MB.TC_SPLIT_F16 else 4)  # splits, GEMM, last-wave part sum
+    # splits, GEMM, last-wave part sum (and the f16 split's floor-check recomputation)
+    assert n1 - n0 == (6 if split == MB.TC_SPLIT_F16 else 4)
     assert bits_equal(first, second).all()
     rows = o.matmul_rows(x, y, 4000, 3, k, n)  # rows of the last wave's tiles
     ref_err = np.abs(rows - first.reshape(m, n)[4000:4003].reshape(-1))
@@ -445,6 +446,41 @@ def test_fused_graph_matches_unfused_bitwise(inplace, rows, dims, split):
     assert bits_equal(fused, plain).all()
     assert bits_equal(fused2, plain2).all()
     assert not bits_equal(fused, fused2).all()
+
+
+@pytest.mark.parametrize("split", SPLITS)
+def test_fused_graph_with_zero_bias_reads_no_bias(split):
+    """Biases that nothing has written (fresh storage holds zeros) are planned as known zeros:
+    the fused epilogue adds +0.0f instead of reading them, and gives the unfused graph's bits.
+    Writing a bias changes the graph's key: the next replay is captured again with the bias
+    read, and again matches the unfused graph."""
+    dev = device()
+    _split(dev, split)
+    o = oracle()
+    rows, dims = 4096, [512, 1024, 256]
+    X, Ws, Bs, root = _build_mlp(dev, rows, dims)
+    s = o.stream(9150)
+    X.write(s.uniform(rows * dims[0], -1, 1))
+    for W, (a, b) in zip(Ws, zip(dims[:-1], dims[1:])):
+        W.write(s.normal(a * b, 0.0, (2.0 / a) ** 0.5))
+    MB.check(dev.L.mag_cuda_set_matmul_mode(dev.p, 2), "tc")
+    try:
+        dev.graph_exec(root)
+        plain0 = root.read()
+        dev.graph_exec(root, fused=True)
+        fused0 = root.read()
+        Bs[0].write(s.uniform(rows * dims[1], -0.5, 0.5))
+        dev.graph_exec(root, fused=True)
+        fused1 = root.read()
+        dev.graph_exec(root)
+        plain1 = root.read()
+    finally:
+        dev.L.mag_cuda_set_matmul_mode(dev.p, 0)
+        dev.graph_release(root)
+    assert dev.L.mag_cuda_synchronize(dev.p) == 0
+    assert bits_equal(fused0, plain0).all()
+    assert bits_equal(fused1, plain1).all()
+    assert not bits_equal(fused0, fused1).all()
 
 
 @pytest.mark.parametrize("split", SPLITS)
@@ -575,6 +611,115 @@ def test_matmul_f16_split_scaling_extremes():
     assert dev.L.mag_cuda_synchronize(dev.p) == 0
     assert np.all(got.reshape(m, n)[5] == 0) and np.all(got.reshape(m, n)[:, 9] == 0)
     assert _normwise_ok(got, x, y, m, k, n)
+
+
+def _far_operands(m, k, n, seed, rowwise):
+    """Uniform operands where a few entries lie 2^24 .. 2^40 above the rest of their row of X
+    (rowwise) or column of Y, and meet zeros in the other operand: the other elements of that
+    row (column) then carry the whole of |X||Y| for those outputs."""
+    s = oracle().stream(seed)
+    x = s.uniform(m * k, -1.0, 1.0).reshape(m, k)
+    y = s.uniform(k * n, -1.0, 1.0).reshape(k, n)
+    for i, (a, b, e) in enumerate([(3, 5, 28), (m - 1, k - 1, 40), (m // 2, k // 3, 24)]):
+        sign = -1.0 if i % 2 else 1.0
+        if rowwise:
+            x[a, b] = sign * 2.0 ** e
+            y[b, :] = 0
+        else:
+            y[b, a % n] = sign * 2.0 ** e
+            x[:, b] = 0
+    return x.astype(np.float32).reshape(-1), y.astype(np.float32).reshape(-1)
+
+
+@pytest.mark.parametrize("split", SPLITS)
+@pytest.mark.parametrize("rowwise", [True, False])
+@pytest.mark.parametrize("mkn", [(256, 1024, 64), (4096, 512, 1024)])
+def test_matmul_far_elements_within_rows_and_columns(mkn, rowwise, split):
+    """A row of X (or column of Y) with one entry 2^28 (up to 2^40) above the rest, meeting a zero
+    row of Y (zero column of X): every output of that row is carried by elements 2^28 below the
+    row's maximum, where the scaled f16 split keeps only a few significant bits.  Its floor check
+    lists those outputs and recomputes them exactly, so the bound 1e-5 of |X||Y| holds per
+    output (the split alone gave 4.6e-5 at 2^28); the tf32 split keeps them in its 8-bit
+    exponent."""
+    m, k, n = mkn
+    dev = device()
+    _split(dev, split)
+    x, y = _far_operands(m, k, n, 7800 + m, rowwise)
+    MB.check(dev.L.mag_cuda_set_matmul_mode(dev.p, 2), "tc mode")
+    try:
+        got, _, _ = run_op(dev, "MATMUL", [x, y], [(m, k), (k, n)])
+    finally:
+        dev.L.mag_cuda_set_matmul_mode(dev.p, 0)
+    assert dev.L.mag_cuda_synchronize(dev.p) == 0
+    assert _normwise_ok(got, x, y, m, k, n)
+
+
+def test_matmul_far_elements_batched():
+    """Far elements in some batches of a batched product (rows of X in batch 3, a column of Y in
+    batch 6): each batch's outputs stay within 1e-5 of |X||Y|."""
+    dev = device()
+    _split(dev, MB.TC_SPLIT_F16)
+    o = oracle()
+    b, m, k, n = 8, 384, 256, 320
+    s = o.stream(7850)
+    x = s.uniform(b * m * k, -1, 1).reshape(b, m, k)
+    y = s.uniform(b * k * n, -1, 1).reshape(b, k, n)
+    x[3, 10, 7] = 2.0 ** 30
+    y[3, 7, :] = 0
+    y[6, 100, 33] = -2.0 ** 33
+    x[6, :, 100] = 0
+    x, y = x.astype(np.float32).reshape(-1), y.astype(np.float32).reshape(-1)
+    tx, ty, tr = dev.tensor((b * m * k,)), dev.tensor((b * k * n,)), dev.tensor((b * m * n,))
+    tx.write(x)
+    ty.write(y)
+    MB.check(dev.L.mag_cuda_matmul_batched_f32(dev.p, tr.data_ptr, tx.data_ptr, ty.data_ptr, b, m, k, n), "bmm")
+    assert dev.L.mag_cuda_synchronize(dev.p) == 0
+    got = _raw(dev, tr.data_ptr, b * m * n)
+    for i in range(b):
+        assert _normwise_ok(got[i * m * n:(i + 1) * m * n], x[i * m * k:(i + 1) * m * k],
+                            y[i * k * n:(i + 1) * k * n], m, k, n), i
+
+
+@pytest.mark.parametrize("rows", [256, 4096])
+def test_fused_layer_with_far_elements_matches_unfused_bitwise(rows):
+    """MATMUL -> ADD(bias) -> GELU with rows of X and a column of W whose other elements lie far
+    below their maximum, and outputs where the two meet.  The floor check of the fused epilogue
+    (rows = 4096) or of the split-K part sum (rows = 256) lists those outputs, and their exact
+    recomputation applies the bias and GELU as the unfused graph's ops do: both graphs give the
+    same bits, and the product alone is within 1e-5 of |X||W|."""
+    dev = device()
+    _split(dev, MB.TC_SPLIT_F16)
+    o = oracle()
+    k, n = 512, 1024
+    X, Ws, Bs, root = _build_mlp(dev, rows, [k, n, 64])
+    s = o.stream(7900 + rows)
+    x = s.uniform(rows * k, -1, 1).reshape(rows, k)
+    w = s.normal(k * n, 0.0, (2.0 / k) ** 0.5).reshape(k, n)
+    x[5, 10] = 2.0 ** 30                # row 5: every other element is far
+    x[rows - 3, :] *= 2.0 ** -25        # and a row spanning two scales
+    x[rows - 3, 0] = 1.0
+    w[20, 33] = 2.0 ** 30               # column 33: every other element is far
+    w[21, 700] = -2.0 ** 26
+    x, w = x.astype(np.float32).reshape(-1), w.astype(np.float32).reshape(-1)
+    X.write(x)
+    Ws[0].write(w)
+    Ws[1].write(s.normal(n * 64, 0.0, (2.0 / n) ** 0.5))
+    Bs[0].write(s.uniform(rows * n, -0.1, 0.1))
+    Bs[1].write(s.uniform(rows * 64, -0.1, 0.1))
+    MB.check(dev.L.mag_cuda_set_matmul_mode(dev.p, 2), "tc")
+    try:
+        dev.graph_exec(root)
+        plain = root.read()
+        dev.graph_exec(root, fused=True)
+        fused = root.read()
+        prod, _, _ = run_op(dev, "MATMUL", [x, w], [(rows, k), (k, n)])
+    finally:
+        dev.L.mag_cuda_set_matmul_mode(dev.p, 0)
+        dev.graph_release(root)
+    assert dev.L.mag_cuda_synchronize(dev.p) == 0
+    assert np.all(np.isfinite(plain))
+    assert bits_equal(fused, plain).all()
+    assert _normwise_ok(prod, x, w, rows, k, n)
 
 
 def test_two_layer_mlp_forward_batch_256():

@@ -30,6 +30,16 @@ def _raw(dev, ptr, n):
     return torch.as_tensor(_A(), device=f"cuda:{dev.L.mag_cuda_device_ordinal(dev.p)}").cpu().numpy()
 
 
+def _scratch_bytes(m, k, n, sms):
+    """Partial-sum bytes of an m x k x n skinny product: K cut into slices so that about four
+    CTAs per SM (256 threads, 4 columns each, 16 rows per CTA) stream Y, 16 <= slice <= 64 k
+    (the sizing rule of skinny_slices, csrc/k_matmul_exact.cu), times m x n floats."""
+    colblocks, rowblocks = -(-n // 1024), -(-m // 16)
+    want = max(1, -(-4 * sms // (colblocks * rowblocks)))
+    kc = min(64, max(16, -(-(-(-k // want)) // 16) * 16))
+    return -(-k // kc) * m * n * 4
+
+
 def _normwise_ok(got, x, y, m, k, n, tol=1e-5):
     x64 = x.reshape(m, k).astype(np.float64)
     y64 = y.reshape(k, n).astype(np.float64)
@@ -39,10 +49,16 @@ def _normwise_ok(got, x, y, m, k, n, tol=1e-5):
 
 @pytest.mark.parametrize("m", [1, 8])
 def test_noalloc_matches_allocating_entry_point_twice(m):
+    """M = 1 and M = 8 at K = N = 4096.  On a 148-SM B200 the M = 8 product needs exactly the
+    whole array (128 slices x 8 x 4096 x 4 B = 16 MiB): it covers the boundary, where a call is
+    still accepted."""
     dev = device()
     L = dev.L
     k = n = 4096
     assert L.mag_cuda_matmul_skinny_noalloc_limit() == 16 << 20
+    import torch
+    sms = torch.cuda.get_device_properties(dev.ordinal).multi_processor_count
+    assert _scratch_bytes(m, k, n, sms) <= 16 << 20
     s = oracle().stream(0x5EED0A00 + m)
     x = s.normal(m * k, 0.0, k ** -0.5) if (m * k) % 2 == 0 else s.uniform(m * k, -1, 1)
     y = s.normal(k * n, 0.0, k ** -0.5)
@@ -66,11 +82,20 @@ def test_noalloc_matches_allocating_entry_point_twice(m):
 
 
 def test_noalloc_rejects_products_above_the_array():
+    """Products whose partial sums exceed the array are refused before anything runs: 16 x 4096 x
+    8192 (64 slices x 16 x 8192 x 4 B = 32 MiB) and, one row past the boundary above,
+    9 x 4096 x 4096 (18 MiB on a 148-SM B200)."""
     dev = device()
     L = dev.L
-    m, k, n = 16, 4096, 8192  # needs 37 slices x 16 x 8192 x 4 B = 19.4 MB > 16 MiB
+    import torch
+    sms = torch.cuda.get_device_properties(dev.ordinal).multi_processor_count
+    m, k, n = 16, 4096, 8192
+    assert _scratch_bytes(m, k, n, sms) > 16 << 20
     tx, ty, tr = dev.tensor((m * k,)), dev.tensor((k * n,)), dev.tensor((m * n,))
     rc = L.mag_cuda_matmul_skinny_f32_noalloc(dev.p, tr.data_ptr, tx.data_ptr, ty.data_ptr, m, k, n)
     assert rc == MB.E_SCRATCH_LIMIT
+    if _scratch_bytes(9, 4096, 4096, sms) > 16 << 20:
+        rc = L.mag_cuda_matmul_skinny_f32_noalloc(dev.p, tr.data_ptr, tx.data_ptr, ty.data_ptr, 9, 4096, 4096)
+        assert rc == MB.E_SCRATCH_LIMIT
     assert L.mag_cuda_matmul_skinny_f32_noalloc(dev.p, tr.data_ptr, tx.data_ptr, ty.data_ptr, 17, k, n) == MB.E_INVALID
     assert L.mag_cuda_synchronize(dev.p) == 0
