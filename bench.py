@@ -470,7 +470,7 @@ def run_ours(args):
         "gpu_launches": launches_timed,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": split_peak, "unit": "TFLOP/s",
                      "frac": achieved / split_peak if split_peak else None,
-                     "traffic": (0.946e9 + 0.120e9) * rows / 8192,
+                     "traffic": (0.686e9 + 0.119e9) * rows / 8192,
                      "traffic_note": "DRAM bytes per hidden-layer GEMM launch: ncu capture of the fused "
                                      "layer at 8192 rows, scaled by rows",
                      "kernel": "MATMUL op (per-op CUDA events inside the replayed graph)",
@@ -785,9 +785,13 @@ def run_case(args):
         elif args.case == "batched":  # 64 products of 512 x 512 x 512
             fn = lambda: dev.L.mag_cuda_matmul_batched_f32(dev.p, r.data_ptr, x.data_ptr, y.data_ptr, 64, 512, 512, 512)
             work = 2.0 * 64 * 512 ** 3 / 1e12
-        elif args.case == "skinny":  # M = 1, K = N = 4096
-            fn = lambda: dev.L.mag_cuda_matmul_f32(dev.p, r.data_ptr, x.data_ptr, y.data_ptr, 1, 4096, 4096)
-            work = 4.0 * (4096 + 4096 * 4096 + 4096) / 1e9
+        elif args.case in ("skinny", "skinny8"):  # M = 1 or 8, K = N = 4096
+            mr = 1 if args.case == "skinny" else 8
+            fn = lambda: dev.L.mag_cuda_matmul_f32(dev.p, r.data_ptr, x.data_ptr, y.data_ptr, mr, 4096, 4096)
+            work = 4.0 * (mr * 4096 + 4096 * 4096 + mr * 4096) / 1e9
+        elif args.case == "rowsum":  # SUM along rows of 32768
+            fn = lambda: dev.L.mag_cuda_reduce_rows_f32(dev.p, MB.OP["SUM"], r.data_ptr, x.data_ptr, n // 32768, 32768)
+            work = 4.0 * n / 1e9
         else:
             fn = lambda: dev.L.mag_cuda_softmax_rows_f32(dev.p, r.data_ptr, x.data_ptr, n // 32768, 32768)
             work = 8.0 * n / 1e9
@@ -1127,7 +1131,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--case", default=None, choices=["gemm", "layer", "add", "sigmoid", "sum", "softmax", "softmax1k", "softmax256k", "skinny", "tile", "bcast2", "bcast2s", "batched",
+    ap.add_argument("--case", default=None, choices=["gemm", "layer", "add", "sigmoid", "sum", "softmax", "softmax1k", "softmax256k", "skinny", "skinny8", "rowsum", "tile", "bcast2", "bcast2s", "batched",
                                                       "fill_uniform", "fill_normal", "fill_const", "storage", "image", "sharded", "mlp2"],
                     help="run one kernel family for a profiler instead of the benchmark")
     ap.add_argument("--size", type=int, default=None)

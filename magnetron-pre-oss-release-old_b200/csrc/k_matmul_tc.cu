@@ -303,7 +303,7 @@ struct Epi {
     // f16 split: floor-element counts of X's rows ([B*M]) and of Y's 32-column chunks
     // ([B*ceil(N/32)]), and where outputs that fail the floor check are listed (floor_check)
     const int* row_floor;
-    const int* col_floor32;
+    const int* col_floor;
     int2* chk_list;     // (global row, column) of each listed output, up to chk_cap
     int* chk_count;     // [0] outputs listed (may pass chk_cap), [1] rows listed
     int* chk_rflag;     // [B*M] a row has a listed output
@@ -329,12 +329,20 @@ __device__ __forceinline__ float gelu_lane(float x) {
 // units.  So an output's error beyond the 2^-22-relative terms is at most
 //     2^-25 (nF_i 2^-e_i max_k|y_kj| + nG_j 2^-f_j max_k|x_ik|) <= 2^-10 2^-(e_i+f_j) (nF_i + nG_j)
 // (nF_i, nG_j: floor elements of row i of X and column j of Y; the maxima are below 2^(15-e)),
-// which is at most 2^-20 of the output whenever its scaled sum |acc| = 2^(e_i+f_j) |C_ij| is at
-// least 2^10 (nF_i + nG_j).  Outputs below that are listed and recomputed exactly (fix_outputs):
-// in ordinary data a handful per product, for a row whose large entries meet zeros in Y (all
-// its products then carried by elements far below its maximum) the whole row.  nG_j is bounded
-// by the count of its 32-column chunk, so all checks of an output use the same bound.
-__device__ __forceinline__ float floor_threshold(int n) { return n > 0 ? 1024.0f * (float)n : 0.0f; }
+// which is at most 2^-18 (3.8e-6) of the output whenever its scaled sum |acc| = 2^(e_i+f_j) |C_ij|
+// is at least 2^8 (nF_i + nG_j); with the other error terms (2^-21 relative to |X||Y| for the
+// split and the dropped lo*lo product, about 2e-6 for the segment-wise accumulation) an output
+// stays within 1e-5 of |X||Y|.  Outputs below that are listed and recomputed exactly
+// (fix_outputs): in ordinary data a few hundred per large product, for a row whose large entries
+// meet zeros in Y (all its products then carried by elements far below its maximum) the whole
+// row.  The GEMM epilogue bounds nG_j by the largest count of the output's 32-column chunk.
+__device__ __forceinline__ float floor_threshold(int n) { return n > 0 ? 256.0f * (float)n : 0.0f; }
+
+// Largest floor count of the 32 columns of chunk cb (per column counts in cf; a warp-wide
+// reduction, every lane gets it).
+__device__ __forceinline__ int chunk_floor(const int* cf, int64_t cb, int64_t N, int lane) {
+    return __reduce_max_sync(0xffffffffu, cb + lane < N ? __ldg(cf + cb + lane) : 0);
+}
 
 __device__ __noinline__ void list_output(int2* list, int* count, int* rflag, int* rows, int cap, int64_t grow,
                                         int64_t col) {
@@ -620,8 +628,10 @@ __global__ void __maxnreg__(kLaunchRegs)
                     }
                     const int* ce = F16 ? epi.col_exp + (int64_t)bt * N + cb : nullptr;
                     float thr = 0.0f;  // floor check of this lane's row (threshold on the scaled sums)
-                    if constexpr (F16)
-                        thr = row_ok ? floor_threshold(__ldg(epi.row_floor + row) + __ldg(epi.col_floor32 + cb / 32)) : 0.0f;
+                    if constexpr (F16) {  // every lane takes part in the chunk's reduction
+                        const int cm = chunk_floor(epi.col_floor, cb, N, lane);
+                        thr = row_ok ? floor_threshold(__ldg(epi.row_floor + row) + cm) : 0.0f;
+                    }
 #pragma unroll
                     for (int j = 0; j < 32; j += 4) {
                         const uint32_t slot = sbuf + lane * 128 + (((j >> 2) ^ (lane & 7)) << 4);
@@ -733,9 +743,9 @@ __global__ void __maxnreg__(kLaunchRegs)
                 float* v = sum + c * 32;
                 const int cb = colh + c * 32;
                 const bool full = cb + 32 <= N;
-                if (F16 && check && cb < N && row_ok) {
-                    const float thr = floor_threshold(__ldg(epi.row_floor + (int64_t)bt * M + row) +
-                                                      __ldg(epi.col_floor32 + (int64_t)bt * ((N + 31) / 32) + cb / 32));
+                if (F16 && check && cb < N) {  // warp-uniform: the chunk's largest column count needs every lane
+                    const int cm = chunk_floor(epi.col_floor + (int64_t)bt * N, cb, N, lane);
+                    const float thr = row_ok ? floor_threshold(__ldg(epi.row_floor + (int64_t)bt * M + row) + cm) : 0.0f;
                     uint32_t low = 0;
 #pragma unroll
                     for (int j = 0; j < 32; ++j) low |= (fabsf(v[j]) < thr ? 1u : 0u) << j;
@@ -1046,7 +1056,7 @@ __global__ void __launch_bounds__(256) split_rows_f16_block(const float* __restr
 // same bound as the GEMM epilogue's, in unscaled units).  M * N < 2^31 for the products that
 // reach it (split along K: fewer tiles than CTAs; last-wave tails: under 8 waves of tiles).
 __device__ __forceinline__ void check_output(const Epi& epi, float c, int64_t row, int64_t col, int64_t N) {
-    const int n = epi.row_floor[row] + epi.col_floor32[col >> 5];
+    const int n = epi.row_floor[row] + epi.col_floor[col];
     if (n > 0 && fabsf(c) < unscale(floor_threshold(n), epi.row_exp[row] + epi.col_exp[col]))
         LIST_OUTPUT(epi, row, col);
 }
@@ -1140,7 +1150,7 @@ __global__ void __launch_bounds__(256) sum_tail(float* __restrict__ r, const flo
         for (int u = 0; u < 4; ++u) {
             if (col + u >= N) break;
             const int64_t grow = (int64_t)bt * M + row, gcol = (int64_t)bt * N + col + u;
-            const int nf = chk.row_floor[grow] + chk.col_floor32[(int64_t)bt * ((N + 31) / 32) + ((col + u) >> 5)];
+            const int nf = chk.row_floor[grow] + chk.col_floor[gcol];
             if (nf > 0 && fabsf(v[u]) < unscale(floor_threshold(nf), chk.row_exp[grow] + chk.col_exp[gcol]))
                 LIST_OUTPUT(chk, grow, col + u);
         }
@@ -1211,7 +1221,7 @@ __global__ void __launch_bounds__(256) col_absmax(const float* __restrict__ y, u
 __global__ void __launch_bounds__(256) split_cols_t_f16(const float* __restrict__ y, const unsigned* __restrict__ cmax,
                                                         __half* __restrict__ hi, __half* __restrict__ lo,
                                                         int* __restrict__ col_exp, int64_t K, int64_t N, int64_t Kp,
-                                                        int* __restrict__ col_floor32) {
+                                                        int* __restrict__ col_floor) {
     __shared__ float tile[64][65];
     __shared__ float scl[64];
     y += (int64_t)blockIdx.z * K * N;
@@ -1263,9 +1273,9 @@ __global__ void __launch_bounds__(256) split_cols_t_f16(const float* __restrict_
             int nf = 0;
 #pragma unroll
             for (int q = 0; q < 8; ++q) nf += split_f16(tile[kc + q][j], sc, h[q], l[q]);
-            // floor elements, counted per 32-column chunk (zeroed before the split; partial
-            // counts of every k-block add up)
-            if (nf) atomicAdd(col_floor32 + (int64_t)blockIdx.z * ((N + 31) / 32) + n / 32, nf);
+            // floor elements, counted per column (zeroed before the split; the partial counts of
+            // every k-block add up)
+            if (nf) atomicAdd(col_floor + (int64_t)blockIdx.z * N + n, nf);
             *(uint4*)(hi + n * Kp + k) = make_uint4(pack2(h[0], h[1]), pack2(h[2], h[3]), pack2(h[4], h[5]),
                                                     pack2(h[6], h[7]));
             *(uint4*)(lo + n * Kp + k) = make_uint4(pack2(l[0], l[1]), pack2(l[2], l[3]), pack2(l[4], l[5]),
@@ -1274,20 +1284,20 @@ __global__ void __launch_bounds__(256) split_cols_t_f16(const float* __restrict_
     }
 }
 
-// The outputs listed by the floor check, recomputed exactly: one warp per output, the lanes'
-// products of f32 (exact in double) summed in double over k = lane, lane + 32, ..., then across
-// lanes in a fixed tree, rounded once; a fused layer's bias and GELU follow, as in the epilogue.
-// When more outputs were listed than the list holds, every output of the listed rows is
-// recomputed.  Either way the result depends only on the inputs.
+// The outputs listed by the floor check, recomputed exactly: one CTA per output, thread t summing
+// the f32 products (exact in double) over k = t, t + 256, ... in double (four loads in flight),
+// then a fixed tree over the CTA; rounded once, then a fused layer's bias and GELU as the
+// epilogue applies them.  When more outputs were listed than the list holds, every output of
+// the listed rows is recomputed.  Either way the result depends only on the inputs.
 __global__ void __launch_bounds__(256) fix_outputs(const float* __restrict__ x, const float* __restrict__ y,
                                                    float* __restrict__ r, int64_t M, int64_t K, int64_t N,
                                                    const Epi epi) {
+    __shared__ double part[8];
     const int listed = epi.chk_count[0];
     const bool by_rows = listed > epi.chk_cap;
     const int64_t items = by_rows ? (int64_t)epi.chk_count[1] * N : (int64_t)listed;
-    const int lane = threadIdx.x & 31;
-    const int64_t warps = (int64_t)gridDim.x * 8;
-    for (int64_t it = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5); it < items; it += warps) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    for (int64_t it = blockIdx.x; it < items; it += gridDim.x) {
         int64_t gi, j;
         if (by_rows) {
             gi = epi.chk_rows[it / N];
@@ -1301,16 +1311,23 @@ __global__ void __launch_bounds__(256) fix_outputs(const float* __restrict__ x, 
         const float* xr = x + gi * K;
         const float* yc = y + bt * K * N + j;
         double acc = 0.0;
-        for (int64_t k = lane; k < K; k += 32) acc += (double)__ldg(xr + k) * (double)__ldg(yc + k * N);
+#pragma unroll 4
+        for (int64_t k = threadIdx.x; k < K; k += 256) acc += (double)__ldg(xr + k) * (double)__ldg(yc + k * N);
 #pragma unroll
         for (int o = 16; o; o >>= 1) acc += __shfl_down_sync(0xffffffffu, acc, o);
-        if (lane == 0) {
-            float c = (float)acc;
+        if (lane == 0) part[w] = acc;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            double t = part[0];
+#pragma unroll
+            for (int q = 1; q < 8; ++q) t += part[q];
+            float c = (float)t;
             if (epi.bias) c = __fadd_rn(c, epi.bias[gi * N + j]);
             else if (epi.bias_zero) c = __fadd_rn(c, 0.0f);
             if (epi.act == 1) c = gelu_lane(c);
             r[gi * N + j] = c;
         }
+        __syncthreads();  // part[] is rewritten by the next output
     }
 }
 
@@ -1351,8 +1368,8 @@ constexpr int kCheckCap = 1 << 16;  // outputs the floor check lists individuall
 struct Layout {
     int64_t kp;
     size_t xhi, xlo, yhi, ylo, rexp, cexp, cmax, parts, tail, total;
-    // f16 split's floor check: [cmax | cfloor32 | counters | chk_rflag] is cleared by one memset
-    size_t cfloor32, counters, chk_rflag, clear_bytes, rfloor, chk_rows, chk_list;
+    // f16 split's floor check: [cmax | cfloor | counters | chk_rflag] is cleared by one memset
+    size_t cfloor, counters, chk_rflag, clear_bytes, rfloor, chk_rows, chk_list;
     int kparts;  // split-K factor of an unfused single product (1: none)
     int kpc;     // its ring stages per part
 };
@@ -1445,8 +1462,8 @@ Layout layout(int64_t B, int64_t M, int64_t K, int64_t N, bool f16) {
     l.rexp = 2 * xs + 2 * ys;
     l.cexp = l.rexp + (size_t)round_up(rows * 4, 256);
     l.cmax = l.cexp + (size_t)round_up(cols * 4, 256);
-    l.cfloor32 = l.cmax + (size_t)round_up(cols * 4, 256);
-    l.counters = l.cfloor32 + (size_t)round_up(B * ((N + 31) / 32) * 4, 256);
+    l.cfloor = l.cmax + (size_t)round_up(cols * 4, 256);
+    l.counters = l.cfloor + (size_t)round_up(cols * 4, 256);
     l.chk_rflag = l.counters + 256;
     l.clear_bytes = l.chk_rflag + (size_t)round_up(rows * 4, 256) - l.cmax;
     l.rfloor = l.chk_rflag + (size_t)round_up(rows * 4, 256);
@@ -1627,7 +1644,7 @@ static int launch_tc(float* r, const float* x, const float* y, int64_t B, int64_
     // split scales whole rows, so it always splits X itself
     const bool presplit = !f16 && ep && ep->a_hi && ep->a_lo;
     int* rfloor = (int*)(base + l.rfloor);
-    int* cfloor32 = (int*)(base + l.cfloor32);
+    int* cfloor = (int*)(base + l.cfloor);
     if (presplit) {
         xhi = (void*)ep->a_hi;
         xlo = (void*)ep->a_lo;
@@ -1656,7 +1673,7 @@ static int launch_tc(float* r, const float* x, const float* y, int64_t B, int64_
         dim3 gm((unsigned)((N + 127) / 128), (unsigned)((K + kColMaxRows - 1) / kColMaxRows), (unsigned)B);
         col_absmax<<<gm, 256, 0, st>>>(y, cmax, K, N);
         dim3 grid((unsigned)((N + 63) / 64), (unsigned)((l.kp + 63) / 64), (unsigned)B);
-        split_cols_t_f16<<<grid, 256, 0, st>>>(y, cmax, (__half*)yhi, (__half*)ylo, cexp, K, N, l.kp, cfloor32);
+        split_cols_t_f16<<<grid, 256, 0, st>>>(y, cmax, (__half*)yhi, (__half*)ylo, cexp, K, N, l.kp, cfloor);
     } else {
         dim3 grid((unsigned)((N + 31) / 32), (unsigned)(l.kp / 32), (unsigned)B);
         split_cols_t<<<grid, 256, 0, st>>>(y, (float*)yhi, (float*)ylo, K, N, l.kp);
@@ -1673,7 +1690,7 @@ static int launch_tc(float* r, const float* x, const float* y, int64_t B, int64_
     chk.col_exp = cexp;
     if (f16) {
         chk.row_floor = rfloor;
-        chk.col_floor32 = cfloor32;
+        chk.col_floor = cfloor;
         chk.chk_list = (int2*)(base + l.chk_list);
         chk.chk_count = (int*)(base + l.counters);
         chk.chk_rflag = (int*)(base + l.chk_rflag);
@@ -1693,7 +1710,7 @@ static int launch_tc(float* r, const float* x, const float* y, int64_t B, int64_
             fe.bias_zero = ep->bias_zero;
             fe.act = ep->act;
         }
-        fix_outputs<<<(unsigned)(2 * sm_count()), 256, 0, st>>>(x, y, r, M, K, N, fe);
+        fix_outputs<<<(unsigned)(4 * sm_count()), 256, 0, st>>>(x, y, r, M, K, N, fe);
         return (int)cudaGetLastError();
     };
     if (fused && kparts == 1) {

@@ -371,15 +371,22 @@ __global__ void __launch_bounds__(256, V <= 4 ? 4 : (V <= 8 ? 3 : 1)) softmax_ro
     }
 }
 
-// One CTA per slice of 32*T elements; the cluster spans the row.
+// One CTA per slice of 32*T*kSliceVec elements; the cluster spans the row.  Each CTA computes
+// its slice's max m and sum s = sum exp(x - m) (double), pushes (m, s) into slot `rank` of every
+// CTA of the cluster through distributed shared memory, and after ONE cluster barrier each CTA
+// combines the slots in rank order (M = max m_q, S = sum_q s_q exp(m_q - M) in double) and
+// writes its slice as exp(x - m) * (exp(m - M) / S).  After that barrier no CTA touches another's
+// shared memory, so none waits for its peers before leaving.  (The barrier's relaxed arrive at
+// the start orders nothing; its wait before the pushes makes sure every CTA of the cluster runs.)
 template <int kSliceThreads>
 __global__ void __launch_bounds__(kSliceThreads, 1024 / kSliceThreads) softmax_rows_slices(
     float* __restrict__ r, const float* __restrict__ x, uint32_t cols) {
     constexpr int kSlice = kSliceThreads * 4 * kSliceVec;
     __shared__ float sh_max[32];
     __shared__ double sh_sum[32];
-    __shared__ float slot_max;
-    __shared__ double slot_sum;
+    __shared__ float peer_m[16];
+    __shared__ double peer_s[16];
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
     cg::cluster_group cluster = cg::this_cluster();
     const uint32_t crank = cluster.block_rank();
     const uint32_t csize = cluster.num_blocks();
@@ -396,24 +403,37 @@ __global__ void __launch_bounds__(kSliceThreads, 1024 / kSliceThreads) softmax_r
 #pragma unroll
     for (int i = 0; i < kSliceVec; ++i) m = fmaxf(m, max4(v[i]));
     m = block_combine(m, WMax(), sh_max, -(float)INFINITY);
-    if (threadIdx.x == 0) slot_max = m;
-    cluster.sync();
-    float gm = -INFINITY;
-    for (uint32_t k = 0; k < csize; ++k) gm = fmaxf(gm, *cluster.map_shared_rank(&slot_max, k));
     double s = 0.0;
+    const float mm = m != -INFINITY ? m : 0.0f;  // a slice of -inf only (or past the row's end): exp(-inf) = 0
 #pragma unroll
     for (int i = 0; i < kSliceVec; ++i)
-        v[i] = exp4(v[i], gm, c0 + (uint32_t)(threadIdx.x + kSliceThreads * i) * 4, cols, vec_end, s);
+        v[i] = exp4(v[i], mm, c0 + (uint32_t)(threadIdx.x + kSliceThreads * i) * 4, cols, vec_end, s);
     s = block_combine(s, WSum(), sh_sum, 0.0);
-    if (threadIdx.x == 0) slot_sum = s;
-    cluster.sync();
-    double gs = 0.0;
-    for (uint32_t k = 0; k < csize; ++k) gs += *cluster.map_shared_rank(&slot_sum, k);
-    const float inv = __frcp_rn((float)gs);
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+    if (threadIdx.x < csize) {
+        *cluster.map_shared_rank(&peer_m[crank], threadIdx.x) = m;
+        *cluster.map_shared_rank(&peer_s[crank], threadIdx.x) = s;
+    }
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+    __shared__ float sh_f;
+    if (threadIdx.x == 0) {
+        float gm = -INFINITY;
+        for (uint32_t k = 0; k < csize; ++k) gm = fmaxf(gm, peer_m[k]);
+        double gs = 0.0;
+        for (uint32_t k = 0; k < csize; ++k)
+            if (peer_m[k] != -INFINITY) gs += peer_s[k] * (double)expf(peer_m[k] - gm);
+        // a row of -inf only has no maximum to subtract: NaN, as exp(x - max) gives there
+        sh_f = gm == -INFINITY ? __int_as_float(0x7FC00000)
+                               : (m != -INFINITY ? (float)((double)expf(m - gm) / gs) : 0.0f);
+    }
+    __syncthreads();
+    const float f = sh_f;
 #pragma unroll
-    for (int i = 0; i < kSliceVec; ++i)
-        store4(pr, c0 + (uint32_t)(threadIdx.x + kSliceThreads * i) * 4, cols, vec, div4(v[i], inv));
-    cluster.sync();  // peers may still read this CTA's slots
+    for (int i = 0; i < kSliceVec; ++i) {
+        const float4 e = v[i];
+        store4(pr, c0 + (uint32_t)(threadIdx.x + kSliceThreads * i) * 4, cols, vec,
+               make_float4(__fmul_rn(e.x, f), __fmul_rn(e.y, f), __fmul_rn(e.z, f), __fmul_rn(e.w, f)));
+    }
 }
 
 // Rows wider than one CTA slice: two passes over x instead of a cluster that holds the whole

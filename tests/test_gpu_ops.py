@@ -171,6 +171,20 @@ def test_matmul_skinny(m):
     assert _normwise_ok(got, x, y, m, k, n)
 
 
+@pytest.mark.parametrize("m,k,n", [(1, 1000, 4100), (3, 4096, 3000), (8, 333, 8192), (17, 2048, 4096),
+                                   (31, 4099, 2561), (16, 65536, 4096)])
+def test_matmul_skinny_ragged_shapes(m, k, n):
+    """Skinny products (split-K on CUDA cores, slices added in a fixed order) with ragged K and N,
+    two row blocks (m > 16) and a long K: within 1e-5 of |X||Y|."""
+    dev = device()
+    o = oracle()
+    s = o.stream(7050 + m + k)
+    x = s.uniform(m * k, -1, 1)
+    y = s.normal(k * n, 0.0, k ** -0.5)
+    got, _, _ = run_op(dev, "MATMUL", [x, y], [(m, k), (k, n)])
+    assert _normwise_ok(got, x, y, m, k, n)
+
+
 def test_matmul_batched_extension():
     dev = device()
     o = oracle()
@@ -230,8 +244,9 @@ def test_softmax_rows():
         got = _raw(dev, tr.data_ptr, rows * cols)
         want = o.softmax_rows(x, rows, cols)
         rel = np.abs(got - want) / np.maximum(np.abs(want), 1e-30)
-        # parity bar 1e-5; CUDA's expf against the reference's exp lanes measures <= 3.7e-7
-        assert rel.max() <= 1e-6, (rows, cols, rel.max())
+        # parity bar 1e-5; CUDA's expf against the reference's exp lanes, and the cluster kernel's
+        # slice rescaling exp(m_slice - m_row) (one more expf and rounding), measure <= 1.2e-6
+        assert rel.max() <= 2e-6, (rows, cols, rel.max())
 
 
 def test_broadcast2_small_exact():
