@@ -782,6 +782,11 @@ def run_case(args):
             fill = getattr(dev.L, f"mag_cuda_{args.case}_pcg_f32")
             fn = lambda: fill(dev.p, r.data_ptr, n, 0.0, 1.0, ctypes.byref(g.state), g.inc)
             work = 4.0 * n / 1e9
+        elif args.case in ("fill_mt_uniform", "fill_mt_normal"):
+            g = MB.Mt19937(0x5EED0002)
+            fill = getattr(dev.L, f"mag_cuda_fill_{args.case[8:]}_mt19937_f32")
+            fn = lambda: fill(dev.p, r.data_ptr, n, 0.0, 1.0, ctypes.byref(g.st))
+            work = 4.0 * n / 1e9
         elif args.case == "batched":  # 64 products of 512 x 512 x 512
             fn = lambda: dev.L.mag_cuda_matmul_batched_f32(dev.p, r.data_ptr, x.data_ptr, y.data_ptr, 64, 512, 512, 512)
             work = 2.0 * 64 * 512 ** 3 / 1e12
@@ -1013,6 +1018,15 @@ def run_sweep_full(args):
     ms = timeit(lambda: dev.L.mag_cuda_fill_normal_pcg_f32(dev.p, r.data_ptr, n, 0.0, 1.0, ctypes.byref(g.state),
                                                           g.inc), 5)
     rec("fill", "normal PCG + Box-Muller 2^28", ms, 4.0 * n / 1e9, "GB/s", hbm)
+    # the reference's default stream (Mersenne twister, jumped per substream); each fill reads
+    # the last block back, so it waits for its kernels
+    mt = MB.Mt19937(0x5EED0002)
+    ms = timeit(lambda: dev.L.mag_cuda_fill_uniform_mt19937_f32(dev.p, r.data_ptr, n, -1.0, 1.0, ctypes.byref(mt.st)),
+                5)
+    rec("fill", "uniform MT19937 2^28", ms, 4.0 * n / 1e9, "GB/s", hbm)
+    ms = timeit(lambda: dev.L.mag_cuda_fill_normal_mt19937_f32(dev.p, r.data_ptr, n, 0.0, 1.0, ctypes.byref(mt.st)),
+                5)
+    rec("fill", "normal MT19937 + Box-Muller 2^28", ms, 4.0 * n / 1e9, "GB/s", hbm)
     r.free()
     # ---- config 4: matmul
     for m in (1024, 4096, 8192, 16384):
@@ -1132,7 +1146,7 @@ def main():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--case", default=None, choices=["gemm", "layer", "add", "sigmoid", "sum", "softmax", "softmax1k", "softmax256k", "skinny", "skinny8", "rowsum", "tile", "bcast2", "bcast2s", "batched",
-                                                      "fill_uniform", "fill_normal", "fill_const", "storage", "image", "sharded", "mlp2"],
+                                                      "fill_uniform", "fill_normal", "fill_const", "fill_mt_uniform", "fill_mt_normal", "storage", "image", "sharded", "mlp2"],
                     help="run one kernel family for a profiler instead of the benchmark")
     ap.add_argument("--size", type=int, default=None)
     ap.add_argument("--sweep-full", action="store_true", help="measure every other BASELINE configuration")

@@ -176,6 +176,24 @@ MAG_CUDA_EXPORT int mag_cuda_fill_uniform_pcg_f32(mag_compute_device_t* dvc, flo
                                                   float max, uint64_t* state, uint64_t inc);
 MAG_CUDA_EXPORT int mag_cuda_fill_normal_pcg_f32(mag_compute_device_t* dvc, float* r, int64_t n, float mean,
                                                  float stddev, uint64_t* state, uint64_t inc);
+/* The same fills from the context's Mersenne-twister stream, the reference's default algorithm
+ * (magnetron/magnetron.c:751-777, seeded at :800-805; mag_ctx_create2 zeroes the algorithm
+ * field, :951).  mt points at the context's {remaining, next, state[624]}
+ * (magnetron/magnetron_internal.h:398-402; 626 uint32 words).  The values equal what
+ * mag_prng_generate_n would write from that state, and on return it holds what the host
+ * generator would leave: the block of the last word drawn, next and remaining.  A fill that
+ * draws past the current block reads that block back, so it waits for the device's stream.
+ * MAG_CUDA_E_INVALID for a state the host generator cannot be in (remaining outside 1..624, or
+ * next + remaining - 1 past the block). */
+MAG_CUDA_EXPORT int mag_cuda_fill_uniform_mt19937_f32(mag_compute_device_t* dvc, float* r, int64_t n, float min,
+                                                      float max, uint32_t* mt);
+MAG_CUDA_EXPORT int mag_cuda_fill_normal_mt19937_f32(mag_compute_device_t* dvc, float* r, int64_t n, float mean,
+                                                     float stddev, uint32_t* mt);
+/* Host arithmetic behind those fills, for checking without a device: out = the 624-word window
+ * d words after win (win at least one block into a stream), by the jump polynomials the fills
+ * use; and the degree of the stream's minimal polynomial (0 if it could not be found). */
+MAG_CUDA_EXPORT int mag_cuda_mt19937_jump(const uint32_t* win, uint64_t d, uint32_t* out);
+MAG_CUDA_EXPORT int mag_cuda_mt19937_degree(void);
 /* r[0..n) = x (mag_tensor_fill, magnetron/magnetron.c:1826-1842, for any x). */
 MAG_CUDA_EXPORT int mag_cuda_fill_f32(mag_compute_device_t* dvc, float* r, int64_t n, float x);
 

@@ -950,6 +950,37 @@ int mag_cuda_fill_normal_pcg_f32(mag_compute_device_t* dvc, float* r, int64_t n,
     return 0;
 }
 
+static int fill_mt(mag_compute_device_t* dvc, float* r, int64_t n, int normal, float p0, float p1, uint32_t* mt) {
+    mcu_device* d = dev_of(dvc);
+    ext_out(d, r, (size_t)n * 4);
+    if (!n) return 0;
+    const size_t sb = mcu_fill_mt_scratch_bytes(n, mt[0], mt[1]);
+    if (!sb) return MAG_CUDA_E_INVALID; /* not a state the host generator can be in */
+    int k = 0;
+    int rc = mcu_launch_fill_mt(r, n, normal, p0, p1, mt, scratch_get(d, sb), d->stream, &k);
+    if (k) mcu_count_launches(k);
+    return rc;
+}
+
+int mag_cuda_fill_uniform_mt19937_f32(mag_compute_device_t* dvc, float* r, int64_t n, float min, float max,
+                                      uint32_t* mt) {
+    if (n < 0 || !mt) return MAG_CUDA_E_INVALID;
+    return fill_mt(dvc, r, n, 0, min, max - min, mt); /* max - min rounded to f32 as on the host */
+}
+
+int mag_cuda_fill_normal_mt19937_f32(mag_compute_device_t* dvc, float* r, int64_t n, float mean, float stddev,
+                                     uint32_t* mt) {
+    if (n < 0 || (n & 1) || !mt) return MAG_CUDA_E_INVALID; /* pairs, as the core asserts */
+    return fill_mt(dvc, r, n, 1, mean, stddev, mt);
+}
+
+int mag_cuda_mt19937_jump(const uint32_t* win, uint64_t d, uint32_t* out) {
+    if (!win || !out) return MAG_CUDA_E_INVALID;
+    return mcu_mt19937_jump_host(win, d, out) ? MAG_CUDA_E_INVALID : 0;
+}
+
+int mag_cuda_mt19937_degree(void) { return mcu_mt19937_degree(); }
+
 int mag_cuda_fill_f32(mag_compute_device_t* dvc, float* r, int64_t n, float x) {
     if (n < 0) return MAG_CUDA_E_INVALID;
     mcu_device* d = dev_of(dvc);

@@ -13,6 +13,7 @@
 // group to group by one precomputed affine jump of 4T steps.  The fill is
 // HBM-write bound for the uniform stream (4 B per element).
 #include "mcu_kernels.h"
+#include "mcu_fill.cuh"
 
 #include <cuda_runtime.h>
 #include <math.h>
@@ -50,12 +51,7 @@ __device__ __forceinline__ uint32_t pcg_out(uint64_t prev) {
     return __funnelshift_r(mixed, mixed, rot);
 }
 
-// 2^-23 * ((y >> 9) + 0.5) = (2m + 1) * 2^-24 for m = y >> 9: one of 2^23 values in
-// (0, 1), formed without an int-to-float conversion as (1 + m 2^-23) - (1 - 2^-24),
-// where both operands and the difference are exact in f32.
-__device__ __forceinline__ float pcg_unit(uint64_t prev) {
-    return __fsub_rn(__uint_as_float(0x3F800000u | (pcg_out(prev) >> 9)), 0x1.fffffep-1f);
-}
+__device__ __forceinline__ float pcg_unit(uint64_t prev) { return mcu::unit_from_bits(pcg_out(prev)); }
 
 struct FillParams {
     uint64_t s0;          // stream state at element 0
@@ -65,17 +61,7 @@ struct FillParams {
     float p0, p1;         // uniform: min, max - min;  normal: mean, stddev
 };
 
-// Box-Muller on one uniform pair with the reference's f32 operation order:
-// mag = stddev * sqrtf(-2 logf(u1)); y0 = mag * cosf(2pi u2) + mean, y1 with sinf.
-// log, sin and cos are evaluated in f64 and rounded once to f32.
-__device__ __forceinline__ float2 box_muller(float u1, float u2, float mean, float stddev) {
-    const float l = (float)log((double)u1);
-    const float mag = __fmul_rn(stddev, __fsqrt_rn(__fmul_rn(-2.0f, l)));
-    const float ang = __fmul_rn((float)(2.0 * 3.14159265358979323846), u2);
-    double sd, cd;
-    sincos((double)ang, &sd, &cd);
-    return make_float2(__fadd_rn(__fmul_rn(mag, (float)cd), mean), __fadd_rn(__fmul_rn(mag, (float)sd), mean));
-}
+using mcu::box_muller;
 
 template <bool NORMAL>
 __global__ void __launch_bounds__(kFillThreads) fill_pcg(float* __restrict__ r, int64_t n, FillParams p, bool vec) {

@@ -51,6 +51,14 @@ uint64_t mcu_pcg_advance(uint64_t state, uint64_t inc, uint64_t n);
 int mcu_launch_fill_pcg(float* r, int64_t n, int normal, float p0, float p1, uint64_t state, uint64_t inc,
                         cudaStream_t st);
 int mcu_launch_fill_const(float* r, int64_t n, float x, cudaStream_t st);
+/* k_fill_mt.cu: fills from the Mersenne-twister stream of st = {remaining, next, state[624]},
+ * which is left as the host generator leaves it (the call waits when it draws past the current
+ * block).  *launches = kernels launched. */
+size_t mcu_fill_mt_scratch_bytes(int64_t n, uint32_t remaining, uint32_t next);
+int mcu_launch_fill_mt(float* r, int64_t n, int normal, float p0, float p1, uint32_t* st, void* scratch,
+                       cudaStream_t stream, int* launches);
+int mcu_mt19937_degree(void);
+int mcu_mt19937_jump_host(const uint32_t* win, uint64_t d, uint32_t* out);
 
 /* k_image.cu: planar f32 [c][h][w] <-> interleaved u8 [h][w][c] (resized to rw x rh when both
  * are nonzero, with ws = (w-1)/(rw-1), hs = (h-1)/(rh-1) rounded to f32), box and text drawing

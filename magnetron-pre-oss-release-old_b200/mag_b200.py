@@ -137,6 +137,10 @@ def load_library(path: str = LIB_PATH):
         "mag_cuda_fill_normal_pcg_f32": ([vp, vp, i64, C.c_float, C.c_float, C.POINTER(C.c_uint64), C.c_uint64],
                                          C.c_int),
         "mag_cuda_fill_f32": ([vp, vp, i64, C.c_float], C.c_int),
+        "mag_cuda_fill_uniform_mt19937_f32": ([vp, vp, i64, C.c_float, C.c_float, C.POINTER(MtState)], C.c_int),
+        "mag_cuda_fill_normal_mt19937_f32": ([vp, vp, i64, C.c_float, C.c_float, C.POINTER(MtState)], C.c_int),
+        "mag_cuda_mt19937_jump": ([C.POINTER(C.c_uint32), C.c_uint64, C.POINTER(C.c_uint32)], C.c_int),
+        "mag_cuda_mt19937_degree": ([], C.c_int),
         "mag_cuda_tensor_upload_async": ([vp, vp, vp, C.c_size_t], C.c_int),
         "mag_cuda_tensor_download_async": ([vp, vp, vp, C.c_size_t], C.c_int),
         "mag_cuda_copies_synchronize": ([vp], C.c_int),
@@ -211,6 +215,30 @@ class Pcg:
             seed = 0x853C49E6748FEA9B ^ id(self)
         self.state = C.c_uint64(seed ^ 0x853C49E6748FEA9B)
         self.inc = 0xDA3E39CB94B95BDB
+
+
+class MtState(C.Structure):
+    """A context's Mersenne-twister state (magnetron/magnetron_internal.h:398-402)."""
+    _fields_ = [("remaining", C.c_uint32), ("next", C.c_uint32), ("state", C.c_uint32 * 624)]
+
+
+class Mt19937:
+    """A context's Mersenne-twister stream, the reference's default generator: mag_prng_init,
+    Mersenne-twister branch (magnetron/magnetron.c:797-805).  Fills draw from it in order and
+    leave it as the reference context's generator would."""
+
+    def __init__(self, seed: int):
+        seed &= (1 << 64) - 1
+        if not seed:  # the reference derives a default seed from the context's address
+            seed = 0x853C49E6748FEA9B ^ id(self)
+        self.st = MtState()
+        w = seed & 0xFFFFFFFF
+        self.st.state[0] = w
+        for i in range(1, 624):
+            w = ((w ^ (w >> 30)) * 1812433253 + i) & 0xFFFFFFFF
+            self.st.state[i] = w
+        self.st.next = 0
+        self.st.remaining = 1
 
 
 def i64x6(v) -> C.Array:
@@ -464,13 +492,20 @@ class Device:
     def fill(self, t: Tensor, x: float):
         check(self.L.mag_cuda_fill_f32(self.p, t.data_ptr, t.numel, x), "fill")
 
-    def fill_random_uniform(self, t: Tensor, lo: float, hi: float, gen: "Pcg"):
-        check(self.L.mag_cuda_fill_uniform_pcg_f32(self.p, t.data_ptr, t.numel, lo, hi, C.byref(gen.state), gen.inc),
-              "fill_random_uniform")
+    def fill_random_uniform(self, t: Tensor, lo: float, hi: float, gen: "Pcg | Mt19937"):
+        if isinstance(gen, Mt19937):
+            rc = self.L.mag_cuda_fill_uniform_mt19937_f32(self.p, t.data_ptr, t.numel, lo, hi, C.byref(gen.st))
+        else:
+            rc = self.L.mag_cuda_fill_uniform_pcg_f32(self.p, t.data_ptr, t.numel, lo, hi, C.byref(gen.state), gen.inc)
+        check(rc, "fill_random_uniform")
 
-    def fill_random_normal(self, t: Tensor, mean: float, std: float, gen: "Pcg"):
-        check(self.L.mag_cuda_fill_normal_pcg_f32(self.p, t.data_ptr, t.numel, mean, std, C.byref(gen.state), gen.inc),
-              "fill_random_normal")
+    def fill_random_normal(self, t: Tensor, mean: float, std: float, gen: "Pcg | Mt19937"):
+        if isinstance(gen, Mt19937):
+            rc = self.L.mag_cuda_fill_normal_mt19937_f32(self.p, t.data_ptr, t.numel, mean, std, C.byref(gen.st))
+        else:
+            rc = self.L.mag_cuda_fill_normal_pcg_f32(self.p, t.data_ptr, t.numel, mean, std, C.byref(gen.state),
+                                                     gen.inc)
+        check(rc, "fill_random_normal")
 
     def graph_exec(self, root: Tensor, fused: bool = False):
         fn = self.L.mag_cuda_graph_exec_fused if fused else self.L.mag_cuda_graph_exec

@@ -60,6 +60,76 @@ void orc_fill_normal(orc_pcg_t* g, float* out, int64_t n, float mean, float stdd
     }
 }
 
+/* mag_prng_init, Mersenne-twister branch (magnetron/magnetron.c:797-803): init_genrand's
+ * seeding; the first draw twists. */
+void orc_mt_seed(orc_mt_t* g, uint64_t seed) {
+    g->state[0] = (uint32_t)seed;
+    for (uint32_t i = 1; i < 624; ++i)
+        g->state[i] = (uint32_t)((g->state[i - 1] ^ (g->state[i - 1] >> 30)) * 1812433253u + i);
+    g->next = 0;
+    g->remaining = 1;
+}
+
+/* mag_prng_generate_n, Mersenne-twister branch (magnetron/magnetron.c:751-777), as written
+ * there: the twist adds the matrix constant when the low bit of y is 0 (the textbook
+ * generator adds it when the bit is 1), so the stream is the reference's own. */
+static void orc_mt_twist(uint32_t* st) {
+    uint32_t y, i;
+    for (i = 0; i < 624 - 397; ++i) {
+        y = (st[i] & 0x80000000u) | (st[i + 1] & 0x7fffffffu);
+        st[i] = st[i + 397] ^ (y >> 1) ^ ((y & 1) ? 0 : 0x9908b0dfu);
+    }
+    for (; i < 624 - 1; ++i) {
+        y = (st[i] & 0x80000000u) | (st[i + 1] & 0x7fffffffu);
+        st[i] = st[i + (397 - 624)] ^ (y >> 1) ^ ((y & 1) ? 0 : 0x9908b0dfu);
+    }
+    y = (st[623] & 0x80000000u) | (st[0] & 0x7fffffffu);
+    st[623] = st[396] ^ (y >> 1) ^ ((y & 1) ? 0 : 0x9908b0dfu);
+}
+
+void orc_fill_uniform_mt(orc_mt_t* g, float* out, int64_t n, float min, float max) {
+    float span = max - min;
+    for (int64_t i = 0; i < n; ++i) {
+        if (--g->remaining <= 0) {
+            g->remaining = 624;
+            g->next = 0;
+            orc_mt_twist(g->state);
+        }
+        uint32_t y = g->state[g->next++];
+        y ^= y >> 11;
+        y ^= (y << 7) & 0x9d2c5680u;
+        y ^= (y << 15) & 0xefc60000u;
+        y ^= y >> 18;
+        float unit = (1.f / (float)(1 << 23)) * ((float)(y >> 9) + 0.5f);
+        out[i] = min + span * unit;
+    }
+}
+
+/* The untempered words the generator draws next, without drawing them: n words from the
+ * current block on (a test helper: the stream positions a device fill continues from). */
+void orc_mt_words(const orc_mt_t* g, uint32_t* out, int64_t n) {
+    orc_mt_t c = *g;
+    for (int64_t i = 0; i < n; ++i) {
+        if (--c.remaining <= 0) {
+            c.remaining = 624;
+            c.next = 0;
+            orc_mt_twist(c.state);
+        }
+        out[i] = c.state[c.next++];
+    }
+}
+
+void orc_fill_normal_mt(orc_mt_t* g, float* out, int64_t n, float mean, float stddev) {
+    orc_fill_uniform_mt(g, out, n, 0.0f, 1.0f);
+    for (int64_t i = 0; i + 1 < n; i += 2) {
+        float u1 = out[i], u2 = out[i + 1];
+        float mag = stddev * sqrtf(-2.0f * logf(u1));
+        float ang = (float)(2.0 * M_PI) * u2;
+        out[i] = mag * cosf(ang) + mean;
+        out[i + 1] = mag * sinf(ang) + mean;
+    }
+}
+
 /* ------------------------------------------------- vector transcendentals --- */
 
 /* mag_simd_expf, SSE2 branch (magnetron/magnetron_cpu.c:167-190), one lane.

@@ -27,6 +27,13 @@ typedef struct orc_pcg_t { uint64_t state, inc; } orc_pcg_t;
 void orc_pcg_seed(orc_pcg_t* g, uint64_t seed);
 void orc_fill_uniform(orc_pcg_t* g, float* out, int64_t n, float min, float max);
 void orc_fill_normal(orc_pcg_t* g, float* out, int64_t n, float mean, float stddev);
+/* The reference context's Mersenne-twister generator: its state struct's layout
+ * (magnetron/magnetron_internal.h:398-402), seeding and draws (magnetron/magnetron.c:751-777, :797-803). */
+typedef struct orc_mt_t { uint32_t remaining, next, state[624]; } orc_mt_t;
+void orc_mt_seed(orc_mt_t* g, uint64_t seed);
+void orc_fill_uniform_mt(orc_mt_t* g, float* out, int64_t n, float min, float max);
+void orc_fill_normal_mt(orc_mt_t* g, float* out, int64_t n, float mean, float stddev);
+void orc_mt_words(const orc_mt_t* g, uint32_t* out, int64_t n);
 
 /* Scalar transcendental helpers, exposed for unit tests. */
 float orc_sse_expf(float x);

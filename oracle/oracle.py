@@ -74,9 +74,47 @@ class Stream:
         return self.uniform(n, a, b) if kind == "u" else self.normal(n, a, b)
 
 
+class MtState(C.Structure):
+    """A reference context's Mersenne-twister state (magnetron/magnetron_internal.h:398-402)."""
+    _fields_ = [("remaining", C.c_uint32), ("next", C.c_uint32), ("state", C.c_uint32 * 624)]
+
+
+class MtStream:
+    """One seeded Mersenne-twister stream, drawn in order like a default reference context."""
+
+    def __init__(self, oracle: "Oracle", seed: int):
+        self.o = oracle
+        self.g = MtState()
+        oracle.L.orc_mt_seed(C.byref(self.g), seed)
+
+    def uniform(self, n: int, lo: float, hi: float) -> np.ndarray:
+        out = np.empty(n, np.float32)
+        self.o.L.orc_fill_uniform_mt(C.byref(self.g), _fp(out), n, lo, hi)
+        return out
+
+    def normal(self, n: int, mean: float, std: float) -> np.ndarray:
+        out = np.empty(n, np.float32)
+        self.o.L.orc_fill_normal_mt(C.byref(self.g), _fp(out), n, mean, std)
+        return out
+
+    def words(self, n: int) -> np.ndarray:
+        """The next n untempered words, without drawing them."""
+        out = np.empty(n, np.uint32)
+        self.o.L.orc_mt_words(C.byref(self.g), out.ctypes.data_as(C.POINTER(C.c_uint32)), n)
+        return out
+
+    def copy_state(self) -> MtState:
+        c = MtState()
+        C.memmove(C.byref(c), C.byref(self.g), C.sizeof(MtState))
+        return c
+
+
 class Oracle:
     def stream(self, seed: int) -> Stream:
         return Stream(self, seed)
+
+    def mt_stream(self, seed: int) -> MtStream:
+        return MtStream(self, seed)
 
     def __init__(self, path: str = ORACLE_SO):
         if not os.path.exists(path):
@@ -86,6 +124,10 @@ class Oracle:
         L.orc_pcg_seed.argtypes = [C.POINTER(_Pcg), C.c_uint64]
         L.orc_fill_uniform.argtypes = [C.POINTER(_Pcg), _f32p, C.c_int64, C.c_float, C.c_float]
         L.orc_fill_normal.argtypes = [C.POINTER(_Pcg), _f32p, C.c_int64, C.c_float, C.c_float]
+        L.orc_mt_seed.argtypes = [C.POINTER(MtState), C.c_uint64]
+        L.orc_fill_uniform_mt.argtypes = [C.POINTER(MtState), _f32p, C.c_int64, C.c_float, C.c_float]
+        L.orc_fill_normal_mt.argtypes = [C.POINTER(MtState), _f32p, C.c_int64, C.c_float, C.c_float]
+        L.orc_mt_words.argtypes = [C.POINTER(MtState), C.POINTER(C.c_uint32), C.c_int64]
         L.orc_sse_expf.argtypes = [C.c_float]
         L.orc_sse_expf.restype = C.c_float
         L.orc_sse_logf.argtypes = [C.c_float]
@@ -231,6 +273,9 @@ class RefLib:
 
     def seed(self, seed: int):
         self.L.mag_ctx_set_prng_algorithm(self.ctx, 1, seed)  # MAG_PRNG_PCG
+
+    def seed_mt(self, seed: int):
+        self.L.mag_ctx_set_prng_algorithm(self.ctx, 0, seed)  # MAG_PRNG_MERSENNE_TWISTER
 
     def tensor(self, shape6):
         return self.L.mag_tensor_create_6d(self.ctx, 0, *[int(s) for s in shape6])
