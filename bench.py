@@ -1091,12 +1091,14 @@ def run_sweep_full(args):
                 cpu.append({"case": f"{op} 2^24", "rate": 8.0 * n / dt / 1e9, "unit": "GB/s"})
             dt = cpu_time(lambda: R.op("SUM", tx))
             cpu.append({"case": "full SUM 2^24", "rate": 4.0 * n / dt / 1e9, "unit": "GB/s"})
-            for kind in ("uniform", "normal"):
-                fill = getattr(R.L, f"mag_tensor_fill_random_{kind}")
-                t0 = time.perf_counter()
-                fill(tx, 0.0, 1.0)
-                cpu.append({"case": f"fill {kind} 2^24", "rate": 4.0 * n / (time.perf_counter() - t0) / 1e9,
-                            "unit": "GB/s"})
+            for alg, seed_fn in (("PCG", R.seed), ("MT19937", R.seed_mt)):
+                seed_fn(0x5EED0002)
+                for kind in ("uniform", "normal"):
+                    fill = getattr(R.L, f"mag_tensor_fill_random_{kind}")
+                    t0 = time.perf_counter()
+                    fill(tx, 0.0, 1.0)
+                    cpu.append({"case": f"fill {kind} {alg} 2^24",
+                                "rate": 4.0 * n / (time.perf_counter() - t0) / 1e9, "unit": "GB/s"})
             m = 1024
             ta, tb = R.tensor_nd((m, m)), R.tensor_nd((m, m))
             R.write(ta, v[:m * m])

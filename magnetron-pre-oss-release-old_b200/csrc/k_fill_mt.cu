@@ -21,10 +21,11 @@
 // stream.)  The future stream is cut into substreams of L words (L a multiple of 624, chosen by
 // the fill's size); the windows that start them are made by doubling: window 1 from the first
 // twisted block, then windows [h, 2h - 1) from windows [1, h) by a jump of (h - 1) L, so P
-// substreams take about log2(P) launches.  Each jump is shared by 16 CTAs that split q's set
-// bits and XOR their sums into the zeroed window.  Then one CTA per substream generates its
-// words 227 at a time in a 1024-word ring, tempers and maps them as the reference does and
-// writes its range of the output; Box-Muller pairs are formed in a second pass.
+// substreams take about log2(P) launches.  Each jump is shared by 16 to 64 CTAs that split q's
+// set bits and XOR their sums into the zeroed window.  Then one CTA per substream runs the
+// recurrence forward from its window, 454 words per barrier, tempers and maps the words as the
+// reference does and writes its range of the output; Box-Muller pairs are formed in a second
+// pass.
 //
 // The fill draws exactly the words the host generator would draw: first the words left in the
 // current block, then the future stream.  The state struct is left as the host generator leaves
@@ -51,10 +52,10 @@ constexpr int kMtMaxDegree = 19968;       // bits of a window; the minimal polyn
 constexpr int kMtLevels = 16;             // doubling levels: up to 2^16 + 1 substreams
 constexpr int kMtPolys = 1 + kMtLevels;   // x^(L - 624), then x^(L 2^v) for v = 0..15
 constexpr int kMtSets = 3;                // substream lengths, chosen by the fill's size
-constexpr int64_t kMtSubstream[kMtSets] = {624LL * 96, 624LL * 384, 624LL * 1536};
+constexpr int64_t kMtSubstream[kMtSets] = {624LL * 96, 624LL * 384, 624LL * 1536};  // substream length L
 constexpr int kMtThreads = 256;
-constexpr int kMtRing = 1024;             // generation ring (words); holds a window and a phase
-constexpr int kMtSplit = 16;              // CTAs sharing one window's jump
+constexpr int kMtRun = 8 * 2 * kMtLag;    // words a generation CTA forms between moves of its window
+constexpr int kMtChunk = kMtMaxDegree / 16;  // exponents per jump CTA: one window's jump is split 16 ways or more
 constexpr int kMtJumpWords = 34 * kMtN;   // 21216 >= offset 624 + exponent 19967 + 624
 constexpr int kMtOut = 208;               // jump threads: 3 window words each
 
@@ -74,32 +75,47 @@ __device__ __forceinline__ float mt_value(uint32_t y, float p0, float p1) {
 // Exponents of the jump polynomials' set bits, ascending: [set][poly][.. count).
 __device__ uint16_t g_mt_idx[kMtSets][kMtPolys][kMtMaxDegree];
 
+// Phase pairs.  Thread i < 227 forms words k = t + i and k + 227 of each 454-word step: the
+// word 227 back is the thread's own previous result (a register), and the words 624 and 623
+// back were formed at least one step earlier, so one barrier per step keeps them visible.
+
 // Window dst0 + b = the jump `idx` (cnt exponents) of the stream that starts `offset` words after
-// window src0 + b.  CTA (b, c) adds the exponents [c cnt / 16, (c + 1) cnt / 16); the destination
-// window is zero before the launch.
+// window src0 + b.  CTA (b, c) of gridDim.y adds the exponents [c cnt / Y, (c + 1) cnt / Y),
+// at most kMtChunk of them; the destination window is zero before the launch.
 __global__ void __launch_bounds__(kMtThreads) mt_jump(uint32_t* __restrict__ win, int src0, int dst0, int offset,
                                                       const uint16_t* __restrict__ idx, int cnt) {
     extern __shared__ uint32_t s[];  // kMtJumpWords
+    __shared__ uint16_t sidx[kMtChunk];
     const int tid = threadIdx.x;
-    const int lo = (int)((int64_t)cnt * blockIdx.y / kMtSplit);
-    const int hi = (int)((int64_t)cnt * (blockIdx.y + 1) / kMtSplit);
-    if (lo >= hi) return;
+    const int lo = (int)((int64_t)cnt * blockIdx.y / gridDim.y);
+    const int hi = (int)((int64_t)cnt * (blockIdx.y + 1) / gridDim.y);
+    if (lo >= hi || hi - lo > kMtChunk) return;  // the chunk bound holds for gridDim.y >= 16
     const int need = offset + (int)idx[hi - 1] + kMtN;  // stream words s[0 .. need) are read
     if (need > kMtJumpWords) return;                    // excluded by the degree check on the host
     const uint32_t* src = win + (size_t)(src0 + blockIdx.x) * kMtN;
     for (int i = tid; i < kMtN; i += kMtThreads) s[i] = src[i];
+    for (int i = tid; i < hi - lo; i += kMtThreads) sidx[i] = idx[lo + i];
     __syncthreads();
-    for (int t = kMtN; t < need; t += kMtLag) {
+    uint32_t prev = tid < kMtLag ? s[kMtN - kMtLag + tid] : 0u;
+    for (int t = kMtN; t < need; t += 2 * kMtLag) {
         const int k = t + tid;
-        if (tid < kMtLag && k < need) s[k] = mt_word(s[k - 624], s[k - 623], s[k - 227]);
+        if (tid < kMtLag && k < need) {
+            const uint32_t a0 = s[k - 624], a1 = s[k - 623], b0 = s[k - 397], b1 = s[k - 396];
+            prev = mt_word(a0, a1, prev);
+            s[k] = prev;
+            if (k + kMtLag < need) {
+                prev = mt_word(b0, b1, prev);
+                s[k + kMtLag] = prev;
+            }
+        }
         __syncthreads();
     }
     if (tid < kMtOut) {
         const uint32_t* base = s + offset + tid;
         uint32_t a0 = 0, a1 = 0, a2 = 0;
-#pragma unroll 4
-        for (int e = lo; e < hi; ++e) {
-            const int o = idx[e];
+#pragma unroll 8
+        for (int e = 0; e < hi - lo; ++e) {
+            const int o = sidx[e];
             a0 ^= base[o];
             a1 ^= base[o + kMtOut];
             a2 ^= base[o + 2 * kMtOut];
@@ -112,48 +128,81 @@ __global__ void __launch_bounds__(kMtThreads) mt_jump(uint32_t* __restrict__ win
 }
 
 struct MtGen {
-    const uint32_t* win;  // window p starts substream p; window 0 is the current block
+    const uint32_t* win;  // window p starts substream p (future word p L); window 0 is the current block
     uint32_t* last;       // out: the block that holds the last word drawn
     float* r;
-    int64_t first;        // words still to draw from the current block, from position `next`
-    int64_t future;       // words drawn after it
-    int64_t sub;          // words per substream
+    int64_t future;       // words drawn after the current block
+    int sub;              // L: words per substream
+    int first;            // words still to draw from the current block, from position `next`
     int next;
     float p0, p1;         // min, max - min (0, 1 for the normal fill's uniform pass)
 };
 
-// CTA p writes future words [p L, min((p + 1) L, future)) to r[first + ...]; CTA 0 also the
-// words left in the current block.  The CTA that draws the last word completes its block.
-__global__ void __launch_bounds__(kMtThreads) mt_generate(const MtGen g) {
-    __shared__ uint32_t s[kMtRing];
+// One step of thread tid < 227: words j and j + 227 of a substream (j = t + tid), from
+// q = &s[slot of word j - 624] (the buffer is linear within a run, so every access is q plus a
+// constant) into o = &out[j].  CHECK: the step may pass the words formed (span) or written (keep).
+template <bool CHECK>
+__device__ __forceinline__ void mt_step(uint32_t* q, float* o, uint32_t& prev, int j, int span, int keep, float p0,
+                                        float p1) {
+    const uint32_t a0 = q[0], a1 = q[1], b0 = q[kMtLag], b1 = q[kMtLag + 1];
+    if (!CHECK || j < span) {
+        prev = mt_word(a0, a1, prev);
+        q[kMtN] = prev;
+        if (!CHECK || j < keep) o[0] = mt_value(prev, p0, p1);
+        if (!CHECK || j + kMtLag < span) {
+            prev = mt_word(b0, b1, prev);
+            q[kMtN + kMtLag] = prev;
+            if (!CHECK || j + kMtLag < keep) o[kMtLag] = mt_value(prev, p0, p1);
+        }
+    }
+}
+
+// CTA p writes future words [p L, min((p + 1) L, future)) to r[first + ...], running the
+// stream forward from window p; CTA 0 also writes the words left in the current block.  The CTA
+// that draws the last word completes and keeps its block.  Words are formed in runs of up to 8
+// steps: s[0..624) holds the 624 words before the run, the run's words follow, and after each
+// run its last 624 words move to the front.
+__device__ __forceinline__ void mt_forward(const MtGen& g, uint32_t* s, const uint32_t* src, float* out, int keep,
+                                           bool last) {
     const int tid = threadIdx.x;
-    const int64_t p = blockIdx.x;
-    if (p == 0)
-        for (int i = tid; i < g.first; i += kMtThreads) g.r[i] = mt_value(g.win[g.next + i], g.p0, g.p1);
-    const int64_t w0 = p * g.sub;
-    if (w0 >= g.future) return;
-    const int64_t w1 = w0 + g.sub < g.future ? w0 + g.sub : g.future;
-    const bool last = w1 == g.future;
-    const int64_t end = last ? ((g.future - 1) / kMtN + 1) * kMtN : w1;
-    const uint32_t* src = g.win + p * kMtN;
+    const bool act = tid < kMtLag;
+    const int span = last ? ((keep - 1) / kMtN + 1) * kMtN : keep;  // words formed
     for (int i = tid; i < kMtN; i += kMtThreads) s[i] = src[i];
     __syncthreads();
-    float* out = g.r + g.first + w0;
-    const int64_t span = end - w0, keep = w1 - w0;
-    for (int64_t t = 0; t < span; t += kMtLag) {  // word j = t + tid sits in slot (j + 624) & 1023
-        const int64_t j = t + tid;
-        if (tid < kMtLag && j < span) {
-            const int k = (int)(j & (kMtRing - 1));
-            const uint32_t v = mt_word(s[k], s[(k + 1) & (kMtRing - 1)], s[(k + kMtN - kMtLag) & (kMtRing - 1)]);
-            s[(k + kMtN) & (kMtRing - 1)] = v;
-            if (j < keep) out[j] = mt_value(v, g.p0, g.p1);
+    uint32_t prev = act ? s[kMtN - kMtLag + tid] : 0u;  // word tid - 227
+    int j0 = 0, run = 0;
+    while (j0 < span) {
+        run = span - j0 < kMtRun ? span - j0 : kMtRun;
+        const int clean = keep - j0 < run ? keep - j0 : run;  // words of the run that are all written
+        int t = 0;
+        for (; t + 2 * kMtLag <= clean; t += 2 * kMtLag) {
+            if (act) mt_step<false>(s + t + tid, out + j0 + t + tid, prev, 0, 0, 0, g.p0, g.p1);
+            __syncthreads();
         }
-        __syncthreads();
+        for (; t < run; t += 2 * kMtLag) {
+            if (act) mt_step<true>(s + t + tid, out + j0 + t + tid, prev, t + tid, run, keep - j0, g.p0, g.p1);
+            __syncthreads();
+        }
+        j0 += run;
+        if (j0 < span) {  // run == kMtRun >= 624: the source and destination do not overlap
+            for (int i = tid; i < kMtN; i += kMtThreads) s[i] = s[run + i];
+            __syncthreads();
+        }
     }
-    if (last) {  // the last block starts at a block boundary at or after w0
-        const int64_t b0 = (g.future - 1) / kMtN * kMtN - w0;
-        for (int i = tid; i < kMtN; i += kMtThreads) g.last[i] = s[(int)((b0 + i + kMtN) & (kMtRing - 1))];
-    }
+    if (last)  // the last block = the last 624 words formed = s[run .. run + 624)
+        for (int i = tid; i < kMtN; i += kMtThreads) g.last[i] = s[run + i];
+}
+
+__global__ void __launch_bounds__(kMtThreads) mt_generate(const MtGen g) {
+    __shared__ __align__(16) uint32_t s[kMtN + kMtRun];
+    const int64_t p = blockIdx.x;
+    if (p == 0)
+        for (int i = threadIdx.x; i < g.first; i += kMtThreads)
+            g.r[i] = mt_value(g.win[g.next + i], g.p0, g.p1);
+    const int64_t w0 = p * g.sub;
+    if (w0 >= g.future) return;
+    const int keep = (int)(g.future - w0 < g.sub ? g.future - w0 : g.sub);  // words written
+    mt_forward(g, s, g.win + p * kMtN, g.r + g.first + w0, keep, w0 + keep == g.future);
 }
 
 __global__ void __launch_bounds__(kMtThreads) mt_box_muller(float* __restrict__ r, int64_t pairs, float mean,
@@ -378,7 +427,9 @@ int upload_set(int k, const MtSet& s, uint16_t** base) {
 }
 
 struct MtPlan {
-    int64_t first, future, subs, sub;
+    int64_t first, future;
+    int64_t subs;   // substreams (and windows), at future words 0, L, 2L, ...
+    int64_t sub;    // L
     int set;
 };
 
@@ -388,7 +439,10 @@ int plan_fill(int64_t n, uint32_t remaining, uint32_t next, MtPlan* p) {
         return (int)cudaErrorInvalidValue;  // not a state the host generator can be in
     p->first = (int64_t)remaining - 1 < n ? (int64_t)remaining - 1 : n;
     p->future = n - p->first;
-    p->set = p->future <= (1LL << 22) ? 0 : p->future <= (1LL << 26) ? 1 : 2;
+    // jumps cost about 1.2 us of the GPU per window at the widest level and 11-50 us per level
+    // below it; generation about 0.15-0.22 us per 454 words of one substream: these thresholds
+    // keep the sum near its minimum (2^24: 70 windows of 239616 words; 2^28: 281 of 958464)
+    p->set = p->future <= (1LL << 22) ? 0 : p->future <= (3LL << 24) ? 1 : 2;
     if (const char* f = getenv("MAG_CUDA_MT_SUBSTREAM_SET"))  // tests: deep jump levels at small sizes
         if (f[0] >= '0' && f[0] < '0' + kMtSets && !f[1]) p->set = f[0] - '0';
     p->sub = kMtSubstream[p->set];
@@ -444,16 +498,18 @@ extern "C" int mcu_launch_fill_mt(float* r, int64_t n, int normal, float p0, flo
         if (e == cudaSuccess)
             e = cudaMemsetAsync(win + kMtN, 0, (size_t)(p.subs - 1) * kMtN * sizeof(uint32_t), stream);
         if (e != cudaSuccess) return (int)e;
+        // a few windows: split each jump wider, so the level's latency shrinks
+        auto split = [](int64_t windows) { return windows <= 4 ? 64u : windows <= 16 ? 32u : 16u; };
         // window 1: L - 624 words past the first twisted block, which starts 624 words after window 0
-        mt_jump<<<dim3(1, kMtSplit), kMtThreads, smem, stream>>>(win, 0, 1, kMtN, idx, s.cnt[0]);
+        mt_jump<<<dim3(1, split(1)), kMtThreads, smem, stream>>>(win, 0, 1, kMtN, idx, s.cnt[0]);
         ++k;
         // windows [h, min(2h - 1, subs)) = windows [1, ..) jumped by (h - 1) L = L 2^v
         int v = 0;
         for (int64_t h = 2; h < p.subs; h = 2 * h - 1, ++v) {
             const int64_t cnt = (2 * h - 1 < p.subs ? 2 * h - 1 : p.subs) - h;
             const uint16_t* q = idx + (size_t)(1 + v) * kMtMaxDegree;
-            mt_jump<<<dim3((unsigned)cnt, kMtSplit), kMtThreads, smem, stream>>>(win, 1, (int)h, 0, q,
-                                                                                 s.cnt[1 + v]);
+            mt_jump<<<dim3((unsigned)cnt, split(cnt)), kMtThreads, smem, stream>>>(win, 1, (int)h, 0, q,
+                                                                                   s.cnt[1 + v]);
             ++k;
         }
     }
@@ -461,9 +517,9 @@ extern "C" int mcu_launch_fill_mt(float* r, int64_t n, int normal, float p0, flo
     g.win = win;
     g.last = last;
     g.r = r;
-    g.first = p.first;
+    g.first = (int)p.first;
     g.future = p.future;
-    g.sub = p.sub;
+    g.sub = (int)p.sub;
     g.next = (int)st[1];
     g.p0 = normal ? 0.0f : p0;
     g.p1 = normal ? 1.0f : p1;

@@ -25,13 +25,14 @@ def _same_state(g: MB.Mt19937, ref) -> bool:
     return (a.remaining, a.next) == (b.remaining, b.next) and list(a.state) == list(b.state)
 
 
-@pytest.mark.parametrize("n", [1, 3, 623, 624, 625, 1000, 4099, 2 * 59904 + 17, (1 << 22) + 3, (1 << 26) + 5,
+@pytest.mark.parametrize("n", [1, 3, 623, 624, 625, 1000, 4099, 2 * 59904 + 17, 3 * 59904 + 5, (1 << 22) + 3, (1 << 26) + 5,
                                (1 << 27) + 7])
 @pytest.mark.parametrize("lo,hi", [(0.0, 1.0), (-0.0759, 0.0759)])
 def test_uniform_bit_exact(n, lo, hi):
-    """Sizes inside the first block, at block edges, across a few substreams, and at each of the
-    three substream lengths (2^22 + 3 and 2^26 + 5 cross the size thresholds; 2^27 + 7 is 141
-    substreams, eight doubling launches)."""
+    """Sizes inside the first block, at block edges, across a few substreams (3 * 59904 + 5 ends
+    five words into its last substream), and at each of the three substream lengths (2^22 + 3
+    just past the first size threshold, 18 substreams; 2^26 + 5 and 2^27 + 7 in the longest, 71
+    and 141 substreams, the latter from eight doubling launches)."""
     if n > (1 << 26) and lo != 0.0:
         pytest.skip("one range is enough at 2^27")
     dev, o = device(), oracle()
@@ -72,7 +73,7 @@ def test_fills_continue_the_stream_mid_block_and_unaligned():
 
 def test_deep_doubling_levels(monkeypatch):
     """The shortest substreams forced at 2^26 + 9 values: 1121 substreams, eleven doubling
-    launches (windows up to 2^10 L past the first), bit-exact."""
+    launches (jumps up to 2^10 L), bit-exact."""
     monkeypatch.setenv("MAG_CUDA_MT_SUBSTREAM_SET", "0")
     dev, o = device(), oracle()
     n = (1 << 26) + 9
