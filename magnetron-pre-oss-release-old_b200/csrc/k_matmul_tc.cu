@@ -285,7 +285,7 @@ struct Cfg {
     static constexpr int BIAS_BYTES = kEpiWarps * 32 * 32 * 4;
     static constexpr int SMEM_BIAS = STAGES * STAGE_BYTES + 1024 + BIAS_BYTES + 1024;
     static_assert(TMEM_COLS <= 512, "two accumulators must fit TMEM");
-    static_assert(SMEM_BIAS <= 227 * 1024, "ring and bias staging must fit shared memory");
+    static_assert(SMEM <= 227 * 1024, "the ring must fit shared memory");
 };
 
 // Epilogue of a fused dense layer: out = act(acc + bias) and, for the next
@@ -769,7 +769,13 @@ __global__ void __maxnreg__(kLaunchRegs)
                             a[2] = unscale(a[2], ea + e4.z);
                             a[3] = unscale(a[3], ea + e4.w);
                         }
-                        if (row_ok) *(float4*)(out + c * 32 + j) = make_float4(a[0], a[1], a[2], a[3]);
+                        if (row_ok) {
+                            const float4 o4 = make_float4(a[0], a[1], a[2], a[3]);
+                            // the product's result is not read again here: evict it first, so it
+                            // displaces the split operands of later tiles as little as possible
+                            if (tail) *(float4*)(out + c * 32 + j) = o4;
+                            else __stcs((float4*)(out + c * 32 + j), o4);
+                        }
                     }
                     continue;
                 }
@@ -1247,7 +1253,7 @@ __global__ void __launch_bounds__(256) split_cols_t_f16(const float* __restrict_
         if (k < K) {
             const float* py = y + k * N + n;
             if (vec && n + 4 <= N) {
-                v = *(const float4*)py;
+                v = __ldcs((const float4*)py);  // Y's last read: evict first, keep the split halves in L2
             } else {
                 v.x = n < N ? py[0] : 0.0f;
                 v.y = n + 1 < N ? py[1] : 0.0f;
@@ -1544,8 +1550,9 @@ template <bool FUSED, bool F16, bool PAIR>
 int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c, const CUtensorMap& d,
                 const CUtensorMap& bias, float* r, int64_t M, int64_t N, int64_t kp, int* status, const Epi& epi,
                 int64_t B, cudaStream_t st, int kparts, int kpc, int split_from, float* part_out, float* tail_out) {
-    constexpr int STG = PAIR ? kStagesPair : kStages;
+    constexpr int STG = PAIR ? (FUSED ? kStagesPair : kStagesPair + 1) : kStages;
     using C = Cfg<kBN, STG, PAIR>;
+    static_assert(!FUSED || C::SMEM_BIAS <= 227 * 1024, "ring and bias staging must fit shared memory");
     auto kern = gemm_3x<kBN, STG, FUSED, F16, PAIR>;
     const int smem = FUSED ? C::SMEM_BIAS : C::SMEM;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
