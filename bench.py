@@ -305,6 +305,54 @@ class _CudaArray:
                                          "stream": None}
 
 
+def sharded_check(dev, MB, torch, world, rank, local, stream):
+    """Element ranges and the full SUM sharded over the ranks, checked against one GPU's result
+    (run by every rank after the timed region, same collectives in the same order): every rank
+    generates the same seeded 2^24 + 6-element vectors, adds its contiguous range, the ranges are
+    all-gathered over NCCL and compared bit for bit with the whole ADD on this GPU; each rank
+    reduces its range to a 24-byte record, the records are combined in rank order into the full
+    SUM, compared with the one-GPU full SUM of the same vector."""
+    import torch.distributed as dist
+    import dp
+
+    total = (1 << 24) + 6  # not a multiple of 2, 4 or 8 ranks: shards of unequal length
+    start, n = dp.shard_rows(total, world, rank)
+    dvc = torch.device("cuda", local)
+    x, y, rf = dev.tensor((total,)), dev.tensor((total,)), dev.tensor((total,))
+    xs, ys, rs = dev.tensor((n,)), dev.tensor((n,)), dev.tensor((n,))
+    dev.fill_random_normal(x, 0.0, 1.0, MB.Pcg(0x5EED0E00))
+    dev.fill_random_normal(y, 0.0, 1.0, MB.Pcg(0x5EED0E01))
+    view = lambda t, k: torch.as_tensor(_CudaArray(t.data_ptr, k, dev.stream), device=dvc)
+    # this rank's range, copied by the backend (x * 1.0 is x), so it knows the shard is written
+    for src, dst in ((x, xs), (y, ys)):
+        MB.check(dev.L.mag_cuda_unary_f32(dev.p, MB.OP["MULS"], dst.data_ptr, src.data_ptr + 4 * start, 1, n, n, n,
+                                          1.0), "range copy")
+    d6 = lambda k: (MB.i64x6([k, 1, 1, 1, 1, 1]), MB.i64x6(MB.strides6([k, 1, 1, 1, 1, 1])))
+    dn, sn = d6(n)
+    dt, stt = d6(total)
+    MB.check(dev.L.mag_cuda_binary_f32(dev.p, MB.OP["ADD"], rs.data_ptr, xs.data_ptr, ys.data_ptr, dn, sn, sn, dn,
+                                       sn), "sharded add")
+    MB.check(dev.L.mag_cuda_binary_f32(dev.p, MB.OP["ADD"], rf.data_ptr, x.data_ptr, y.data_ptr, dt, stt, stt, dt,
+                                       stt), "whole add")
+    res = dev.tensor((2,))
+    dp.reduce_full(dev, "SUM", xs, res.data_ptr, world)
+    MB.check(dev.L.mag_cuda_reduce_f32(dev.p, MB.OP["SUM"], res.data_ptr + 4, x.data_ptr, dt, stt), "whole sum")
+    with torch.cuda.stream(stream):
+        gathered = dp.gather_rows(view(rs, n), total, 1, world, rank)
+        same = torch.equal(gathered.view(torch.int32), view(rf, total).view(torch.int32))
+        flag = torch.tensor([1 if same else 0], dtype=torch.int32, device=dvc)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    dev.sync()
+    torch.cuda.synchronize()
+    s_sharded, s_one = (float(v) for v in res.read())
+    for t in (x, y, rf, xs, ys, rs, res):
+        t.free()
+    return {"elements": total, "ranks": world, "add_gathered_bitwise_equal_one_gpu": bool(flag.item()),
+            "sum_sharded": s_sharded, "sum_one_gpu": s_one,
+            "sum_rel_diff": abs(s_sharded - s_one) / max(abs(s_one), 1e-30),
+            "note": "every rank's range added and all-gathered over NCCL; range records combined in rank order"}
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -484,6 +532,7 @@ def run_ours(args):
     if rank == 0 and world == 1 and not args.no_sweep:
         line["sweep"] = sweep(dev, MB, torch, local)
     if world > 1:
+        line["sharded_check"] = sharded_check(dev, MB, torch, world, rank, local, stream)
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
     if rank == 0:
