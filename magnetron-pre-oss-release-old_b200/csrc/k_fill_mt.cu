@@ -85,7 +85,7 @@ __device__ uint16_t g_mt_idx[kMtSets][kMtPolys][kMtMaxDegree];
 __global__ void __launch_bounds__(kMtThreads) mt_jump(uint32_t* __restrict__ win, int src0, int dst0, int offset,
                                                       const uint16_t* __restrict__ idx, int cnt) {
     extern __shared__ uint32_t s[];  // kMtJumpWords
-    __shared__ uint16_t sidx[kMtChunk];
+    __shared__ __align__(16) uint16_t sidx[kMtChunk];
     const int tid = threadIdx.x;
     const int lo = (int)((int64_t)cnt * blockIdx.y / gridDim.y);
     const int hi = (int)((int64_t)cnt * (blockIdx.y + 1) / gridDim.y);
@@ -113,13 +113,27 @@ __global__ void __launch_bounds__(kMtThreads) mt_jump(uint32_t* __restrict__ win
     if (tid < kMtOut) {
         const uint32_t* base = s + offset + tid;
         uint32_t a0 = 0, a1 = 0, a2 = 0;
-#pragma unroll 8
-        for (int e = 0; e < hi - lo; ++e) {
-            const int o = sidx[e];
+        auto add = [&](int o) {
             a0 ^= base[o];
             a1 ^= base[o + kMtOut];
             a2 ^= base[o + 2 * kMtOut];
+        };
+        // exponents eight at a time (one 16-byte shared load), then the rest one by one
+        const int ne = hi - lo, ne8 = ne & ~7;
+        const uint4* sv = reinterpret_cast<const uint4*>(sidx);
+#pragma unroll 2
+        for (int e = 0; e < ne8; e += 8) {
+            const uint4 w = sv[e >> 3];
+            add((int)(w.x & 0xffffu));
+            add((int)(w.x >> 16));
+            add((int)(w.y & 0xffffu));
+            add((int)(w.y >> 16));
+            add((int)(w.z & 0xffffu));
+            add((int)(w.z >> 16));
+            add((int)(w.w & 0xffffu));
+            add((int)(w.w >> 16));
         }
+        for (int e = ne8; e < ne; ++e) add(sidx[e]);
         uint32_t* dst = win + (size_t)(dst0 + blockIdx.x) * kMtN + tid;
         atomicXor(dst, a0);
         atomicXor(dst + kMtOut, a1);
