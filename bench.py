@@ -972,7 +972,9 @@ def run_sweep_full(args):
             t.write(src[:m].numpy(), offset_elems=off)
         return t
 
-    clocks = ClockSampler(torch.cuda.current_device(), interval=0.001)
+    # 5 ms between samples: a faster in-process sampler competes with the launching thread and
+    # stretches the short rows
+    clocks = ClockSampler(torch.cuda.current_device(), interval=0.005)
     clocks.start()
     window = [0.0, 0.0]
 
@@ -1077,15 +1079,8 @@ def run_sweep_full(args):
                 5)
     rec("fill", "normal MT19937 + Box-Muller 2^28", ms, 4.0 * n / 1e9, "GB/s", hbm)
     r.free()
-    # ---- config 4: matmul
-    for m in (1024, 4096, 8192, 16384):
-        a = filled(m * m, lambda c: c * (m ** -0.25))
-        c_ = dev.tensor((m * m,))
-        ms = timeit(lambda: dev.L.mag_cuda_matmul_f32(dev.p, c_.data_ptr, a.data_ptr, a.data_ptr, m, m, m),
-                    5 if m < 16384 else 2)
-        rec("matmul", f"square {m}^3 ({SPLIT_NAME} tcgen05)", ms, 2.0 * m ** 3 / 1e12, "TFLOP/s", tf)
-        a.free()
-        c_.free()
+    # ---- config 4: matmul (skinny and batched first, and config 1 before the square products:
+    # the large products' power draw lowers the clock for a while after them)
     k = nn = 4096
     b = filled(k * nn, lambda c: c * (k ** -0.25))
     for m in (1, 8, 64):
@@ -1111,6 +1106,14 @@ def run_sweep_full(args):
         "samples/s", None)
     for t in keep:
         t.free()
+    for m in (1024, 4096, 8192, 16384):
+        a = filled(m * m, lambda c: c * (m ** -0.25))
+        c_ = dev.tensor((m * m,))
+        ms = timeit(lambda: dev.L.mag_cuda_matmul_f32(dev.p, c_.data_ptr, a.data_ptr, a.data_ptr, m, m, m),
+                    5 if m < 16384 else 2)
+        rec("matmul", f"square {m}^3 ({SPLIT_NAME} tcgen05)", ms, 2.0 * m ** 3 / 1e12, "TFLOP/s", tf)
+        a.free()
+        c_.free()
     # ---- reference CPU, single thread, on this host
     cpu = []
     if not args.no_cpu_baseline:
