@@ -219,8 +219,9 @@ __device__ __forceinline__ void umma_commit_pair_local(uint64_t* bar) {
 
 // Shared-memory matrix descriptor: K-major rows of ROW_BYTES bytes, swizzled (64B
 // or 128B), 8-row atoms 8*ROW_BYTES bytes apart.
+template <int RB = ROW_BYTES>
 __device__ __forceinline__ uint64_t sw_desc(uint32_t saddr) {
-    constexpr uint32_t row_bytes = ROW_BYTES;
+    constexpr uint32_t row_bytes = RB;
     uint64_t d = 0;
     d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
     d |= (uint64_t)1 << 16;                         // leading byte offset (unused for swizzled K-major)
@@ -274,10 +275,10 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb
 }
 
 // ------------------------------------------------------------ the GEMM
-template <int BN, int STAGES, bool PAIR = false>
+template <int BN, int STAGES, bool PAIR = false, int RB = ROW_BYTES>
 struct Cfg {
-    static constexpr int A_BYTES = BM * ROW_BYTES;
-    static constexpr int B_BYTES = (PAIR ? BN / 2 : BN) * ROW_BYTES;  // a pair splits Y's rows between its CTAs
+    static constexpr int A_BYTES = BM * RB;
+    static constexpr int B_BYTES = (PAIR ? BN / 2 : BN) * RB;  // a pair splits Y's rows between its CTAs
     static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;
     static constexpr int TMEM_COLS = 2 * BN;
     static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 512;
@@ -371,14 +372,14 @@ __device__ __forceinline__ void decode_unit(int u, int split_from, int kparts, i
     }
 }
 
-template <int BN, int STAGES, bool FUSED, bool F16, bool PAIR>
+template <int BN, int STAGES, bool FUSED, bool F16, bool PAIR, int RB = ROW_BYTES>
 __global__ void __maxnreg__(kLaunchRegs)
     gemm_3x(const __grid_constant__ CUtensorMap map_xhi, const __grid_constant__ CUtensorMap map_xlo,
                 const __grid_constant__ CUtensorMap map_yhi, const __grid_constant__ CUtensorMap map_ylo,
                 const __grid_constant__ CUtensorMap map_bias, float* __restrict__ r, int M, int N, int Kp, int64_t ldr, int* status, const Epi epi,
                 int seg_kb, int first_kb, int batch, int kparts, int kpc, int split_from, float* __restrict__ part_out,
                 float* __restrict__ tail_out, int stall) {
-    using C = Cfg<BN, STAGES, PAIR>;
+    using C = Cfg<BN, STAGES, PAIR, RB>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t* ring = smem;
@@ -404,7 +405,7 @@ __global__ void __maxnreg__(kLaunchRegs)
     const int num_n = (N + BN - 1) / BN;
     const int tiles_per_batch = num_m * num_n;
     const int tiles = tiles_per_batch * batch;  // batch b's operands start at rows b*M (X) and b*N (Y)
-    constexpr int KE = F16 ? BK16 : BK;          // K elements per ring stage
+    constexpr int KE = RB / (F16 ? 2 : 4);       // K elements per ring stage
     const int nk = Kp / KE;
     // Work units: tiles [0, split_from) whole, one unit each; tiles [split_from, tiles) cut into
     // kparts units of kpc K stages (kparts > 1, one batch, no fused epilogue).  split_from == 0:
@@ -508,11 +509,11 @@ __global__ void __maxnreg__(kLaunchRegs)
                         tc_fence_after();
                         const uint32_t base = smem_u32(ring + s * C::STAGE_BYTES);
 #pragma unroll
-                        for (int kk = 0; kk < ROW_BYTES / 32; ++kk) {  // one MMA consumes 32 bytes of K
-                            const uint64_t xhi = sw_desc(base + kk * 32);
-                            const uint64_t xlo = sw_desc(base + C::A_BYTES + kk * 32);
-                            const uint64_t yhi = sw_desc(base + 2 * C::A_BYTES + kk * 32);
-                            const uint64_t ylo = sw_desc(base + 2 * C::A_BYTES + C::B_BYTES + kk * 32);
+                        for (int kk = 0; kk < RB / 32; ++kk) {  // one MMA consumes 32 bytes of K
+                            const uint64_t xhi = sw_desc<RB>(base + kk * 32);
+                            const uint64_t xlo = sw_desc<RB>(base + C::A_BYTES + kk * 32);
+                            const uint64_t yhi = sw_desc<RB>(base + 2 * C::A_BYTES + kk * 32);
+                            const uint64_t ylo = sw_desc<RB>(base + 2 * C::A_BYTES + C::B_BYTES + kk * 32);
                             umma<F16, PAIR>(d, xlo, yhi, idesc, (kb != kb0 || kk != 0) ? 1u : 0u);
                             umma<F16, PAIR>(d, xhi, ylo, idesc, 1);
                             umma<F16, PAIR>(d, xhi, yhi, idesc, 1);
@@ -1350,17 +1351,20 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-// 2-D map over a [rows][Kp] array of f32 or f16, box = box_rows x 64 bytes, 64-byte swizzle.
-bool make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t kp, int box_rows, bool f16) {
+// 2-D map over a [rows][Kp] array of f32 or f16, box = box_rows x rb bytes (64 or 128), swizzled
+// by rb bytes.
+bool make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t kp, int box_rows, bool f16,
+              int rb = ROW_BYTES) {
     auto fn = encode_fn();
     if (!fn) return false;
     const int es = f16 ? 2 : 4;
     cuuint64_t dims[2] = {(cuuint64_t)kp, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)(kp * es)};
-    cuuint32_t box[2] = {(cuuint32_t)(ROW_BYTES / es), (cuuint32_t)box_rows};
+    cuuint32_t box[2] = {(cuuint32_t)(rb / es), (cuuint32_t)box_rows};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = fn(m, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void*)base, dims,
-                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    rb == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
@@ -1401,6 +1405,19 @@ bool use_pairs() {
     return v == 1;
 }
 
+// Pair products of the f16 split stage 128 bytes of K per row (64 f16, 128-byte swizzle, three
+// 64 KB stages): half the TMA rows of 64-byte stages for the same bytes, 2-4 % faster on every
+// size measured.  MAG_CUDA_TC_ROW128=0 (unfused products) and MAG_CUDA_TC_ROW128_FUSED=0 (fused
+// layers) return to 64-byte rows.
+bool wide_rows(bool fused) {
+    static int v[2] = {-2, -2};
+    if (v[fused] == -2) {
+        const char* e = getenv(fused ? "MAG_CUDA_TC_ROW128_FUSED" : "MAG_CUDA_TC_ROW128");
+        v[fused] = (e && *e == '0') ? 0 : 1;
+    }
+    return v[fused] == 1;
+}
+
 // Pairs compute 256-row tiles: products with fewer rows run one CTA per 128-row tile.
 bool pair_for(int64_t M, bool f16) { return f16 && use_pairs() && M >= 2 * BM; }
 
@@ -1421,14 +1438,14 @@ int choose_parts(int64_t M, int64_t K, int64_t N, bool f16) {
     return (int)((nk + kpc - 1) / kpc);  // no empty part
 }
 
-TailPlan plan_tail(int64_t B, int64_t M, int64_t K, int64_t N, bool f16) {
+TailPlan plan_tail(int64_t B, int64_t M, int64_t K, int64_t N, bool f16, int ke = 0) {
     TailPlan tp;
     const bool pair = pair_for(M, f16);
     const int64_t tm = pair ? 2 * BM : BM;
     const int64_t tiles = B * ((M + tm - 1) / tm) * ((N + 255) / 256);
     const int64_t units = pair ? sm_count() / 2 : sm_count();
     const int64_t kp = (K + KPAD - 1) / KPAD * KPAD;
-    const int64_t nk = kp / (f16 ? BK16 : BK);
+    const int64_t nk = kp / (ke ? ke : (f16 ? BK16 : BK));
     // (from 8 waves on, a mostly empty last wave costs under 1/16 of the product)
     if (tiles <= units || tiles >= 8 * units) return tp;
     const int64_t rem = tiles % units;
@@ -1500,14 +1517,14 @@ constexpr int kStages = 4;
 // segment length instead of K (at K = 16384: 2.0e-6 of max|C| for f16 at 512, 2.1e-6 for
 // tf32 at 256).  Longer segments give the epilogue more time per accumulator.  0 = one
 // segment spanning K.  Returned in ring stages.
-int segment_kb(bool f16) {
+int segment_kb(bool f16, int ke = 0) {
     static int k = -2;
     if (k == -2) {
         const char* e = getenv("MAG_CUDA_TC_SEGMENT");
         k = (e && *e) ? atoi(e) : -1;
     }
     const int seg = k == -1 ? (f16 ? 512 : 256) : k;
-    const int ke = f16 ? BK16 : BK;
+    if (!ke) ke = f16 ? BK16 : BK;
     return seg <= 0 ? (1 << 30) : (seg + ke - 1) / ke;
 }
 
@@ -1515,14 +1532,14 @@ int segment_kb(bool f16) {
 // stages.  The epilogue's stores of one tile overlap the MMAs of the next tile's first two
 // segments, so a long first segment hides them while short later segments keep the truncation
 // of the tensor-core accumulator small.
-int segment_first_kb(bool f16) {
+int segment_first_kb(bool f16, int ke = 0) {
     static int k = -2;
     if (k == -2) {
         const char* e = getenv("MAG_CUDA_TC_SEGMENT_FIRST");
         k = (e && *e) ? atoi(e) : -1;
     }
-    if (k == -1) return segment_kb(f16);
-    const int ke = f16 ? BK16 : BK;
+    if (k == -1) return segment_kb(f16, ke);
+    if (!ke) ke = f16 ? BK16 : BK;
     return k <= 0 ? (1 << 30) : (k + ke - 1) / ke;
 }
 
@@ -1546,14 +1563,16 @@ int test_stall() {
     return e && e[0] == '1';
 }
 
-template <bool FUSED, bool F16, bool PAIR>
+template <bool FUSED, bool F16, bool PAIR, int RB = ROW_BYTES>
 int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c, const CUtensorMap& d,
                 const CUtensorMap& bias, float* r, int64_t M, int64_t N, int64_t kp, int* status, const Epi& epi,
                 int64_t B, cudaStream_t st, int kparts, int kpc, int split_from, float* part_out, float* tail_out) {
-    constexpr int STG = PAIR ? (FUSED ? kStagesPair : kStagesPair + 1) : kStages;
-    using C = Cfg<kBN, STG, PAIR>;
+    // 128-byte rows double a stage: three of them fit beside the barriers
+    constexpr int STG = RB == 128 ? 3 : PAIR ? (FUSED ? kStagesPair : kStagesPair + 1) : kStages;
+    using C = Cfg<kBN, STG, PAIR, RB>;
     static_assert(!FUSED || C::SMEM_BIAS <= 227 * 1024, "ring and bias staging must fit shared memory");
-    auto kern = gemm_3x<kBN, STG, FUSED, F16, PAIR>;
+    constexpr int KE = RB / (F16 ? 2 : 4);
+    auto kern = gemm_3x<kBN, STG, FUSED, F16, PAIR, RB>;
     const int smem = FUSED ? C::SMEM_BIAS : C::SMEM;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return (int)e;
@@ -1564,7 +1583,7 @@ int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c
     if constexpr (!PAIR) {
         const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
         kern<<<grid, kThreads, smem, st>>>(a, b, c, d, bias, r, (int)M, (int)N, (int)kp, (int64_t)N, status, epi,
-                                           segment_kb(F16), segment_first_kb(F16), (int)B, kparts, kpc, split_from,
+                                           segment_kb(F16, KE), segment_first_kb(F16, KE), (int)B, kparts, kpc, split_from,
                                            part_out, tail_out, test_stall());
         return (int)cudaGetLastError();
     } else {
@@ -1588,7 +1607,7 @@ int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c
         const int64_t clusters = tiles < max_clusters ? tiles : max_clusters;
         cfg.gridDim = dim3((unsigned)(2 * clusters));
         e = cudaLaunchKernelEx(&cfg, kern, a, b, c, d, bias, r, (int)M, (int)N, (int)kp, (int64_t)N, status, epi,
-                               segment_kb(F16), segment_first_kb(F16), (int)B, kparts, kpc, split_from, part_out,
+                               segment_kb(F16, KE), segment_first_kb(F16, KE), (int)B, kparts, kpc, split_from, part_out,
                                tail_out, test_stall());
         return (int)e;
     }
@@ -1689,8 +1708,12 @@ static int launch_tc(float* r, const float* x, const float* y, int64_t B, int64_
     const bool h = f16 != 0;
     const bool pair = pair_for(M, h);
     const int yrows = pair ? kBN / 2 : kBN;
-    if (!make_map(&mxh, xhi, B * M, l.kp, BM, h) || !make_map(&mxl, xlo, B * M, l.kp, BM, h) ||
-        !make_map(&myh, yhi, B * N, l.kp, yrows, h) || !make_map(&myl, ylo, B * N, l.kp, yrows, h))
+    // unfused, unsplit pair products may stage 128 bytes of K per row (64 f16)
+    const bool any_fused = ep && (ep->bias || ep->bias_zero || ep->act || (ep->out_hi && !f16));
+    const bool wide = h && pair && (B == 1 ? l.kparts : 1) == 1 && l.kp % 64 == 0 && wide_rows(any_fused);
+    const int rb = wide ? 128 : ROW_BYTES;
+    if (!make_map(&mxh, xhi, B * M, l.kp, BM, h, rb) || !make_map(&mxl, xlo, B * M, l.kp, BM, h, rb) ||
+        !make_map(&myh, yhi, B * N, l.kp, yrows, h, rb) || !make_map(&myl, ylo, B * N, l.kp, yrows, h, rb))
         return (int)cudaErrorInvalidValue;
     Epi chk{};  // the f16 split's floor check (no fields for tf32)
     chk.row_exp = rexp;
@@ -1732,7 +1755,10 @@ static int launch_tc(float* r, const float* x, const float* y, int64_t B, int64_
         memset(&mb, 0, sizeof(mb));
         epi.bias_map = ep->bias && make_bias_map(&mb, ep->bias, M, N);
         int rc;
-        if (pair)
+        if (wide)
+            rc = launch_gemm<true, true, true, 128>(mxh, mxl, myh, myl, mb, r, M, N, l.kp, status, epi, B, st, 1, 0, 0,
+                                                    nullptr, nullptr);
+        else if (pair)
             rc = launch_gemm<true, true, true>(mxh, mxl, myh, myl, mb, r, M, N, l.kp, status, epi, B, st, 1, 0, 0,
                                                nullptr, nullptr);
         else
@@ -1747,7 +1773,7 @@ static int launch_tc(float* r, const float* x, const float* y, int64_t B, int64_
     int gparts = kparts, gkpc = l.kpc, split_from = 0;
     float* tail = nullptr;
     if (kparts == 1 && !fused) {
-        const TailPlan tp = plan_tail(B, M, K, N, h);
+        const TailPlan tp = plan_tail(B, M, K, N, h, wide ? 64 : 0);  // no more parts than the buffer holds
         if (tp.parts > 1) {
             gparts = tp.parts;
             gkpc = tp.kpc;
@@ -1755,8 +1781,10 @@ static int launch_tc(float* r, const float* x, const float* y, int64_t B, int64_
             tail = (float*)(base + l.tail);
         }
     }
-    int rc = pair ? launch_gemm<false, true, true>(mxh, mxl, myh, myl, mxh, r, M, N, l.kp, status, plain, B, st, gparts,
-                                                   gkpc, split_from, part, tail)
+    int rc = wide ? launch_gemm<false, true, true, 128>(mxh, mxl, myh, myl, mxh, r, M, N, l.kp, status, plain, B, st,
+                                                        gparts, gkpc, split_from, part, tail)
+         : pair ? launch_gemm<false, true, true>(mxh, mxl, myh, myl, mxh, r, M, N, l.kp, status, plain, B, st, gparts,
+                                                 gkpc, split_from, part, tail)
          : f16 ? launch_gemm<false, true, false>(mxh, mxl, myh, myl, mxh, r, M, N, l.kp, status, plain, B, st, gparts,
                                                  gkpc, split_from, part, tail)
                : launch_gemm<false, false, false>(mxh, mxl, myh, myl, mxh, r, M, N, l.kp, status, plain, B, st, gparts,
