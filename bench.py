@@ -540,7 +540,7 @@ def run_ours(args):
 
 
 def sweep(dev, MB, torch, local):
-    """Short device-timed throughput of the other BASELINE op families (HBM GB/s, TFLOP/s)."""
+    """Short device-timed throughput of the other benchmarked op families (HBM GB/s, TFLOP/s)."""
     out = {}
     stream = torch.cuda.ExternalStream(dev.stream, device=torch.device("cuda", local))
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -947,7 +947,7 @@ def run_sharded(args):
 
 
 def run_sweep_full(args):
-    """Every other BASELINE configuration on one GPU: elementwise/broadcast/unary (config 2),
+    """Every other benchmarked configuration on one GPU: elementwise/broadcast/unary (config 2),
     row reductions and softmax (config 3), the matmul sweep (config 4), each with its roofline
     fraction, and single-thread reference CPU rates for the sizes the CPU finishes quickly."""
     import torch
@@ -1203,7 +1203,7 @@ def main():
                                                       "fill_uniform", "fill_normal", "fill_const", "fill_mt_uniform", "fill_mt_normal", "storage", "image", "sharded", "mlp2"],
                     help="run one kernel family for a profiler instead of the benchmark")
     ap.add_argument("--size", type=int, default=None)
-    ap.add_argument("--sweep-full", action="store_true", help="measure every other BASELINE configuration")
+    ap.add_argument("--sweep-full", action="store_true", help="measure every other benchmarked configuration")
     ap.add_argument("--out", default=None)
     args = ap.parse_args()
     if args.sweep_full:

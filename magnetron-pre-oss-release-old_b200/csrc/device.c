@@ -723,7 +723,7 @@ int mag_cuda_synchronize(mag_compute_device_t* dvc) {
     e = cudaMemcpy(&st, d->d_status, sizeof(int), cudaMemcpyDeviceToHost);
     if (e != cudaSuccess) return (int)e;
     if (!st) return 0;
-    /* reported once: the word is cleared, so later work on this device is judged on its own */
+    /* reported once: the word is cleared, so later work on this device reports its own status */
     e = cudaMemset(d->d_status, 0, sizeof(int));
     return e != cudaSuccess ? (int)e : MAG_CUDA_E_DEVICE_WAIT;
 }
