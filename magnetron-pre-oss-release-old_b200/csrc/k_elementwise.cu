@@ -354,8 +354,10 @@ struct RowWalk {
 // Rows of at most 128 * STEPS columns, vectorised: a warp walks `chunk` consecutive rows
 // (kRowChunk, fewer when the tensor has few rows),
 // decomposing the first row's indices once and carrying them to the next rows, with several
-// rows' loads in flight before their stores.
-template <int OP, int STEPS>
+// rows' loads in flight before their stores.  ONCE = 1 (2): x's (y's) row is the same for every
+// row of a chunk (its dim 1 has extent 1 and chunks do not cross dim 1), so it is loaded once
+// per chunk and only the other operand's rows per row.
+template <int OP, int STEPS, int ONCE>
 __global__ void __launch_bounds__(kThreads, 2) binary_rows_chunked(float* __restrict__ r, const float* __restrict__ x,
                                                                    const float* __restrict__ y, const RowParams p,
                                                                    uint32_t nrows, uint32_t nchunks, uint32_t chunk) {
@@ -404,6 +406,35 @@ __global__ void __launch_bounds__(kThreads, 2) binary_rows_chunked(float* __rest
         RowWalk w;
         w.start(row0, p);
         const uint32_t rows_here = min(chunk, nrows - row0);
+        if constexpr (ONCE != 0) {
+            // one operand's row for the whole chunk, the other's R rows in flight
+            constexpr int R = STEPS <= 2 ? 8 : 2;
+            float4 fixed[STEPS];
+            if constexpr (ONCE == 1) load_x(w.xo, fixed);
+            else load_y(w.yo, fixed);
+            for (uint32_t rr = 0; rr < rows_here; rr += R) {
+                float4 v[R][STEPS];
+                int64_t ro[R];
+                const uint32_t nr = min((uint32_t)R, rows_here - rr);
+#pragma unroll
+                for (int k = 0; k < R; ++k) {
+                    if ((uint32_t)k < nr) {
+                        ro[k] = w.ro;
+                        if constexpr (ONCE == 1) load_y(w.yo, v[k]);
+                        else load_x(w.xo, v[k]);
+                        w.next(p);
+                    }
+                }
+#pragma unroll
+                for (int k = 0; k < R; ++k) {
+                    if ((uint32_t)k < nr) {
+                        if constexpr (ONCE == 1) store_row(ro[k], fixed, v[k]);
+                        else store_row(ro[k], v[k], fixed);
+                    }
+                }
+            }
+            continue;
+        }
         // R rows' loads in flight before their stores: 4 for rows of at most 256 columns
         // (the loads are L2 latency-bound there; 114 registers allow 2 CTAs per SM), else 2
         constexpr int R = STEPS <= 2 ? 4 : 2;
@@ -468,12 +499,24 @@ cudaError_t launch_rows(float* r, const float* x, const float* y, const int64_t*
         while (chunk > 1 && rows / chunk < 4ull * (uint64_t)sm_count()) chunk /= 2;
         const uint32_t nchunks = (uint32_t)((rows + chunk - 1) / chunk);
         const unsigned g = grid_for((uint64_t)nchunks * 32, kThreads);
+        // an operand whose dim 1 has extent 1 keeps its row across a chunk that stays inside dim 1
+        const bool in_dim1 = (uint64_t)dims[1] % chunk == 0;
+        const int once = !in_dim1 ? 0 : xd[1] == 1 && dims[1] > 1 ? 1 : (yd[1] == 1 && dims[1] > 1 ? 2 : 0);
+#define MCU_ROWS_LAUNCH(S, O) binary_rows_chunked<OP, S, O><<<g, kThreads, 0, st>>>(r, x, y, p, (uint32_t)rows, nchunks, chunk)
+#define MCU_ROWS_STEPS(S)                                \
+    do {                                                 \
+        if (once == 1) MCU_ROWS_LAUNCH(S, 1);            \
+        else if (once == 2) MCU_ROWS_LAUNCH(S, 2);       \
+        else MCU_ROWS_LAUNCH(S, 0);                      \
+    } while (0)
         switch (p.steps) {
-            case 1: binary_rows_chunked<OP, 1><<<g, kThreads, 0, st>>>(r, x, y, p, (uint32_t)rows, nchunks, chunk); break;
-            case 2: binary_rows_chunked<OP, 2><<<g, kThreads, 0, st>>>(r, x, y, p, (uint32_t)rows, nchunks, chunk); break;
-            case 3: binary_rows_chunked<OP, 3><<<g, kThreads, 0, st>>>(r, x, y, p, (uint32_t)rows, nchunks, chunk); break;
-            default: binary_rows_chunked<OP, 4><<<g, kThreads, 0, st>>>(r, x, y, p, (uint32_t)rows, nchunks, chunk); break;
+            case 1: MCU_ROWS_STEPS(1); break;
+            case 2: MCU_ROWS_STEPS(2); break;
+            case 3: MCU_ROWS_STEPS(3); break;
+            default: MCU_ROWS_STEPS(4); break;
         }
+#undef MCU_ROWS_STEPS
+#undef MCU_ROWS_LAUNCH
         return cudaGetLastError();
     }
     unsigned grid = grid_for(p.nseg * 32, kThreads);
