@@ -191,6 +191,8 @@ __global__ void __launch_bounds__(kThreads) matmul_skinny_part(float* __restrict
                                                                const float* __restrict__ y, int M, int64_t K,
                                                                int64_t N, int64_t kc) {
     __shared__ float xs[MR][kSkinnyKc];
+    // the slice sum may be scheduled now; it waits for this grid's completion before reading
+    asm volatile("griddepcontrol.launch_dependents;");
     const int64_t c = (int64_t)blockIdx.x * kSkinnyCols + 4 * threadIdx.x;
     const int64_t k0 = (int64_t)blockIdx.y * kc;
     const int64_t k1 = (k0 + kc < K) ? k0 + kc : K;
@@ -268,6 +270,8 @@ __global__ void __launch_bounds__(kThreads) matmul_skinny_sum(float* __restrict_
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const int64_t i = (int64_t)blockIdx.x * 32 + lane;
     const int s0 = (int)((int64_t)nslices * w / 8), s1 = (int)((int64_t)nslices * (w + 1) / 8);
+    // launched as a programmatic dependent of the part kernel: wait until its partials are complete
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     float s = 0.0f;
     if (i < MN) {
 #pragma unroll 8
@@ -370,8 +374,20 @@ extern "C" int mcu_launch_matmul_skinny(float* r, const float* x, const float* y
         default: matmul_skinny_part<16><<<grid, kThreads, 0, st>>>(part, x, y, (int)M, K, N, kc); break;
     }
     const int64_t MN = M * N;
-    matmul_skinny_sum<<<(unsigned)((MN + 31) / 32), kThreads, 0, st>>>(r, part, MN, (int)slices, N, r_ld);
-    return (int)cudaGetLastError();
+    // programmatic dependent launch: the sum's CTAs are set up while the part kernel finishes
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = dim3((unsigned)((MN + 31) / 32));
+    cfg.blockDim = dim3(kThreads);
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return (int)e;
+    e = cudaLaunchKernelEx(&cfg, matmul_skinny_sum, r, (const float*)part, MN, (int)slices, N, r_ld);
+    return (int)e;
 }
 
 // ---------------------------------------------------------------------------

@@ -43,6 +43,8 @@
 #include "mcu_kernels.h"
 #include "mcu_math.cuh"
 
+#include <utility>
+
 namespace {
 
 constexpr int BM = 128;          // UMMA M (one CTA, TMEM lanes 0..127)
@@ -130,6 +132,15 @@ __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* ba
             "r"(smem_u32(dst)),
         "l"((uint64_t)map), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
         : "memory");
+}
+
+// Programmatic dependent launch: every kernel of a product's chain after the first is launched so
+// that it may be scheduled while its predecessor finishes; each kernel waits for the previous
+// grid's completion (and memory) before it touches memory, and lets its own dependents be
+// scheduled at once.  Both are no-ops for a kernel launched without the attribute.
+__device__ __forceinline__ void pdl_begin() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;");
 }
 
 // ---- CTA pairs (2-CTA clusters): the leader (rank 0) issues the MMAs for both CTAs
@@ -379,6 +390,7 @@ __global__ void __maxnreg__(kLaunchRegs)
                 const __grid_constant__ CUtensorMap map_bias, float* __restrict__ r, int M, int N, int Kp, int64_t ldr, int* status, const Epi epi,
                 int seg_kb, int first_kb, int batch, int kparts, int kpc, int split_from, float* __restrict__ part_out,
                 float* __restrict__ tail_out, int stall) {
+    pdl_begin();
     using C = Cfg<BN, STAGES, PAIR, RB>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -827,6 +839,7 @@ __device__ __forceinline__ float rna_tf32(float x) {
 // X[M][K] -> hi/lo [M][Kp]; one thread per 4 consecutive k.
 __global__ void __launch_bounds__(256) split_rows(const float* __restrict__ x, float* __restrict__ hi,
                                                   float* __restrict__ lo, int64_t M, int64_t K, int64_t Kp) {
+    pdl_begin();
     const int64_t q = Kp / 4;
     const int64_t n = M * q;
     const bool vec = (K % 4 == 0) && ((((uintptr_t)x) & 15) == 0);
@@ -853,6 +866,7 @@ __global__ void __launch_bounds__(256) split_rows(const float* __restrict__ x, f
 // Y[K][N] -> hi/lo transposed [N][Kp] through a 32x32 shared tile.
 __global__ void __launch_bounds__(256) split_cols_t(const float* __restrict__ y, float* __restrict__ hi,
                                                     float* __restrict__ lo, int64_t K, int64_t N, int64_t Kp) {
+    pdl_begin();
     __shared__ float tile[32][33];
     y += (int64_t)blockIdx.z * K * N;   // batch b: Y[b] is K x N, its split rows start at b*N
     hi += (int64_t)blockIdx.z * N * Kp;
@@ -902,6 +916,7 @@ __device__ __forceinline__ bool split_f16(float v, float scale, __half& hi, __ha
 __global__ void __launch_bounds__(256) split_rows_f16(const float* __restrict__ x, __half* __restrict__ hi,
                                                       __half* __restrict__ lo, int* __restrict__ row_exp, int64_t M,
                                                       int64_t K, int64_t Kp, int* __restrict__ row_floor) {
+    pdl_begin();
     const int64_t m = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (m >= M) return;
@@ -950,6 +965,7 @@ template <int V>
 __global__ void __launch_bounds__(256) split_rows_f16_warp(const float* __restrict__ x, __half* __restrict__ hi,
                                                            __half* __restrict__ lo, int* __restrict__ row_exp,
                                                            int64_t M, int64_t K, int64_t Kp, int* __restrict__ row_floor) {
+    pdl_begin();
     const int64_t m = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (m >= M) return;
@@ -1000,6 +1016,7 @@ template <int V>
 __global__ void __launch_bounds__(256) split_rows_f16_block(const float* __restrict__ x, __half* __restrict__ hi,
                                                             __half* __restrict__ lo, int* __restrict__ row_exp,
                                                             int64_t K, int64_t Kp, int* __restrict__ row_floor) {
+    pdl_begin();
     __shared__ float wmax[8];
     __shared__ int wfloor[8];
     const int64_t m = blockIdx.x;
@@ -1070,6 +1087,7 @@ __device__ __forceinline__ void check_output(const Epi& epi, float c, int64_t ro
 
 __global__ void __launch_bounds__(256) sum_parts(float* __restrict__ r, const float* __restrict__ part, int64_t M,
                                                  int64_t N, int parts, const Epi epi) {
+    pdl_begin();
     const int64_t n = M * N;
     if (!epi.out_hi && (n & 3) == 0 && ((((uintptr_t)r) & 15) == 0) && (!epi.bias || ((((uintptr_t)epi.bias) & 15) == 0))) {
         for (int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x; i < n / 4; i += (int64_t)gridDim.x * 256) {
@@ -1132,6 +1150,7 @@ template <int BN>
 __global__ void __launch_bounds__(256) sum_tail(float* __restrict__ r, const float* __restrict__ tail, int M, int N,
                                                 int TM, int num_m, int num_n, int split_from, int kparts,
                                                 const Epi chk) {
+    pdl_begin();
     const int per_tile = TM * BN / 4;
     const int64_t idx = (int64_t)blockIdx.x * 256 + threadIdx.x;
     const int j = (int)(idx / per_tile);
@@ -1180,6 +1199,7 @@ __global__ void __launch_bounds__(256) sum_tail(float* __restrict__ r, const flo
 constexpr int kColMaxRows = 128;
 __global__ void __launch_bounds__(256) col_absmax(const float* __restrict__ y, unsigned* __restrict__ cmax, int64_t K,
                                                   int64_t N) {
+    pdl_begin();
     __shared__ unsigned part[8][128];
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const int64_t n = (int64_t)blockIdx.x * 128 + lane * 4;
@@ -1229,6 +1249,7 @@ __global__ void __launch_bounds__(256) split_cols_t_f16(const float* __restrict_
                                                         __half* __restrict__ hi, __half* __restrict__ lo,
                                                         int* __restrict__ col_exp, int64_t K, int64_t N, int64_t Kp,
                                                         int* __restrict__ col_floor) {
+    pdl_begin();
     __shared__ float tile[64][65];
     __shared__ float scl[64];
     y += (int64_t)blockIdx.z * K * N;
@@ -1299,6 +1320,7 @@ __global__ void __launch_bounds__(256) split_cols_t_f16(const float* __restrict_
 __global__ void __launch_bounds__(256) fix_outputs(const float* __restrict__ x, const float* __restrict__ y,
                                                    float* __restrict__ r, int64_t M, int64_t K, int64_t N,
                                                    const Epi epi) {
+    pdl_begin();
     __shared__ double part[8];
     const int listed = epi.chk_count[0];
     const bool by_rows = listed > epi.chk_cap;
@@ -1563,6 +1585,24 @@ int test_stall() {
     return e && e[0] == '1';
 }
 
+// A kernel of a product's chain launched as a programmatic dependent of the previous kernel on the
+// stream (it waits in the kernel, pdl_begin, before touching memory).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_dep(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 template <bool FUSED, bool F16, bool PAIR, int RB = ROW_BYTES>
 int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c, const CUtensorMap& d,
                 const CUtensorMap& bias, float* r, int64_t M, int64_t N, int64_t kp, int* status, const Epi& epi,
@@ -1582,22 +1622,23 @@ int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c
     const int64_t tiles = split_from + (all - split_from) * kparts;  // work units
     if constexpr (!PAIR) {
         const int grid = (int)(tiles < sm_count() ? tiles : sm_count());
-        kern<<<grid, kThreads, smem, st>>>(a, b, c, d, bias, r, (int)M, (int)N, (int)kp, (int64_t)N, status, epi,
-                                           segment_kb(F16, KE), segment_first_kb(F16, KE), (int)B, kparts, kpc, split_from,
-                                           part_out, tail_out, test_stall());
-        return (int)cudaGetLastError();
+        return (int)launch_dep(kern, dim3(grid), dim3(kThreads), (size_t)smem, st, a, b, c, d, bias, r, (int)M, (int)N,
+                               (int)kp, (int64_t)N, status, epi, segment_kb(F16, KE), segment_first_kb(F16, KE), (int)B,
+                               kparts, kpc, split_from, part_out, tail_out, test_stall());
     } else {
         cudaLaunchConfig_t cfg = {};
-        cudaLaunchAttribute attr[1];
+        cudaLaunchAttribute attr[2];
         attr[0].id = cudaLaunchAttributeClusterDimension;
         attr[0].val.clusterDim.x = 2;
         attr[0].val.clusterDim.y = 1;
         attr[0].val.clusterDim.z = 1;
+        attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[1].val.programmaticStreamSerializationAllowed = 1;
         cfg.blockDim = dim3(kThreads);
         cfg.dynamicSmemBytes = (size_t)smem;
         cfg.stream = st;
         cfg.attrs = attr;
-        cfg.numAttrs = 1;
+        cfg.numAttrs = 1;  // the occupancy query below takes the cluster shape only
         cfg.gridDim = dim3((unsigned)sm_count());
         int max_clusters = 0;
         if (cudaOccupancyMaxActiveClusters(&max_clusters, kern, &cfg) != cudaSuccess || max_clusters <= 0) {
@@ -1606,6 +1647,7 @@ int launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& c
         }
         const int64_t clusters = tiles < max_clusters ? tiles : max_clusters;
         cfg.gridDim = dim3((unsigned)(2 * clusters));
+        cfg.numAttrs = 2;  // and a programmatic dependent of the split kernels
         e = cudaLaunchKernelEx(&cfg, kern, a, b, c, d, bias, r, (int)M, (int)N, (int)kp, (int64_t)N, status, epi,
                                segment_kb(F16, KE), segment_first_kb(F16, KE), (int)B, kparts, kpc, split_from, part_out,
                                tail_out, test_stall());
@@ -1697,12 +1739,16 @@ static int launch_tc(float* r, const float* x, const float* y, int64_t B, int64_
     }
     if (f16) {
         dim3 gm((unsigned)((N + 127) / 128), (unsigned)((K + kColMaxRows - 1) / kColMaxRows), (unsigned)B);
-        col_absmax<<<gm, 256, 0, st>>>(y, cmax, K, N);
+        cudaError_t e = launch_dep(col_absmax, gm, dim3(256), 0, st, y, cmax, K, N);
+        if (e != cudaSuccess) return (int)e;
         dim3 grid((unsigned)((N + 63) / 64), (unsigned)((l.kp + 63) / 64), (unsigned)B);
-        split_cols_t_f16<<<grid, 256, 0, st>>>(y, cmax, (__half*)yhi, (__half*)ylo, cexp, K, N, l.kp, cfloor);
+        e = launch_dep(split_cols_t_f16, grid, dim3(256), 0, st, y, (const unsigned*)cmax, (__half*)yhi, (__half*)ylo, cexp,
+                       K, N, l.kp, cfloor);
+        if (e != cudaSuccess) return (int)e;
     } else {
         dim3 grid((unsigned)((N + 31) / 32), (unsigned)(l.kp / 32), (unsigned)B);
-        split_cols_t<<<grid, 256, 0, st>>>(y, (float*)yhi, (float*)ylo, K, N, l.kp);
+        cudaError_t e = launch_dep(split_cols_t, grid, dim3(256), 0, st, y, (float*)yhi, (float*)ylo, K, N, l.kp);
+        if (e != cudaSuccess) return (int)e;
     }
     CUtensorMap mxh, mxl, myh, myl;
     const bool h = f16 != 0;
@@ -1740,8 +1786,7 @@ static int launch_tc(float* r, const float* x, const float* y, int64_t B, int64_
             fe.bias_zero = ep->bias_zero;
             fe.act = ep->act;
         }
-        fix_outputs<<<(unsigned)(4 * sm_count()), 256, 0, st>>>(x, y, r, M, K, N, fe);
-        return (int)cudaGetLastError();
+        return (int)launch_dep(fix_outputs, dim3((unsigned)(4 * sm_count())), dim3(256), 0, st, x, y, r, M, K, N, fe);
     };
     if (fused && kparts == 1) {
         if (!f16 && ep->out_hi && (N % 32 != 0 || ep->kp_out != round_up(N, KPAD))) return (int)cudaErrorInvalidValue;
@@ -1795,9 +1840,8 @@ static int launch_tc(float* r, const float* x, const float* y, int64_t B, int64_
         const int num_m = (int)((M + tm - 1) / tm), num_n = (int)((N + kBN - 1) / kBN);
         const int64_t ntail = B * num_m * num_n - split_from;
         const int64_t blocks = ntail * tm * kBN / 4 / 256;
-        sum_tail<kBN><<<(unsigned)blocks, 256, 0, st>>>(r, tail, (int)M, (int)N, tm, num_m, num_n, split_from, gparts,
-                                                         chk);
-        rc = (int)cudaGetLastError();
+        rc = (int)launch_dep(sum_tail<kBN>, dim3((unsigned)blocks), dim3(256), 0, st, r, (const float*)tail, (int)M,
+                             (int)N, tm, num_m, num_n, split_from, gparts, chk);
         return rc ? rc : fix();
     }
     if (kparts == 1) return fix();
@@ -1815,8 +1859,8 @@ static int launch_tc(float* r, const float* x, const float* y, int64_t B, int64_
     const int64_t n = M * N;
     int64_t g = (n + 255) / 256;
     if (g > 8 * sm_count()) g = 8 * sm_count();
-    sum_parts<<<(unsigned)(g ? g : 1), 256, 0, st>>>(r, part, M, N, kparts, fe);
-    rc = (int)cudaGetLastError();
+    rc = (int)launch_dep(sum_parts, dim3((unsigned)(g ? g : 1)), dim3(256), 0, st, r, (const float*)part, M, N, kparts,
+                         fe);
     return rc ? rc : fix();
 }
 
