@@ -263,10 +263,11 @@ def test_row_reductions(op):
 def test_softmax_rows():
     dev = device()
     o = oracle()
-    # 8193 and wider: two passes over slice statistics, in chunks of rows (300 x 32768 and
-    # 40 x 262144 take two chunks each)
+    # up to 2048 columns one warp per row, up to 65536 a cluster of 8192-element slices; wider
+    # rows two passes over slice statistics with a per-row combine between them (5000003 columns:
+    # 611 slices per row)
     for i, (rows, cols) in enumerate([(5, 10), (64, 1024), (9, 8192), (7, 8193), (3, 32768), (300, 32768),
-                                      (2, 262144), (40, 262144), (3, 1000003)]):
+                                      (2, 262144), (40, 262144), (3, 1000003), (2, 5000003)]):
         x = o.stream(8100 + i).uniform(rows * cols, -6, 6)
         tx, tr = dev.tensor((rows * cols,)), dev.tensor((rows * cols,))
         tx.write(x)

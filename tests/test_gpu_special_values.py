@@ -172,14 +172,18 @@ def test_exact_matmul_on_special_values():
 @pytest.mark.gpu
 def test_softmax_rows_with_masked_entries():
     """Rows with -inf entries (masked positions) give exact zeros there and a normal softmax over
-    the rest; a row that is all -inf gives NaN, as exp(x - max) / sum does in the oracle."""
+    the rest; a row that is all -inf gives NaN, as exp(x - max) / sum does in the oracle.  The
+    200003-wide rows take the two passes over 8192-element slice statistics, and row 3 there also
+    has a fully masked slice (its statistics are skipped in the row combine)."""
     dev, o = device(), oracle()
-    for cols in (10, 1024, 8193):
+    for cols in (10, 1024, 8193, 200003):
         rows = 4
         x = np.random.default_rng(cols).uniform(-5, 5, rows * cols).astype(np.float32)
         x[0:cols:3] = -np.inf               # row 0: every third entry masked
         x[cols:2 * cols] = -np.inf          # row 1: fully masked
         x[2 * cols + 1] = np.inf            # row 2: one +inf (max - max is NaN there)
+        if cols > 65536:
+            x[3 * cols + 8192:3 * cols + 16384] = -np.inf  # row 3: its second slice masked
         tx, tr = dev.tensor((rows * cols,)), dev.tensor((rows * cols,))
         tx.write(x)
         import mag_b200 as MB
