@@ -8,14 +8,17 @@
 // block over the block partials), so results are deterministic run to run.
 //
 // Row reductions and the normalised row softmax are extensions with the same
-// arithmetic per row.  The softmax keeps a whole row on chip (registers of one
-// warp, or of a thread-block cluster of up to 16 CTAs that combine the row max
-// and the double sum through distributed shared memory), so HBM sees one read
-// and one write per element (8 B/elem) and exp is evaluated once.
+// arithmetic per row.  The softmax keeps rows of up to 65536 on chip (registers
+// of one warp, or of a thread-block cluster of up to 8 CTAs that combine the row
+// max and the double sum through distributed shared memory), so HBM sees one
+// read and one write per element (8 B/elem) and exp is evaluated once; wider
+// rows are held in L2 between a statistics pass and the output pass (still
+// 8 B/elem of HBM while the resident CTAs' parts fit in L2).
 #include <cuda_runtime.h>
 #include <cooperative_groups.h>
 #include <cstdint>
 #include <cfloat>
+#include <cstdlib>
 #include "mcu_math.cuh"
 #include "mcu_kernels.h"
 
@@ -270,14 +273,14 @@ cudaError_t launch_rows_op(float* r, const float* x, int64_t rows, int64_t cols,
 
 // ----------------------------------------------------------- row softmax ---
 //
-// Rows stay in registers between the three phases (max, exp + double sum,
-// divide), so HBM sees one read and one write per element.  Short rows
-// (<= 2048) get one warp each; rows up to 65536 are split into slices of 8192
-// elements (one 256-thread CTA each) that form a thread-block cluster combining
-// the row max and sum through distributed shared memory; wider rows take two
-// passes over per-slice statistics (below).  Without scratch for the statistics,
-// rows up to 262144 use clusters of up to 16 slices of 16384 (512 threads), and
-// longer ones a three-pass kernel.
+// Short rows (<= 2048) get one warp each and rows up to 65536 a thread-block
+// cluster of 8192-element slices (one 256-thread CTA each) combining the row max
+// and sum through distributed shared memory; both keep the row in registers
+// between the phases (max, exp + double sum, scale), so HBM sees one read and
+// one write per element.  Wider rows go to softmax_rows_l2, which keeps each
+// CTA's part of the row in L2 between its statistics pass and its output pass;
+// two passes over per-slice statistics (scratch) remain for a cluster shape that
+// cannot be scheduled, and a three-pass kernel behind the register clusters.
 
 constexpr int kWarpRowMax = 2048;  // rows up to this length get one warp (16 float4 per lane at most)
 constexpr int kSliceVec = 8;      // float4 per thread: slices of 32 x threads elements
@@ -514,6 +517,100 @@ __global__ void __launch_bounds__(kStatThreads) softmax_slice_apply(float* __res
     }
 }
 
+// Rows wider than 65536: a cluster of up to 8 CTAs per row, CTA q owning the columns
+// [q * part, (q + 1) * part).  Pass 1 reads the part from HBM with the default caching (it stays
+// in L2) and keeps a running max m and double sum s of exp(x - m) per thread, rescaling s by
+// exp(m_old - m_new) in double when the max grows; the block and then the cluster combine
+// (max, then the rescaled double sums, the cluster's in rank order through distributed shared
+// memory).  Pass 2 re-reads the part, an L2 hit while the parts of the resident CTAs fit in L2,
+// and writes exp(x - M) * rn(1/S) as the two-kernel path does.  HBM sees 8 B per element against
+// that path's 12, with no scratch and no wait on other clusters.
+// 512 threads, parts of at least 32768 columns and clusters of at most 8 measured fastest at
+// 262144 columns (0.464 ms per 2^28; 256 threads 0.499, 1024 threads 0.875, parts of 16384 in
+// clusters of 16: 0.488 with 256 threads, 0.566 with 512).
+constexpr int kL2Threads = 512;
+constexpr int kL2Unroll = 4;          // float4 loads in flight per thread in pass 1
+constexpr int64_t kL2Part = 32768;    // columns per CTA at least
+constexpr int kL2MaxCluster = 8;      // portable cluster size
+
+__device__ __forceinline__ void online_add4(float4 v, float& m, double& s, uint32_t c, uint32_t cols,
+                                            uint32_t vec_end) {
+    const float mx = max4(v);
+    if (mx > m) {
+        if (m != -INFINITY) s *= exp((double)m - (double)mx);
+        m = mx;
+    }
+    if (m != -INFINITY) (void)exp4(v, m, c, cols, vec_end, s);
+}
+
+__global__ void __launch_bounds__(kL2Threads) softmax_rows_l2(float* __restrict__ r, const float* __restrict__ x,
+                                                              uint32_t cols, uint32_t part) {
+    __shared__ float sh_max[32];
+    __shared__ double sh_sum[32];
+    __shared__ float peer_m[kL2MaxCluster];
+    __shared__ double peer_s[kL2MaxCluster];
+    __shared__ float sh_gm, sh_inv;
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+    cg::cluster_group cluster = cg::this_cluster();
+    const uint32_t crank = cluster.block_rank();
+    const uint32_t csize = cluster.num_blocks();
+    const uint64_t row = blockIdx.x / csize;
+    const uint32_t cb = crank * part;
+    const uint32_t ce = cb + part < cols ? cb + part : cols;
+    const float* px = x + row * cols;
+    float* pr = r + row * cols;
+    const uint32_t vec_end = cols & ~3u;
+    const bool vec = (cols % 4 == 0) && ((((uintptr_t)px) | ((uintptr_t)pr)) & 15) == 0;
+    float m = -INFINITY;
+    double s = 0.0;
+    if (vec) {
+        constexpr uint32_t kStep = 4u * kL2Threads;
+        for (uint32_t c = cb + 4u * threadIdx.x; c < ce; c += kStep * kL2Unroll) {
+            float4 v[kL2Unroll];
+#pragma unroll
+            for (int u = 0; u < kL2Unroll; ++u)
+                v[u] = c + kStep * u < ce ? *(const float4*)(px + c + kStep * u) : neg_inf4();
+#pragma unroll
+            for (int u = 0; u < kL2Unroll; ++u) online_add4(v[u], m, s, c + kStep * u, cols, vec_end);
+        }
+    } else {
+        for (uint32_t c = cb + threadIdx.x; c < ce; c += kL2Threads) {
+            const float v = px[c];
+            if (v > m) {
+                if (m != -INFINITY) s *= exp((double)m - (double)v);
+                m = v;
+            }
+            if (m != -INFINITY) s += (double)expf(fs(v, m));
+        }
+    }
+    const float bm = block_combine(m, WMax(), sh_max, -(float)INFINITY);
+    s = block_combine(m != -INFINITY ? s * exp((double)m - (double)bm) : 0.0, WSum(), sh_sum, 0.0);
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+    if (threadIdx.x < csize) {
+        *cluster.map_shared_rank(&peer_m[crank], threadIdx.x) = bm;
+        *cluster.map_shared_rank(&peer_s[crank], threadIdx.x) = s;
+    }
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+    if (threadIdx.x == 0) {
+        float gm = -INFINITY;
+        for (uint32_t k = 0; k < csize; ++k) gm = fmaxf(gm, peer_m[k]);
+        double gs = 0.0;
+        for (uint32_t k = 0; k < csize; ++k)
+            if (peer_m[k] != -INFINITY) gs += peer_s[k] * exp((double)peer_m[k] - (double)gm);
+        sh_gm = gm;
+        sh_inv = __frcp_rn((float)gs);
+    }
+    __syncthreads();
+    const float gm = sh_gm, inv = sh_inv;
+    double unused = 0.0;
+    if (vec) {
+        for (uint32_t c = cb + 4u * threadIdx.x; c < ce; c += 4u * kL2Threads)
+            __stcs((float4*)(pr + c), div4(exp4(__ldcs((const float4*)(px + c)), gm, c, cols, vec_end, unused), inv));
+    } else {
+        for (uint32_t c = cb + threadIdx.x; c < ce; c += kL2Threads) pr[c] = __fmul_rn(expf(fs(px[c], gm)), inv);
+    }
+}
+
 // Rows longer than 16 slices: three passes from HBM.
 constexpr int kSoftmaxThreads = 512;
 __global__ void __launch_bounds__(kSoftmaxThreads) softmax_rows_global(float* __restrict__ r,
@@ -602,9 +699,21 @@ extern "C" int mcu_launch_reduce_rows(int op, float* r, const float* x, int64_t 
     }
 }
 
-// Rows wider than this go through the two-pass slice kernels (scratch: one SliceStat per slice):
-// measured faster than clusters of 16 slices (131072-wide rows: 0.51 vs 0.61 ms per 2^28).
+// Rows wider than this go to softmax_rows_l2 (131072-wide rows: 0.445 ms per 2^28 against 0.506
+// for the two-pass slice kernels and 0.61 for register-resident clusters of 16 slices); the
+// two-pass slice kernels (scratch: one SliceStat per slice) remain for a cluster shape that cannot
+// be scheduled.
 constexpr int64_t kClusterRowMax = 8 * 8192;
+
+// MAG_CUDA_SOFTMAX_L2=0 sends rows wider than 65536 to the two-kernel path.
+static bool l2_rows_on() {
+    static int on = -1;
+    if (on < 0) {
+        const char* e = getenv("MAG_CUDA_SOFTMAX_L2");
+        on = !(e && e[0] == '0');
+    }
+    return on != 0;
+}
 
 extern "C" size_t mcu_softmax_rows_scratch_bytes(int64_t rows, int64_t cols) {
     if (cols <= kClusterRowMax) return 0;
@@ -613,13 +722,37 @@ extern "C" size_t mcu_softmax_rows_scratch_bytes(int64_t rows, int64_t cols) {
 
 extern "C" int mcu_softmax_rows_kernels(int64_t rows, int64_t cols) {
     if (rows <= 0 || cols <= 0) return 0;
-    return cols <= kClusterRowMax ? 1 : 3;
+    return cols <= kClusterRowMax || l2_rows_on() ? 1 : 3;
 }
 
 extern "C" int mcu_launch_softmax_rows(float* r, const float* x, int64_t rows, int64_t cols, void* scratch,
                                        cudaStream_t st) {
     if (rows <= 0 || cols <= 0) return (int)cudaSuccess;
     if (cols >= (1ll << 31) || rows >= (1ll << 31)) return (int)cudaErrorInvalidValue;
+    if (cols > kClusterRowMax && l2_rows_on()) {
+        // clusters of up to kL2MaxCluster CTAs, parts of at least kL2Part columns (a multiple of 4)
+        int64_t cl = (cols + kL2Part - 1) / kL2Part;
+        if (cl > kL2MaxCluster) cl = kL2MaxCluster;
+        const int64_t part = ((cols + cl - 1) / cl + 3) & ~(int64_t)3;
+        cl = (cols + part - 1) / part;
+        if (rows * cl < (1ll << 31)) {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3((unsigned)(rows * cl));
+            cfg.blockDim = dim3(kL2Threads);
+            cfg.dynamicSmemBytes = 0;
+            cfg.stream = st;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = (unsigned)cl;
+            attr[0].val.clusterDim.y = 1;
+            attr[0].val.clusterDim.z = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            cudaError_t e = cudaLaunchKernelEx(&cfg, softmax_rows_l2, r, x, (uint32_t)cols, (uint32_t)part);
+            if (e == cudaSuccess) return (int)cudaSuccess;
+            cudaGetLastError();  // cluster shape not schedulable here: the two-kernel path below
+        }
+    }
     if (cols > kClusterRowMax) {
         const int64_t ns = (cols + kStatSlice - 1) / kStatSlice;
         if (!scratch || rows * ns >= (1ll << 31)) return (int)cudaErrorInvalidValue;

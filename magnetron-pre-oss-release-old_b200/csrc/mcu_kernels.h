@@ -39,8 +39,8 @@ int mcu_launch_reduce_partial(McuReducePart* part, const float* x, const int64_t
 int mcu_launch_reduce_combine(int op, float* r, const McuReducePart* parts, int nparts, cudaStream_t st);
 int mcu_launch_reduce_rows(int op, float* r, const float* x, int64_t rows, int64_t cols, cudaStream_t st);
 /* Normalised row softmax; scratch needs mcu_softmax_rows_scratch_bytes(rows, cols) bytes
- * (nonzero only for rows wider than 65536, which take two passes over slice statistics and a
- * per-row combine). */
+ * (nonzero only for rows wider than 65536, whose fallback, when their cluster shape cannot be
+ * scheduled, takes two passes over slice statistics and a per-row combine). */
 size_t mcu_softmax_rows_scratch_bytes(int64_t rows, int64_t cols);
 int mcu_softmax_rows_kernels(int64_t rows, int64_t cols); /* kernel launches of one call */
 int mcu_launch_softmax_rows(float* r, const float* x, int64_t rows, int64_t cols, void* scratch, cudaStream_t st);

@@ -263,9 +263,9 @@ def test_row_reductions(op):
 def test_softmax_rows():
     dev = device()
     o = oracle()
-    # up to 2048 columns one warp per row, up to 65536 a cluster of 8192-element slices; wider
-    # rows two passes over slice statistics with a per-row combine between them (5000003 columns:
-    # 611 slices per row)
+    # up to 2048 columns one warp per row, up to 65536 a register-resident cluster of 8192-element
+    # slices; wider rows an L2-resident cluster of up to 8 parts (5000003 columns: parts of 625001,
+    # larger than L2 holds for all resident CTAs)
     for i, (rows, cols) in enumerate([(5, 10), (64, 1024), (9, 8192), (7, 8193), (3, 32768), (300, 32768),
                                       (2, 262144), (40, 262144), (3, 1000003), (2, 5000003)]):
         x = o.stream(8100 + i).uniform(rows * cols, -6, 6)
@@ -280,6 +280,49 @@ def test_softmax_rows():
         # slice rescaling exp(m_slice - m_row) (one more expf and rounding), measure <= 1.2e-6
         assert rel.max() <= 2e-6, (rows, cols, rel.max())
 
+
+
+_TWO_PASS = r"""
+import sys, numpy as np
+import mag_b200 as MB
+from harness import oracle
+o, dev = oracle(), MB.Device()
+worst = 0.0
+for i, (rows, cols) in enumerate([(2, 262144), (40, 131075), (3, 1000003), (2, 5000003)]):
+    x = o.stream(8200 + i).uniform(rows * cols, -6, 6)
+    if i == 1:
+        x[3 * cols + 8192:3 * cols + 16384] = -np.inf  # one masked slice
+        x[5 * cols:6 * cols] = -np.inf                 # one masked row: NaN
+    tx, tr = dev.tensor((rows * cols,)), dev.tensor((rows * cols,))
+    tx.write(x)
+    MB.check(dev.L.mag_cuda_softmax_rows_f32(dev.p, tr.data_ptr, tx.data_ptr, rows, cols), "softmax")
+    got, want = tr.read(), o.softmax_rows(x, rows, cols)
+    assert np.array_equal(np.isnan(got), np.isnan(want)), (rows, cols)
+    fin = ~np.isnan(want)
+    assert np.all(got[fin][want[fin] == 0] == 0), (rows, cols)
+    nz = fin & (want != 0)
+    worst = max(worst, float((np.abs(got[nz] - want[nz]) / np.abs(want[nz])).max()))
+    tx.free(); tr.free()
+assert worst <= 2e-6, worst
+print("ok", worst)
+"""
+
+
+def test_softmax_rows_two_pass_fallback():
+    """The two passes over 8192-element slice statistics, which rows wider than 65536 take when
+    their cluster shape cannot be scheduled, forced with MAG_CUDA_SOFTMAX_L2=0 in a process of
+    their own (the switch is read once per process): within 2e-6 of the oracle, masked slices
+    exact zeros, a masked row NaN."""
+    import os
+    import subprocess
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    root = os.path.dirname(here)
+    paths = [here, os.path.join(here, "golden"), os.path.join(root, "oracle"),
+             os.path.join(root, "magnetron-pre-oss-release-old_b200"), root]
+    env = dict(os.environ, MAG_CUDA_SOFTMAX_L2="0", PYTHONPATH=os.pathsep.join(paths))
+    res = subprocess.run([sys.executable, "-c", _TWO_PASS], env=env, capture_output=True, text=True, timeout=600)
+    assert res.returncode == 0 and res.stdout.startswith("ok"), res.stdout + res.stderr
 
 def test_broadcast2_small_exact():
     dev = device()

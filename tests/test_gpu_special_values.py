@@ -173,8 +173,8 @@ def test_exact_matmul_on_special_values():
 def test_softmax_rows_with_masked_entries():
     """Rows with -inf entries (masked positions) give exact zeros there and a normal softmax over
     the rest; a row that is all -inf gives NaN, as exp(x - max) / sum does in the oracle.  The
-    200003-wide rows take the two passes over 8192-element slice statistics, and row 3 there also
-    has a fully masked slice (its statistics are skipped in the row combine)."""
+    200003-wide rows take the L2-resident cluster (7 parts of 28572 columns), and row 3 there also
+    has its second part fully masked (that CTA's statistics are skipped in the cluster combine)."""
     dev, o = device(), oracle()
     for cols in (10, 1024, 8193, 200003):
         rows = 4
@@ -183,7 +183,7 @@ def test_softmax_rows_with_masked_entries():
         x[cols:2 * cols] = -np.inf          # row 1: fully masked
         x[2 * cols + 1] = np.inf            # row 2: one +inf (max - max is NaN there)
         if cols > 65536:
-            x[3 * cols + 8192:3 * cols + 16384] = -np.inf  # row 3: its second slice masked
+            x[3 * cols + 28572:3 * cols + 57144] = -np.inf  # row 3: its second part masked
         tx, tr = dev.tensor((rows * cols,)), dev.tensor((rows * cols,))
         tx.write(x)
         import mag_b200 as MB
