@@ -254,8 +254,9 @@ MAG_CUDA_EXPORT int mag_cuda_img_draw_text(mag_compute_device_t* dvc, mag_tensor
 /* ---- allocation-free entry point (no counterpart in the reference) ----
  * R[M,N] = X[M,K] Y[K,N] for 1 <= M <= 16, the same split-K kernels as
  * mag_cuda_matmul_f32 uses for such shapes, but it never allocates: for callers
- * that cannot call cudaMalloc when they need the product, such as code running
- * inside a stream capture or a host path that must stay off the allocator.  Its
+ * that cannot call cudaMalloc when they need the product, such as a
+ * latency-critical host path that must not enter the CUDA allocator (which can
+ * block or synchronise) or code under a memory budget fixed up front.  Its
  * partial sums go to one fixed 16 MiB array in this library's device image,
  * which every GPU that loads the library keeps until the process exits.  Calls
  * needing more (slices x M x N x 4 bytes) return MAG_CUDA_E_SCRATCH_LIMIT.  On a

@@ -394,10 +394,9 @@ extern "C" int mcu_launch_matmul_skinny(float* r, const float* x, const float* y
 // Allocation-free variant of the skinny product.
 //
 // Some callers cannot allocate device memory at the moment they need a
-// product: code running while a CUDA stream is being captured into a graph
-// (an allocation there either fails or becomes part of the graph), hosts that
-// must not touch the allocator on a latency-critical or real-time path, and
-// hosts whose device memory is carved up by a framework that owns every
+// product: hosts that must not touch the allocator (which can block or
+// synchronise the device) on a latency-critical or real-time path, and hosts
+// whose device memory is carved up by a framework that owns every
 // allocation.  For them the split-K partial sums live in one fixed array that
 // is part of this library's device image: it is created when the library's
 // device code is loaded on a GPU and stays there until the process exits.

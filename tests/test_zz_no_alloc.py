@@ -1,9 +1,10 @@
 """The allocation-free skinny matmul entry point.
 
 mag_cuda_matmul_skinny_f32_noalloc exists for callers that cannot allocate
-device memory when they need the product (for example, code running while a
-stream is being captured into a CUDA graph, or a latency-critical host path
-that must stay off the allocator): its split-K partial sums live in a fixed
+device memory when they need the product (for example, a latency-critical
+host path that must not enter the CUDA allocator, which can block or
+synchronise, or code that runs under a memory budget fixed up front): its
+split-K partial sums live in a fixed
 array inside the library's device image instead of a buffer from cudaMalloc.
 
 This file sorts last so that a run stopping at the first failure has already
